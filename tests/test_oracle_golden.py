@@ -1,0 +1,190 @@
+"""Pin the CPU oracle to golden vectors produced by the reference itself.
+
+The fixtures come from ``tests/golden/make_golden.py``, which imports the
+reference unchanged. These tests run on CPU only.
+"""
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import sampler as osampler
+from oracle.attention import paged_attention, write_pool
+from oracle.metadata import pack_tick, pack_uniform
+from oracle.model import OracleConfig, OracleModel, OracleRequests, build_state_dict, new_pools
+from tests.golden.inputs import attention_inputs, digest
+
+
+def _metadata_cases(golden_dir):
+    return json.loads((golden_dir / "metadata.json").read_text())
+
+
+def test_metadata_known_answers(golden_dir):
+    cases = _metadata_cases(golden_dir)
+    assert {c["name"] for c in cases} >= {"ref_mixed_lengths", "ref_prefill_two", "page_boundary",
+                                          "config1_tick", "config3_tick", "drafted_rows",
+                                          "chunked_prefill", "restored_prefix"}
+    for case in cases:
+        if case["mode"] == "uniform":
+            got = pack_uniform(case["lengths"], case["tokens"], case["page_tables"], case["capacities"])
+        else:
+            got = pack_tick(case["lengths"], case["counts"], case["page_tables"], case["capacities"],
+                            logit_counts=case["logit_counts"])
+        for key, value in case["expected"].items():
+            if key == "positions":  # the reference returns positions as [1, T]
+                value = value[0]
+            assert got[key] == value, (case["name"], key)
+    # The reference test's literal answers (tests/test_paged_attention.py:111-113, :262-263).
+    by_name = {c["name"]: c for c in cases}
+    assert by_name["ref_mixed_lengths"]["expected"]["seqused_k"] == [4, 8]
+    assert by_name["ref_mixed_lengths"]["expected"]["cu_seq_q"] == [0, 1, 2]
+    assert by_name["ref_mixed_lengths"]["expected"]["cu_seq_k"] == [0, 4, 12]
+    assert by_name["ref_prefill_two"]["expected"]["cu_seq_q"] == [0, 2, 4]
+    assert by_name["ref_prefill_two"]["expected"]["cu_seq_k"] == [0, 2, 4]
+
+
+def test_page_allocation_is_lifo(golden_dir):
+    """The reference pool hands out pages 0, 1, 2, ... from a reversed free list."""
+    case = {c["name"]: c for c in _metadata_cases(golden_dir)}["config1_tick"]
+    requests = OracleRequests(16)
+    rows = []
+    for length, cap in zip(case["lengths"], case["capacities"]):
+        row = requests.add(cap)
+        if length:
+            requests.tick([row], [length])
+            requests.advance([row], [length])
+        rows.append(row)
+    requests.tick(rows, case["counts"])
+    assert [requests.tables[r] for r in rows] == case["page_tables"]
+
+
+CONFIG1 = OracleConfig(vocab_size=4096, context_length=4096, hidden_size=256, n_heads=4, n_layers=2,
+                       hidden_dim=768, head_dim=64, n_kv_heads=2, dtype=torch.float32)
+BF16 = OracleConfig(vocab_size=4096, context_length=4096, hidden_size=512, n_heads=8, n_layers=2,
+                    hidden_dim=1024, head_dim=128, n_kv_heads=2, dtype=torch.bfloat16)
+
+
+def _run_tick_and_greedy(config, sd, prompts, chunks, capacities, logit_counts, steps, pages):
+    model = OracleModel(config, sd)
+    kp, vp = new_pools(config, pages)
+    req = OracleRequests(pages)
+    rows = [req.add(cap) for cap in capacities]
+    with torch.inference_mode():
+        for row, prompt in zip(rows, prompts):
+            meta = req.tick([row], [len(prompt)])
+            model.forward_packed(prompt, kp, vp, meta)
+            req.advance([row], [len(prompt)])
+        counts = [len(c) for c in chunks]
+        meta = req.tick(rows, counts, logit_counts)
+        logits = model.forward_packed([t for c in chunks for t in c], kp, vp, meta)
+        req.advance(rows, counts)
+        last = np.cumsum(logit_counts) - 1
+        tokens = [logits[torch.as_tensor(last)].float().argmax(-1).tolist()]
+        for _ in range(steps - 1):
+            meta = req.tick(rows, [1] * len(rows))
+            out = model.forward_packed(tokens[-1], kp, vp, meta)
+            req.advance(rows, [1] * len(rows))
+            tokens.append(out.float().argmax(-1).tolist())
+    return logits, np.array(tokens).T, req, rows
+
+
+def test_config1_logits_and_greedy_match_reference_dense_path(golden_dir):
+    """tiny fp32 Qwen3, seed 0; reference dense-KV logits + 16 greedy steps."""
+    g = np.load(golden_dir / "config1.npz")
+    assert bool(g["weights_match"])
+    sd = build_state_dict(CONFIG1, 0)
+    assert float(sd["token_embedding.weight"].double().sum()) == float(g["embedding_sum"])
+    lengths = g["prompt_lengths"].tolist()
+    flat = g["prompts"].tolist()
+    prompts, at = [], 0
+    for n in lengths:
+        prompts.append(flat[at:at + n]); at += n
+    chunks = [[t] for t in g["pending"].tolist()] + [g["chunk"].tolist()]
+    caps = [n + 17 for n in lengths] + [216]
+    logits, greedy, _, _ = _run_tick_and_greedy(CONFIG1, sd, prompts, chunks, caps, [1] * 5, 16, 16)
+    expected = torch.from_numpy(g["dense_logits"])
+    torch.testing.assert_close(logits, expected, atol=1e-4, rtol=1e-4)
+    assert float(g["packed_vs_dense_max_abs"]) < 1e-4
+    assert (greedy == g["greedy"]).all()
+
+
+def test_bf16_mixed_tick_matches_reference_packed_path(golden_dir):
+    """bf16 mixed tick at the Qwen3-4B head shape; logits within 2e-2, greedy ids identical."""
+    g = np.load(golden_dir / "bf16_tick.npz")
+    sd = build_state_dict(BF16, 0)
+    flat = g["prompts"].tolist()
+    prompts, at = [], 0
+    for n in g["prompt_lengths"].tolist():
+        prompts.append(flat[at:at + n]); at += n
+    flat = g["chunks"].tolist()
+    chunks, at = [], 0
+    for n in g["chunk_lengths"].tolist():
+        chunks.append(flat[at:at + n]); at += n
+    caps = [n + 320 + 16 for n in g["prompt_lengths"].tolist()] + [316]
+    logits, greedy, req, rows = _run_tick_and_greedy(BF16, sd, prompts, chunks, caps,
+                                                     g["logit_counts"].tolist(), 16, 24)
+    ref = torch.from_numpy(g["logits"])
+    # bf16 logits of a random-init model reach |logit| ~ 500, where one bf16 ulp is 2-4;
+    # the 2e-2 bound is therefore taken relative to each row's logit scale.
+    diff = (logits.float() - ref).abs().max(-1).values
+    scale = ref.abs().max(-1).values
+    assert (diff <= 2e-2 * scale).all(), (diff, scale)
+    assert (greedy == g["greedy"]).all()
+    tables = [p for r in rows for p in req.tables[r]]
+    assert tables == g["page_tables"].tolist()
+
+
+def test_attention_matches_reference_packed_attend(golden_dir):
+    g = np.load(golden_dir / "attention.npz")
+    lengths, counts = g["lengths"].tolist(), g["counts"].tolist()
+    key_pool, value_pool, q, k, v = attention_inputs(int(g["num_pages"]), sum(counts))
+    assert digest(key_pool, value_pool, q, k, v) == str(g["input_sha256"])
+    slots = g["write_slots"].tolist()
+    write_pool(key_pool, slots, k[0].transpose(0, 1))
+    write_pool(value_pool, slots, v[0].transpose(0, 1))
+    out = paged_attention(q[0].transpose(0, 1).contiguous(), key_pool, value_pool,
+                          g["block_table"].tolist(), g["cu_seq_q"].tolist(), g["seqused_k"].tolist())
+    expected = torch.from_numpy(g["out"]).view(torch.bfloat16)[0].transpose(0, 1)
+    diff = (out.float() - expected.float()).abs()
+    assert diff.max().item() <= 1.6e-2, diff.max().item()
+    assert diff.mean().item() < 1e-3
+
+
+def test_sampler_rules_match_reference(golden_dir):
+    g = np.load(golden_dir / "sampler.npz")
+    logits = torch.from_numpy(g["logits"]).view(torch.bfloat16).float()
+    assert osampler.greedy(logits).tolist() == g["greedy"].tolist()
+    assert osampler.greedy(logits)[3].item() == 17  # first index among tied maxima
+    vocab = logits.shape[-1]
+    for temperature, top_p, packed in zip(g["temperature"], g["top_p"], g["kept"]):
+        ref = torch.from_numpy(np.unpackbits(packed, axis=-1)[:, :vocab].astype(bool))
+        mine = osampler.keep_mask(logits, float(temperature), float(top_p))
+        probs = osampler.probabilities(logits, float(temperature))
+        # The reference drops tokens whose probability underflows to 0; so do we for comparison.
+        mine = mine & (probs > 0)
+        for row in range(logits.shape[0]):
+            if torch.equal(ref[row], mine[row]):
+                continue
+            # bf16 logits tie often; the reference's sort is not stable, so which of
+            # several equal-probability tokens sits at the cut may differ. The kept
+            # probabilities, as a multiset, must not.
+            assert ref[row].sum() == mine[row].sum(), (temperature, top_p, row)
+            a = torch.sort(logits[row][ref[row]]).values
+            b = torch.sort(logits[row][mine[row]]).values
+            assert torch.equal(a, b), (temperature, top_p, row)
+
+
+def test_sampler_deterministic_draw_is_inverse_cdf():
+    logits = torch.tensor([[0.0, 1.0, 2.0, 3.0]])
+    probs = torch.softmax(logits, -1)[0].double()
+    cdf = torch.cumsum(probs, 0)
+    for u in (0.0, 0.05, 0.3, 0.9, 0.999):
+        tok = osampler.sample(logits, 1.0, 1.0, torch.tensor([u])).item()
+        assert tok == int(torch.nonzero(cdf > u * cdf[-1])[0])
+    # top_p keeps the largest tokens until the preceding mass exceeds p.
+    # softmax([0,1,2,3]) = [.032, .087, .237, .644]: at p=0.5 only the top token is
+    # kept (nothing precedes it); at p=0.7 the second survives (0.644 precedes it).
+    assert osampler.keep_mask(logits, 1.0, 0.5)[0].tolist() == [False, False, False, True]
+    assert osampler.keep_mask(logits, 1.0, 0.7)[0].tolist() == [False, False, True, True]
