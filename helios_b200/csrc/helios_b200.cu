@@ -1,0 +1,374 @@
+// C-ABI of libhelios_b200.so: the packed-tick hot path for sm_100a.
+//
+// Every entry point takes raw device pointers, sizes and a cudaStream_t, borrows
+// the memory for the duration of the launch and allocates nothing. Each returns
+// 0 on success or a negative code (HB_ERR_*) with a message in hb_last_error().
+// Declarations and the reference interface each one replaces: include/helios_b200.h.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/helios_b200.h"
+#include "attention_decode.cuh"
+#include "attention_prefill.cuh"
+#include "hb_common.cuh"
+#include "model_ops.cuh"
+#include "norm_rope_append.cuh"
+#include "sampler.cuh"
+#include "tick_pack.cuh"
+
+namespace {
+
+thread_local char g_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(HB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return HB_OK;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// ---- cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 3-D bf16 tensor map: dims (inner, mid, outer) with byte strides for mid and outer,
+// 128-byte swizzle, box (box0, box1, box2). Out-of-range boxes are zero-filled.
+int encode_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2,
+              uint32_t b0, uint32_t b1, uint32_t b2) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(HB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {s1, s2};
+  const cuuint32_t box[3] = {b0, b1, b2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return HB_OK;
+}
+
+// Per-device one-time opt-in to large dynamic shared memory.
+template <typename K>
+int ensure_smem(K kernel, int bytes, bool (&done)[64]) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(HB_ERR_CUDA, "cudaGetDevice failed");
+  if (!done[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return fail(HB_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    done[dev] = true;
+  }
+  return HB_OK;
+}
+
+bool g_dec_smem[4][64], g_pre_smem[4][64], g_tick_smem[64];
+
+int group_slot(int group) { return group == 1 ? 0 : group == 2 ? 1 : group == 4 ? 2 : 3; }
+
+}  // namespace
+
+extern "C" {
+
+int hb_version(void) { return HB_VERSION; }
+
+const char* hb_last_error(void) { return g_error; }
+
+int hb_device_status(uint32_t* status, int clear) {
+  if (status == nullptr) return fail(HB_ERR_INVALID, "status is null");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(HB_ERR_CUDA, "synchronize: %s", cudaGetErrorString(e));
+  e = cudaMemcpyFromSymbol(status, hb::g_status, sizeof(uint32_t));
+  if (e != cudaSuccess) return fail(HB_ERR_CUDA, "read status: %s", cudaGetErrorString(e));
+  if (clear) {
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(hb::g_status, &zero, sizeof(uint32_t));
+    if (e != cudaSuccess) return fail(HB_ERR_CUDA, "clear status: %s", cudaGetErrorString(e));
+  }
+  return HB_OK;
+}
+
+int hb_tick_pack(const int32_t* rows, int32_t num_rows, const int32_t* updates, int32_t num_updates, int32_t* arena,
+                 int32_t arena_slots, int32_t arena_width, int32_t page_size, int32_t width, int32_t num_pages,
+                 int32_t decode_max_tokens, int32_t split_keys, int32_t prefill_tile_tokens, int32_t total_tokens,
+                 int32_t* block_table, int32_t* cu_seq_q, int32_t* cu_seq_k, int32_t* seqused_k, int64_t* positions,
+                 int64_t* write_slots, int32_t* token_row, int64_t* logit_indices, int32_t logit_capacity,
+                 int32_t* decode_items, int32_t decode_capacity, int32_t* prefill_items, int32_t prefill_capacity,
+                 cudaStream_t stream) {
+  if (num_rows < 1 || num_rows > HB_MAX_TICK_ROWS)
+    return fail(HB_ERR_INVALID, "num_rows %d outside [1, %d]", num_rows, HB_MAX_TICK_ROWS);
+  if (rows == nullptr || arena == nullptr || block_table == nullptr || cu_seq_q == nullptr || cu_seq_k == nullptr ||
+      seqused_k == nullptr)
+    return fail(HB_ERR_INVALID, "null metadata pointer");
+  if (num_updates < 0 || (num_updates > 0 && updates == nullptr)) return fail(HB_ERR_INVALID, "bad page updates");
+  if (page_size < 1 || width < 1 || arena_width < 1 || arena_slots < 1 || num_pages < 1 || split_keys < page_size ||
+      split_keys % page_size != 0 || prefill_tile_tokens < 1 || total_tokens < 0)
+    return fail(HB_ERR_INVALID, "bad tick sizes");
+  if (total_tokens > 0 && (positions == nullptr || write_slots == nullptr || token_row == nullptr))
+    return fail(HB_ERR_INVALID, "null per-token output");
+  if ((logit_capacity > 0 && logit_indices == nullptr) || (decode_capacity > 0 && decode_items == nullptr) ||
+      (prefill_capacity > 0 && prefill_items == nullptr) || logit_capacity < 0 || decode_capacity < 0 ||
+      prefill_capacity < 0)
+    return fail(HB_ERR_INVALID, "bad output capacities");
+  hb::TickPackParams p{rows, updates, arena, num_rows, num_updates, arena_width, arena_slots, page_size, width,
+                       num_pages, decode_max_tokens, split_keys, prefill_tile_tokens, block_table, cu_seq_q, cu_seq_k,
+                       seqused_k, positions, write_slots, token_row, logit_indices, decode_items, prefill_items,
+                       total_tokens, logit_capacity, decode_capacity, prefill_capacity};
+  const int smem = 6 * (num_rows + 1) * static_cast<int>(sizeof(int32_t));
+  if (int rc = ensure_smem(hb::tick_pack_kernel, 6 * (HB_MAX_TICK_ROWS + 1) * 4, g_tick_smem)) return rc;
+  hb::tick_pack_kernel<<<1, hb::kTickThreads, smem, stream>>>(p);
+  return check_launch("tick_pack_kernel");
+}
+
+int hb_qk_norm_rope_append(const void* q, int64_t q_token_stride, int64_t q_head_stride, const void* k,
+                           int64_t k_token_stride, int64_t k_head_stride, const void* v, int64_t v_token_stride,
+                           int64_t v_head_stride, const float* q_scale, const float* k_scale, float eps,
+                           const float* cos, const float* sin, int64_t rope_rows, const int64_t* positions,
+                           const int64_t* write_slots, void* q_out, void* key_pool, void* value_pool,
+                           int64_t pool_slots, int32_t tokens, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                           cudaStream_t stream) {
+  if (tokens < 0 || heads < 1 || kv_heads < 1 || heads % kv_heads) return fail(HB_ERR_INVALID, "bad head counts");
+  if (head_dim != 64 && head_dim != 128) return fail(HB_ERR_UNSUPPORTED, "head_dim %d (supported: 64, 128)", head_dim);
+  if (tokens == 0) return HB_OK;
+  if (k == nullptr || v == nullptr || key_pool == nullptr || value_pool == nullptr || write_slots == nullptr)
+    return fail(HB_ERR_INVALID, "null key/value pointer");
+  if (q_out != nullptr && q == nullptr) return fail(HB_ERR_INVALID, "q_out without q");
+  if ((cos == nullptr) != (sin == nullptr) || (cos != nullptr && positions == nullptr))
+    return fail(HB_ERR_INVALID, "rope tables need cos, sin and positions");
+  const uintptr_t vec = head_dim == 128 ? 8 : 4;
+  if (!aligned(k, vec) || !aligned(v, vec) || (q && !aligned(q, vec)) || (q_out && !aligned(q_out, vec)))
+    return fail(HB_ERR_INVALID, "q/k/v rows must be %d-byte aligned", static_cast<int>(vec));
+  hb::NormRopeParams p{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+                       static_cast<const __nv_bfloat16*>(v), q_token_stride, q_head_stride, k_token_stride,
+                       k_head_stride, v_token_stride, v_head_stride, q_scale, k_scale, eps, cos, sin, rope_rows,
+                       positions, write_slots, static_cast<__nv_bfloat16*>(q_out),
+                       static_cast<__nv_bfloat16*>(key_pool), static_cast<__nv_bfloat16*>(value_pool), pool_slots,
+                       tokens, heads, kv_heads};
+  const int64_t items = static_cast<int64_t>(tokens) * (heads + 2 * kv_heads);
+  const unsigned blocks = static_cast<unsigned>((items + 7) / 8);
+  if (head_dim == 128)
+    hb::norm_rope_append_kernel<128><<<blocks, 256, 0, stream>>>(p);
+  else
+    hb::norm_rope_append_kernel<64><<<blocks, 256, 0, stream>>>(p);
+  return check_launch("norm_rope_append_kernel");
+}
+
+size_t hb_attention_workspace_bytes(int32_t partial_records, int32_t heads, int32_t head_dim) {
+  if (partial_records <= 0 || heads <= 0 || head_dim <= 0) return 0;
+  return static_cast<size_t>(partial_records) * heads * (head_dim + 1) * sizeof(float);
+}
+
+int hb_paged_attention(const void* q, const void* key_pool, const void* value_pool, int64_t num_pages,
+                       int32_t page_size, const int32_t* block_table, int32_t width, const int32_t* cu_seq_q,
+                       const int32_t* seqused_k, const int32_t* decode_items, int32_t num_decode_items,
+                       const int32_t* prefill_items, int32_t num_prefill_items, int32_t partial_records,
+                       int32_t split_keys, int32_t total_tokens, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                       float scale, void* workspace, size_t workspace_bytes, void* out, cudaStream_t stream) {
+  if (head_dim != 128) return fail(HB_ERR_UNSUPPORTED, "paged attention supports head_dim 128, got %d", head_dim);
+  if (heads < 1 || kv_heads < 1 || heads % kv_heads) return fail(HB_ERR_INVALID, "bad head counts");
+  const int group = heads / kv_heads;
+  if (group != 1 && group != 2 && group != 4 && group != 8)
+    return fail(HB_ERR_UNSUPPORTED, "query heads per KV head must be 1, 2, 4 or 8 (got %d)", group);
+  if (page_size % hb::kDecTileKeys != 0 || split_keys % page_size != 0 || split_keys < page_size)
+    return fail(HB_ERR_INVALID, "page_size must be a multiple of 64 and split_keys of page_size");
+  if (num_decode_items < 0 || num_prefill_items < 0 || total_tokens < 0 || num_pages < 1 || width < 1 ||
+      partial_records < 0)
+    return fail(HB_ERR_INVALID, "bad work sizes");
+  if (num_pages * page_size > (int64_t(1) << 31)) return fail(HB_ERR_UNSUPPORTED, "pool exceeds 2^31 tokens");
+  if (q == nullptr || key_pool == nullptr || value_pool == nullptr || out == nullptr || block_table == nullptr ||
+      cu_seq_q == nullptr || seqused_k == nullptr)
+    return fail(HB_ERR_INVALID, "null attention pointer");
+  if (!aligned(key_pool, 16) || !aligned(value_pool, 16) || !aligned(q, 16) || !aligned(out, 16))
+    return fail(HB_ERR_INVALID, "q, out and pools must be 16-byte aligned");
+  const size_t need = hb_attention_workspace_bytes(partial_records, heads, head_dim);
+  if (workspace_bytes < need || (need > 0 && workspace == nullptr))
+    return fail(HB_ERR_INVALID, "workspace holds %zu bytes, needs %zu", workspace_bytes, need);
+  if (total_tokens == 0) return HB_OK;
+
+  hb::AttentionParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.block_table = block_table;
+  p.cu_seq_q = cu_seq_q;
+  p.seqused_k = seqused_k;
+  p.decode_items = decode_items;
+  p.prefill_items = prefill_items;
+  p.ws_out = static_cast<float*>(workspace);
+  p.ws_lse = p.ws_out ? p.ws_out + static_cast<size_t>(partial_records) * heads * head_dim : nullptr;
+  p.width = width;
+  p.num_pages = static_cast<int32_t>(num_pages);
+  p.page_size = page_size;
+  p.heads = heads;
+  p.kv_heads = kv_heads;
+  p.split_keys = split_keys;
+  p.tokens = total_tokens;
+  p.scale_log2 = scale * 1.4426950408889634f;
+
+  const uint64_t pool_tokens = static_cast<uint64_t>(num_pages) * page_size;
+  const uint64_t row_bytes = static_cast<uint64_t>(kv_heads) * head_dim * 2;
+  CUtensorMap kmap, vmap;
+  if (int rc = encode_3d(&kmap, key_pool, head_dim, kv_heads, pool_tokens, head_dim * 2, row_bytes, 64, 1,
+                         hb::kDecTileKeys))
+    return rc;
+  if (int rc = encode_3d(&vmap, value_pool, head_dim, kv_heads, pool_tokens, head_dim * 2, row_bytes, 64, 1,
+                         hb::kDecTileKeys))
+    return rc;
+  const int gs = group_slot(group);
+
+  if (num_decode_items > 0) {
+    if (decode_items == nullptr) return fail(HB_ERR_INVALID, "null decode items");
+    const dim3 grid(num_decode_items, kv_heads);
+#define HB_DECODE(G)                                                                                          \
+  do {                                                                                                        \
+    if (int rc = ensure_smem(hb::decode_attention_kernel<G>, hb::kDecSmemBytes, g_dec_smem[gs])) return rc;   \
+    hb::decode_attention_kernel<G><<<grid, hb::kDecThreads, hb::kDecSmemBytes, stream>>>(p, kmap, vmap);      \
+    if (int rc = check_launch("decode_attention_kernel")) return rc;                                          \
+    if (partial_records > 0) {                                                                                \
+      hb::decode_combine_kernel<G><<<grid, 128, 0, stream>>>(p);                                              \
+      if (int rc = check_launch("decode_combine_kernel")) return rc;                                          \
+    }                                                                                                         \
+  } while (0)
+    switch (group) {
+      case 1: HB_DECODE(1); break;
+      case 2: HB_DECODE(2); break;
+      case 4: HB_DECODE(4); break;
+      default: HB_DECODE(8); break;
+    }
+#undef HB_DECODE
+  }
+  if (num_prefill_items > 0) {
+    if (prefill_items == nullptr) return fail(HB_ERR_INVALID, "null prefill items");
+    CUtensorMap qmap;
+    const dim3 grid(num_prefill_items, kv_heads);
+#define HB_PREFILL(G)                                                                                           \
+  do {                                                                                                          \
+    if (int rc = encode_3d(&qmap, q, head_dim, heads, total_tokens, head_dim * 2,                               \
+                           static_cast<uint64_t>(heads) * head_dim * 2, 64, G, hb::kPreRows / G))               \
+      return rc;                                                                                                \
+    if (int rc = ensure_smem(hb::prefill_attention_kernel<G>, hb::kPreSmemBytes, g_pre_smem[gs])) return rc;     \
+    hb::prefill_attention_kernel<G><<<grid, hb::kPreThreads, hb::kPreSmemBytes, stream>>>(p, qmap, kmap, vmap);  \
+    if (int rc = check_launch("prefill_attention_kernel")) return rc;                                           \
+  } while (0)
+    switch (group) {
+      case 1: HB_PREFILL(1); break;
+      case 2: HB_PREFILL(2); break;
+      case 4: HB_PREFILL(4); break;
+      default: HB_PREFILL(8); break;
+    }
+#undef HB_PREFILL
+  }
+  return HB_OK;
+}
+
+int hb_rmsnorm(const void* x, int64_t rows_in, const int64_t* row_index, const float* scale, float eps, void* out,
+               int32_t rows, int32_t hidden, cudaStream_t stream) {
+  if (rows < 0 || hidden < 8 || hidden % 8 || hidden > 8 * hb::kRowVecs * hb::kRowThreads)
+    return fail(HB_ERR_UNSUPPORTED, "hidden %d must be a multiple of 8 up to %d", hidden,
+                8 * hb::kRowVecs * hb::kRowThreads);
+  if (rows == 0) return HB_OK;
+  if (x == nullptr || scale == nullptr || out == nullptr) return fail(HB_ERR_INVALID, "null rmsnorm pointer");
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(scale, 16))
+    return fail(HB_ERR_INVALID, "rmsnorm pointers must be 16-byte aligned");
+  hb::RowNormParams p{static_cast<const __nv_bfloat16*>(x), nullptr, row_index, scale, nullptr,
+                      static_cast<__nv_bfloat16*>(out), rows, hidden, row_index ? rows_in : rows, eps};
+  hb::rmsnorm_kernel<<<rows, hb::kRowThreads, 0, stream>>>(p);
+  return check_launch("rmsnorm_kernel");
+}
+
+int hb_add_rmsnorm(const void* x, const void* y, const float* scale, float eps, void* sum_out, void* norm_out,
+                   int32_t rows, int32_t hidden, cudaStream_t stream) {
+  if (rows < 0 || hidden < 8 || hidden % 8 || hidden > 8 * hb::kRowVecs * hb::kRowThreads)
+    return fail(HB_ERR_UNSUPPORTED, "hidden %d must be a multiple of 8 up to %d", hidden,
+                8 * hb::kRowVecs * hb::kRowThreads);
+  if (rows == 0) return HB_OK;
+  if (x == nullptr || y == nullptr || scale == nullptr || sum_out == nullptr || norm_out == nullptr)
+    return fail(HB_ERR_INVALID, "null add_rmsnorm pointer");
+  if (!aligned(x, 16) || !aligned(y, 16) || !aligned(sum_out, 16) || !aligned(norm_out, 16) || !aligned(scale, 16))
+    return fail(HB_ERR_INVALID, "add_rmsnorm pointers must be 16-byte aligned");
+  hb::RowNormParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y), nullptr, scale,
+                      static_cast<__nv_bfloat16*>(sum_out), static_cast<__nv_bfloat16*>(norm_out), rows, hidden,
+                      rows, eps};
+  hb::rmsnorm_kernel<<<rows, hb::kRowThreads, 0, stream>>>(p);
+  return check_launch("add_rmsnorm_kernel");
+}
+
+int hb_swiglu(const void* gate_up, void* out, int64_t rows, int64_t inter, cudaStream_t stream) {
+  if (rows < 0 || inter < 8 || inter % 8)
+    return fail(HB_ERR_UNSUPPORTED, "inter %lld must be a multiple of 8", static_cast<long long>(inter));
+  if (rows == 0) return HB_OK;
+  if (gate_up == nullptr || out == nullptr || !aligned(gate_up, 16) || !aligned(out, 16))
+    return fail(HB_ERR_INVALID, "swiglu pointers must be non-null and 16-byte aligned");
+  hb::SwigluParams p{static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(out), rows, inter};
+  const int64_t vecs = rows * inter / 8;
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((vecs + 255) / 256, 148 * 16));
+  hb::swiglu_kernel<<<blocks, 256, 0, stream>>>(p);
+  return check_launch("swiglu_kernel");
+}
+
+int hb_embedding(const int64_t* ids, const void* table, int64_t vocab, void* out, int64_t tokens, int32_t hidden,
+                 cudaStream_t stream) {
+  if (tokens < 0 || hidden < 8 || hidden % 8)
+    return fail(HB_ERR_UNSUPPORTED, "hidden %d must be a multiple of 8", hidden);
+  if (tokens == 0) return HB_OK;
+  if (ids == nullptr || table == nullptr || out == nullptr || !aligned(table, 16) || !aligned(out, 16))
+    return fail(HB_ERR_INVALID, "embedding pointers must be non-null and 16-byte aligned");
+  hb::EmbedParams p{ids, static_cast<const __nv_bfloat16*>(table), static_cast<__nv_bfloat16*>(out), tokens, vocab,
+                    hidden};
+  hb::embed_kernel<<<static_cast<unsigned>(tokens), 256, 0, stream>>>(p);
+  return check_launch("embed_kernel");
+}
+
+int hb_page_copy(void* pool_base, int64_t tensor_stride_bytes, int32_t tensors, int64_t page_bytes, int64_t num_pages,
+                 const int32_t* src_pages, const int32_t* dst_pages, int32_t pairs, cudaStream_t stream) {
+  if (pairs < 0 || tensors < 1 || page_bytes < 16 || page_bytes % 16 || num_pages < 1)
+    return fail(HB_ERR_INVALID, "bad page copy sizes");
+  if (pairs == 0) return HB_OK;
+  if (pool_base == nullptr || src_pages == nullptr || dst_pages == nullptr || !aligned(pool_base, 16) ||
+      tensor_stride_bytes % 16)
+    return fail(HB_ERR_INVALID, "page copy pointers must be non-null and 16-byte aligned");
+  hb::PageCopyParams p{static_cast<uint8_t*>(pool_base), tensor_stride_bytes, tensors, page_bytes, num_pages,
+                       src_pages, dst_pages, pairs};
+  const int64_t vecs = static_cast<int64_t>(pairs) * tensors * (page_bytes / 16);
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((vecs + 255) / 256, 148 * 8));
+  hb::page_copy_kernel<<<blocks, 256, 0, stream>>>(p);
+  return check_launch("page_copy_kernel");
+}
+
+int hb_sample(const void* logits, int64_t row_stride, int32_t rows, int32_t vocab, const float* temperature,
+              const float* top_p, const float* uniforms, int64_t* out_ids, cudaStream_t stream) {
+  if (rows < 0 || vocab < 1 || row_stride < vocab) return fail(HB_ERR_INVALID, "bad sampler sizes");
+  if (rows == 0) return HB_OK;
+  if (logits == nullptr || temperature == nullptr || top_p == nullptr || uniforms == nullptr || out_ids == nullptr)
+    return fail(HB_ERR_INVALID, "null sampler pointer");
+  hb::SampleParams p{static_cast<const __nv_bfloat16*>(logits), row_stride, rows, vocab, temperature, top_p, uniforms,
+                     out_ids};
+  hb::sample_kernel<<<rows, hb::kSampleThreads, 0, stream>>>(p);
+  return check_launch("sample_kernel");
+}
+
+}  // extern "C"

@@ -1,0 +1,224 @@
+// Kernel (a): GPU-side tick packing.
+//
+// One scheduler tick selects rows (requests) and a token count per row. The
+// reference builds the attention metadata for that selection in Python lists
+// (PackedBatchCache.prepare_packed, src/helios/runtime/qwen3/paged_cache.py:418-494;
+// PagedBatchCache.prepare, :221-270) and copies each list to the device. Here the
+// host uploads only O(rows + new pages) integers and one CTA expands them:
+//
+//   * page updates are applied to a device-resident page arena
+//     ([slots, arena_width] int32, one slot per live request cache);
+//   * block-scans over rows give cu_seq_q, cu_seq_k, seqused_k, logit offsets and
+//     the attention work-list offsets;
+//   * block_table[r, j] = arena[slot_r, j] for j < n_pages_r, else 0;
+//   * per token: position = length_r + i, write slot = page(pos / P) * P + pos % P,
+//     and the owning row;
+//   * logit_indices: the trailing logit_count_r tokens of each row;
+//   * the attention work lists: split-K items for decode-class rows
+//     (count <= decode_max_tokens) and query tiles for prefill-class rows.
+// Every output write is bounded by the capacity the host sized it for; an entry
+// that would fall outside is skipped and reported in the status word.
+#pragma once
+
+#include "hb_common.cuh"
+
+namespace hb {
+
+struct TickPackParams {
+  const int32_t* rows;     // [B][5] slot, length, count, logit_count, n_pages
+  const int32_t* updates;  // [U][3] slot, page position, page index
+  int32_t* arena;          // [slots][arena_width]
+  int32_t num_rows, num_updates, arena_width, arena_slots, page_size, width, num_pages;
+  int32_t decode_max_tokens, split_keys, prefill_tile_tokens;
+  int32_t* block_table;    // [B][width]
+  int32_t* cu_seq_q;       // [B+1]
+  int32_t* cu_seq_k;       // [B+1]
+  int32_t* seqused_k;      // [B]
+  int64_t* positions;      // [T]
+  int64_t* write_slots;    // [T]
+  int32_t* token_row;      // [T]
+  int64_t* logit_indices;  // [logit_capacity]
+  int32_t* decode_items;   // [decode_capacity][4] row, split, partial_base, n_splits
+  int32_t* prefill_items;  // [prefill_capacity][2] row, query start
+  int32_t total_tokens, logit_capacity, decode_capacity, prefill_capacity;
+};
+
+constexpr int kTickThreads = 1024;
+
+__device__ __forceinline__ int row_splits(int end, int split_keys) { return (end + split_keys - 1) / split_keys; }
+
+__global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams p) {
+  extern __shared__ int32_t sm[];
+  const int B = p.num_rows;
+  // Exclusive offsets per row, B+1 entries each.
+  int32_t* q_off = sm;
+  int32_t* k_off = q_off + (B + 1);
+  int32_t* l_off = k_off + (B + 1);
+  int32_t* d_off = l_off + (B + 1);
+  int32_t* r_off = d_off + (B + 1);
+  int32_t* f_off = r_off + (B + 1);
+  __shared__ int32_t warp_tot[32][6];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  // 1. Page-arena updates (pages acquired or restored since the last tick).
+  for (int u = tid; u < p.num_updates; u += kTickThreads) {
+    const int32_t slot = p.updates[3 * u], pos = p.updates[3 * u + 1], page = p.updates[3 * u + 2];
+    if (slot < 0 || slot >= p.arena_slots || pos < 0 || pos >= p.arena_width || page < 0 || page >= p.num_pages) {
+      raise_status(kStatusBadPage);
+      continue;
+    }
+    p.arena[static_cast<int64_t>(slot) * p.arena_width + pos] = page;
+  }
+
+  // 2. Block scan over rows. Each thread owns a contiguous chunk of rows.
+  const int per = (B + kTickThreads - 1) / kTickThreads;
+  const int r0 = min(B, tid * per), r1 = min(B, r0 + per);
+  int32_t s[6] = {0, 0, 0, 0, 0, 0};
+  for (int r = r0; r < r1; ++r) {
+    const int32_t len = p.rows[5 * r + 1], cnt = p.rows[5 * r + 2], lc = p.rows[5 * r + 3];
+    const int32_t end = len + cnt;
+    s[0] += cnt;
+    s[1] += end;
+    s[2] += lc;
+    if (cnt <= p.decode_max_tokens) {
+      const int sp = row_splits(end, p.split_keys);
+      s[3] += sp;
+      s[4] += sp * cnt;
+    } else {
+      s[5] += (cnt + p.prefill_tile_tokens - 1) / p.prefill_tile_tokens;
+    }
+  }
+  int32_t incl[6];
+#pragma unroll
+  for (int f = 0; f < 6; ++f) {
+    int32_t v = s[f];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t n = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += n;
+    }
+    incl[f] = v;
+    if (lane == 31) warp_tot[warp][f] = v;
+  }
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int f = 0; f < 6; ++f) {
+      int32_t v = warp_tot[lane][f];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+      }
+      warp_tot[lane][f] = v;  // inclusive over warps
+    }
+  }
+  __syncthreads();
+  int32_t base[6];
+#pragma unroll
+  for (int f = 0; f < 6; ++f) base[f] = (warp ? warp_tot[warp - 1][f] : 0) + incl[f] - s[f];
+  for (int r = r0; r < r1; ++r) {
+    const int32_t len = p.rows[5 * r + 1], cnt = p.rows[5 * r + 2], lc = p.rows[5 * r + 3];
+    const int32_t end = len + cnt;
+    q_off[r] = base[0];
+    k_off[r] = base[1];
+    l_off[r] = base[2];
+    d_off[r] = base[3];
+    r_off[r] = base[4];
+    f_off[r] = base[5];
+    base[0] += cnt;
+    base[1] += end;
+    base[2] += lc;
+    if (cnt <= p.decode_max_tokens) {
+      const int sp = row_splits(end, p.split_keys);
+      base[3] += sp;
+      base[4] += sp * cnt;
+    } else {
+      base[5] += (cnt + p.prefill_tile_tokens - 1) / p.prefill_tile_tokens;
+    }
+  }
+  if (tid == kTickThreads - 1) {
+    q_off[B] = base[0];
+    k_off[B] = base[1];
+    l_off[B] = base[2];
+    d_off[B] = base[3];
+    r_off[B] = base[4];
+    f_off[B] = base[5];
+  }
+  __syncthreads();
+
+  // 3. Row-level outputs, logit rows and attention work items.
+  for (int r = tid; r <= B; r += kTickThreads) {
+    p.cu_seq_q[r] = q_off[r];
+    p.cu_seq_k[r] = k_off[r];
+  }
+  for (int r = tid; r < B; r += kTickThreads) {
+    const int32_t len = p.rows[5 * r + 1], cnt = p.rows[5 * r + 2], lc = p.rows[5 * r + 3];
+    const int32_t end = len + cnt;
+    p.seqused_k[r] = end;
+    for (int i = 0; i < lc; ++i) {
+      if (l_off[r] + i >= p.logit_capacity) { raise_status(kStatusBadRow); break; }
+      p.logit_indices[l_off[r] + i] = static_cast<int64_t>(q_off[r + 1] - lc + i);
+    }
+    if (cnt <= p.decode_max_tokens) {
+      const int sp = row_splits(end, p.split_keys);
+      for (int sidx = 0; sidx < sp; ++sidx) {
+        if (d_off[r] + sidx >= p.decode_capacity) { raise_status(kStatusBadRow); break; }
+        int32_t* it = p.decode_items + 4 * (d_off[r] + sidx);
+        it[0] = r;
+        it[1] = sidx;
+        it[2] = r_off[r] + sidx * cnt;
+        it[3] = sp;
+      }
+    } else {
+      const int tiles = (cnt + p.prefill_tile_tokens - 1) / p.prefill_tile_tokens;
+      for (int t = 0; t < tiles; ++t) {
+        if (f_off[r] + t >= p.prefill_capacity) { raise_status(kStatusBadRow); break; }
+        p.prefill_items[2 * (f_off[r] + t)] = r;
+        p.prefill_items[2 * (f_off[r] + t) + 1] = t * p.prefill_tile_tokens;
+      }
+    }
+  }
+
+  // 4. Block table rows from the arena, zero-padded to `width`.
+  const int64_t cells = static_cast<int64_t>(B) * p.width;
+  for (int64_t c = tid; c < cells; c += kTickThreads) {
+    const int r = static_cast<int>(c / p.width), j = static_cast<int>(c % p.width);
+    const int32_t slot = p.rows[5 * r], npages = p.rows[5 * r + 4];
+    int32_t v = 0;
+    if (j < npages) {
+      v = (j < p.arena_width && slot >= 0 && slot < p.arena_slots)
+              ? p.arena[static_cast<int64_t>(slot) * p.arena_width + j]
+              : -1;
+      if (v < 0 || v >= p.num_pages) {
+        raise_status(kStatusBadPage);
+        v = 0;
+      }
+    }
+    p.block_table[c] = v;
+  }
+
+  // 5. Per-token positions, KV write slots and owning rows.
+  for (int t = tid; t < p.total_tokens && t < q_off[B]; t += kTickThreads) {
+    int lo = 0, hi = B;  // largest r with q_off[r] <= t
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (q_off[mid] <= t) lo = mid; else hi = mid;
+    }
+    const int r = lo;
+    const int32_t slot = p.rows[5 * r], len = p.rows[5 * r + 1], npages = p.rows[5 * r + 4];
+    const int32_t pos = len + (t - q_off[r]);
+    const int32_t pidx = pos / p.page_size;
+    int32_t page = 0;
+    if (pidx < npages && pidx < p.arena_width && slot >= 0 && slot < p.arena_slots) {
+      page = p.arena[static_cast<int64_t>(slot) * p.arena_width + pidx];
+    } else {
+      raise_status(kStatusBadPage);
+    }
+    p.positions[t] = pos;
+    p.write_slots[t] = static_cast<int64_t>(page) * p.page_size + (pos % p.page_size);
+    p.token_row[t] = r;
+  }
+}
+
+}  // namespace hb

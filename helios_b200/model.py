@@ -1,0 +1,203 @@
+"""Qwen3 decoder over the paged caches, running the B200 kernels.
+
+Module tree, parameter names and construction order are the reference's
+(src/helios/runtime/qwen3/model.py:13-30, layers.py:13-232): ``token_embedding``,
+``blocks.{i}.attention.{query,key,value,output,q_norm,k_norm}``,
+``blocks.{i}.feed_forward.{gate,up,down}``, ``blocks.{i}.{input_norm,post_attention_norm}``,
+``final_norm``, ``output`` tied to the embedding, fp32 norm scales and fp32
+``cos``/``sin`` buffers. So ``load_state_dict`` of reference weights works and
+``torch.manual_seed(s); Qwen3Model(config)`` draws the same random weights.
+
+The forward is the packed mixed-batch path of ``Qwen3Model._forward_packed``
+(model.py:92-110), restated for one flattened token dimension:
+
+    x = embed(ids)                                       kernel: embed
+    n = rmsnorm(x, input_norm_0)                         kernel: rmsnorm
+    per layer:
+      qkv = n @ [Wq; Wk; Wv]^T                           cuBLAS GEMM (one, fused weights)
+      q = attend(norm+rope(q), append(norm+rope(k), v))  kernels b + c
+      h, n2 = x + q @ Wo^T, rmsnorm(.)                   GEMM + kernel: add_rmsnorm
+      m = silu(n2 @ Wg^T) * (n2 @ Wu^T) @ Wd^T           GEMM (fused gate|up) + kernel: swiglu + GEMM
+      x, n = h + m, rmsnorm(., next norm)                kernel: add_rmsnorm
+    logits = n[logit rows] @ E^T                         GEMM
+
+Every bf16 rounding point of the reference is kept (projection outputs,
+residual sums, silu output, gated product, norms). Decode-only and uniform
+prefill ticks (``PagedBatchCache`` + ``prepare(tokens)``, model.py:32-90,
+:133-169) use the same path with one logit row per sequence.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from helios_b200 import ops
+from helios_b200.config import Qwen3Config
+from helios_b200.paged_cache import PackedBatchCache, PagedBatchCache
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, hidden_size: int, eps: float) -> None:
+        super().__init__()
+        self.eps = eps
+        self.scale = nn.Parameter(torch.ones(hidden_size))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        flat = x.reshape(-1, x.shape[-1])
+        return ops.rmsnorm(flat.contiguous(), self.scale, self.eps).view(x.shape)
+
+
+def rope_parameters(config: Qwen3Config) -> tuple[torch.Tensor, torch.Tensor]:
+    """Same tables as layers.py:43-51: angles = pos * theta^(-2i/d), duplicated halves."""
+    inverse = 1.0 / (config.rope_base ** (torch.arange(0, config.head_dim, 2, dtype=torch.float32) / config.head_dim))
+    angles = torch.arange(config.context_length, dtype=torch.float32).unsqueeze(1) * inverse.unsqueeze(0)
+    angles = torch.cat((angles, angles), dim=1)
+    return torch.cos(angles), torch.sin(angles)
+
+
+class _Fused:
+    """Concatenation of several Linear weights along the output dimension, rebuilt
+    when any of them is replaced or modified in place (e.g. by load_state_dict)."""
+
+    def __init__(self, *linears: nn.Linear) -> None:
+        self.linears = linears
+        self.key = None
+        self.weight: torch.Tensor | None = None
+
+    def _key(self):
+        return tuple((l.weight.data_ptr(), l.weight._version, l.weight.device) for l in self.linears)
+
+    def get(self) -> torch.Tensor:
+        if self._key() != self.key:
+            # Normal (not inference-mode) tensors, so the weights stay loadable afterwards.
+            with torch.inference_mode(False), torch.no_grad():
+                fused = torch.cat([l.weight for l in self.linears], dim=0).contiguous()
+                # Point the Linear weights at slices of the fused copy: no duplicate storage.
+                start = 0
+                for l in self.linears:
+                    n = l.weight.shape[0]
+                    l.weight = nn.Parameter(fused[start:start + n], requires_grad=False)
+                    start += n
+            self.weight = fused
+            self.key = self._key()
+        return self.weight
+
+
+class FeedForward(nn.Module):
+    def __init__(self, config: Qwen3Config) -> None:
+        super().__init__()
+        self.gate = nn.Linear(config.hidden_size, config.hidden_dim, bias=False, dtype=config.dtype)
+        self.up = nn.Linear(config.hidden_size, config.hidden_dim, bias=False, dtype=config.dtype)
+        self.down = nn.Linear(config.hidden_dim, config.hidden_size, bias=False, dtype=config.dtype)
+        self._gate_up = _Fused(self.gate, self.up)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        """``x [T, hidden]`` -> ``[T, hidden]``: one gate|up GEMM, fused SwiGLU, down GEMM."""
+        gate_up = F.linear(x, self._gate_up.get())
+        act = torch.empty((x.shape[0], self.gate.out_features), dtype=x.dtype, device=x.device)
+        ops.swiglu(gate_up, act)
+        return F.linear(act, self.down.weight)
+
+
+class GroupedQueryAttention(nn.Module):
+    def __init__(self, config: Qwen3Config) -> None:
+        super().__init__()
+        if config.n_heads % config.n_kv_heads:
+            raise ValueError("The number of Q heads must be divisible by the number of KV heads.")
+        self.n_heads = config.n_heads
+        self.n_kv_heads = config.n_kv_heads
+        self.group_size = config.n_heads // config.n_kv_heads
+        self.head_dim = config.head_dim
+        self.query = nn.Linear(config.hidden_size, config.n_heads * config.head_dim, bias=False, dtype=config.dtype)
+        self.key = nn.Linear(config.hidden_size, config.n_kv_heads * config.head_dim, bias=False, dtype=config.dtype)
+        self.value = nn.Linear(config.hidden_size, config.n_kv_heads * config.head_dim, bias=False, dtype=config.dtype)
+        self.output = nn.Linear(config.n_heads * config.head_dim, config.hidden_size, bias=False, dtype=config.dtype)
+        self.q_norm = RMSNorm(config.head_dim, config.rms_norm_eps)
+        self.k_norm = RMSNorm(config.head_dim, config.rms_norm_eps)
+        self._qkv = _Fused(self.query, self.key, self.value)
+
+    def forward(self, x: torch.Tensor, cache: PagedBatchCache, layer_index: int, cos: torch.Tensor,
+                sin: torch.Tensor) -> torch.Tensor:
+        """``x [T, hidden]`` (already input-normed) -> attention block output ``[T, hidden]``."""
+        qkv = F.linear(x, self._qkv.get())
+        context = cache.attend_fused(layer_index, qkv, self.q_norm.scale, self.k_norm.scale, self.q_norm.eps, cos, sin)
+        return F.linear(context.view(x.shape[0], -1), self.output.weight)
+
+
+class TransformerBlock(nn.Module):
+    def __init__(self, config: Qwen3Config) -> None:
+        super().__init__()
+        self.attention = GroupedQueryAttention(config)
+        self.feed_forward = FeedForward(config)
+        self.input_norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        self.post_attention_norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+
+
+class Qwen3Model(nn.Module):
+    def __init__(self, config: Qwen3Config) -> None:
+        super().__init__()
+        self.config = config
+        self.token_embedding = nn.Embedding(config.vocab_size, config.hidden_size, dtype=config.dtype)
+        self.blocks = nn.ModuleList(TransformerBlock(config) for _ in range(config.n_layers))
+        self.final_norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        self.output = nn.Linear(config.hidden_size, config.vocab_size, bias=False, dtype=config.dtype)
+        self.output.weight = self.token_embedding.weight
+        cos, sin = rope_parameters(config)
+        self.register_buffer("cos", cos, persistent=False)
+        self.register_buffer("sin", sin, persistent=False)
+
+    def forward(self, input_ids: torch.Tensor, cache: PagedBatchCache | None = None,
+                position_ids: torch.Tensor | None = None,
+                cache_slots: Sequence[int] | torch.Tensor | None = None) -> torch.Tensor:
+        """Reference signature (model.py:32-90). Packed caches return ``[logit rows, V]``;
+        uniform paged batches return the last position of each row, ``[B, 1, V]``.
+        Positions always come from the paged cache (``position_ids`` is accepted for
+        signature compatibility; the reference derives the same values)."""
+        if isinstance(cache, PackedBatchCache):
+            return self._forward_packed(input_ids, cache)
+        if not isinstance(cache, PagedBatchCache):
+            raise TypeError("The B200 model runs over paged KV caches (PagedBatchCache / PackedBatchCache).")
+        if cache_slots is not None:
+            cache.slot_ids(cache_slots)
+        tokens = input_ids.shape[1]
+        if input_ids.shape[0] != cache.batch_size:
+            raise ValueError("Paged input rows must match the paged batch.")
+        if max(c.length + tokens for c in cache.caches) > self.config.context_length:
+            raise ValueError(f"Qwen3-4B supports at most {self.config.context_length:,} tokens per request.")
+        # prepare(tokens) packed one logit row per sequence: its last position.
+        _, normed = self._layers(input_ids.reshape(-1), cache)
+        cache.advance(tokens, slots=cache_slots)
+        rows = normed.index_select(0, cache.logit_rows)
+        return F.linear(rows, self.output.weight).view(cache.batch_size, 1, -1)
+
+    def _forward_packed(self, input_ids: torch.Tensor, cache: PackedBatchCache) -> torch.Tensor:
+        if input_ids.shape != (1, sum(cache.counts)):
+            raise ValueError("Packed input does not match query lengths.")
+        _, normed = self._layers(input_ids.reshape(-1), cache)
+        cache.advance_packed()
+        rows = normed.index_select(0, cache.logit_indices)
+        return F.linear(rows, self.output.weight)
+
+    def _layers(self, ids: torch.Tensor, cache: PagedBatchCache) -> tuple[torch.Tensor, torch.Tensor]:
+        """Run every block; returns (residual stream, final-normed stream) ``[T, hidden]``."""
+        if ids.dtype != torch.long:
+            ids = ids.long()
+        ids = ids.contiguous()
+        tokens, hidden = ids.numel(), self.config.hidden_size
+        eps = self.config.rms_norm_eps
+        dev, dt = self.token_embedding.weight.device, self.config.dtype
+        x = ops.embedding(ids, self.token_embedding.weight, torch.empty((tokens, hidden), dtype=dt, device=dev))
+        normed = ops.rmsnorm(x, self.blocks[0].input_norm.scale, eps)
+        h = torch.empty_like(x)
+        normed2 = torch.empty_like(x)
+        for index, block in enumerate(self.blocks):
+            attn = block.attention(normed, cache, index, self.cos, self.sin)
+            ops.add_rmsnorm(x, attn, block.post_attention_norm.scale, eps, h, normed2)
+            mlp = block.feed_forward(normed2)
+            nxt = self.blocks[index + 1].input_norm.scale if index + 1 < len(self.blocks) else self.final_norm.scale
+            ops.add_rmsnorm(h, mlp, nxt, eps, x, normed)
+        return x, normed

@@ -1,0 +1,167 @@
+/*
+ * helios_b200 — C ABI of the B200 (sm_100a) packed-tick hot path.
+ *
+ * The reference (sidmanale643/helios) runs its packed mixed-batch forward in
+ * Python/PyTorch; these entry points replace the op sequences it runs per tick.
+ * Every function takes raw device pointers, element counts and a cudaStream_t
+ * (a CUstream handle, e.g. torch.cuda.current_stream().cuda_stream), borrows the
+ * memory for the launch only, allocates nothing, and returns 0 or a negative
+ * HB_ERR_* code with a message from hb_last_error() (per calling thread).
+ * Device-side input checks (page indices, KV slots, RoPE positions, token ids)
+ * skip the bad element and set a bit in a device status word read back by
+ * hb_device_status(). All tensors are bf16 unless stated.
+ *
+ * Paths below are within the reference project.
+ */
+#ifndef HELIOS_B200_H_
+#define HELIOS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define HB_API __attribute__((visibility("default")))
+#else
+#define HB_API
+#endif
+
+typedef struct CUstream_st* hb_stream_t; /* same object as cudaStream_t / CUstream */
+#if !defined(__CUDACC__) && !defined(__DRIVER_TYPES_H__)
+typedef hb_stream_t cudaStream_t;
+#endif
+
+#define HB_VERSION 1
+#define HB_OK 0
+#define HB_ERR_INVALID (-1)     /* bad pointer, size or layout: the reference's ValueError */
+#define HB_ERR_UNSUPPORTED (-2) /* shape outside what the kernels are built for */
+#define HB_ERR_CUDA (-3)        /* launch or driver failure */
+#define HB_MAX_TICK_ROWS 8192
+
+/* Device status bits (hb_device_status). */
+#define HB_STATUS_WAIT_TIMEOUT (1u << 0)
+#define HB_STATUS_BAD_SLOT (1u << 1)
+#define HB_STATUS_BAD_POSITION (1u << 2)
+#define HB_STATUS_BAD_PAGE (1u << 3)
+#define HB_STATUS_BAD_TOKEN (1u << 4)
+#define HB_STATUS_BAD_ROW (1u << 5)
+
+HB_API int hb_version(void);
+HB_API const char* hb_last_error(void);
+
+/* Synchronise the current device, read the status word, optionally clear it. */
+HB_API int hb_device_status(uint32_t* status, int clear);
+
+/*
+ * (a) Tick packing. Replaces PackedBatchCache.prepare_packed
+ * (src/helios/runtime/qwen3/paged_cache.py:418-494) and PagedBatchCache.prepare
+ * (paged_cache.py:221-270), whose Python lists are rebuilt and copied every tick.
+ *   rows     device int32 [num_rows][5]: arena slot, committed length, query count,
+ *            logit count, pages held (after this tick's acquisitions)
+ *   updates  device int32 [num_updates][3]: arena slot, page position, page index
+ *   arena    device int32 [arena_slots][arena_width]: per-request page lists
+ * Outputs (all device): block_table int32 [num_rows][width] (zero-padded),
+ * cu_seq_q/cu_seq_k int32 [num_rows+1], seqused_k int32 [num_rows], positions,
+ * write_slots int64 [total_tokens], token_row int32 [total_tokens], logit_indices
+ * int64 [logit_capacity], decode_items int32 [decode_capacity][4] (row, split,
+ * partial base, splits) for rows with count <= decode_max_tokens, split every
+ * split_keys keys, prefill_items int32 [prefill_capacity][2] (row, query start)
+ * every prefill_tile_tokens queries. Entries past a capacity are not written.
+ */
+HB_API int hb_tick_pack(const int32_t* rows, int32_t num_rows, const int32_t* updates, int32_t num_updates,
+                        int32_t* arena, int32_t arena_slots, int32_t arena_width, int32_t page_size, int32_t width,
+                        int32_t num_pages, int32_t decode_max_tokens, int32_t split_keys, int32_t prefill_tile_tokens,
+                        int32_t total_tokens, int32_t* block_table, int32_t* cu_seq_q, int32_t* cu_seq_k,
+                        int32_t* seqused_k, int64_t* positions, int64_t* write_slots, int32_t* token_row,
+                        int64_t* logit_indices, int32_t logit_capacity, int32_t* decode_items,
+                        int32_t decode_capacity, int32_t* prefill_items, int32_t prefill_capacity,
+                        cudaStream_t stream);
+
+/*
+ * (b) Fused per-head q/k RMSNorm + RoPE + paged KV append. Replaces, in
+ * GroupedQueryAttention.forward (src/helios/runtime/qwen3/layers.py:147-160),
+ * q_norm/k_norm (RMSNorm.forward, layers.py:36-40) and apply_rope with position ids
+ * (layers.py:54-72), plus PagedBatchCache._write (paged_cache.py:335-345).
+ * q/k/v are addressed by element strides per token and per head; q_out is
+ * [tokens][heads][head_dim] (null: q not produced); the pools are
+ * [pool_slots][kv_heads][head_dim] (one layer). Null q_scale/k_scale skip the norm,
+ * null cos/sin skip the rotation (plain append, as PagedBatchCache.attend needs).
+ */
+HB_API int hb_qk_norm_rope_append(const void* q, int64_t q_token_stride, int64_t q_head_stride, const void* k,
+                                  int64_t k_token_stride, int64_t k_head_stride, const void* v,
+                                  int64_t v_token_stride, int64_t v_head_stride, const float* q_scale,
+                                  const float* k_scale, float eps, const float* cos, const float* sin,
+                                  int64_t rope_rows, const int64_t* positions, const int64_t* write_slots,
+                                  void* q_out, void* key_pool, void* value_pool, int64_t pool_slots, int32_t tokens,
+                                  int32_t heads, int32_t kv_heads, int32_t head_dim, cudaStream_t stream);
+
+/* Bytes of float workspace hb_paged_attention needs for `partial_records` split records. */
+HB_API size_t hb_attention_workspace_bytes(int32_t partial_records, int32_t heads, int32_t head_dim);
+
+/*
+ * (c) Paged varlen GQA attention, bottom-right causal. Replaces the
+ * varlen_attn(..., block_table, seqused_k, window_size=(-1, 0), num_splits=1) calls
+ * of PackedBatchCache.attend (src/helios/runtime/qwen3/paged_cache.py:501-520) and
+ * PagedBatchCache.attend (paged_cache.py:301-333); CPU meaning in
+ * paged_cache.py:521-546. q and out are [total_tokens][heads][head_dim]; the
+ * pools [num_pages][page_size][kv_heads][head_dim]. Work items come from
+ * hb_tick_pack: decode items run split-K (partials in `workspace`, merged by a
+ * combine launch), prefill items run on tcgen05 tensor cores.
+ */
+HB_API int hb_paged_attention(const void* q, const void* key_pool, const void* value_pool, int64_t num_pages,
+                              int32_t page_size, const int32_t* block_table, int32_t width, const int32_t* cu_seq_q,
+                              const int32_t* seqused_k, const int32_t* decode_items, int32_t num_decode_items,
+                              const int32_t* prefill_items, int32_t num_prefill_items, int32_t partial_records,
+                              int32_t split_keys, int32_t total_tokens, int32_t heads, int32_t kv_heads,
+                              int32_t head_dim, float scale, void* workspace, size_t workspace_bytes, void* out,
+                              cudaStream_t stream);
+
+/*
+ * Hidden-size RMSNorm (RMSNorm.forward, src/helios/runtime/qwen3/layers.py:36-40).
+ * With row_index (int64 [rows]) the rows are gathered first, as the logit-row
+ * index_select before the final norm (src/helios/runtime/qwen3/model.py:108-110).
+ */
+HB_API int hb_rmsnorm(const void* x, int64_t rows_in, const int64_t* row_index, const float* scale, float eps,
+                      void* out, int32_t rows, int32_t hidden, cudaStream_t stream);
+
+/* Residual add rounded to bf16 (TransformerBlock.forward, layers.py:220-232) fused with the next RMSNorm. */
+HB_API int hb_add_rmsnorm(const void* x, const void* y, const float* scale, float eps, void* sum_out,
+                          void* norm_out, int32_t rows, int32_t hidden, cudaStream_t stream);
+
+/* silu(gate) * up from a [rows][2*inter] gate|up GEMM output (FeedForward.forward, layers.py:26-27). */
+HB_API int hb_swiglu(const void* gate_up, void* out, int64_t rows, int64_t inter, cudaStream_t stream);
+
+/* Token-embedding gather (Qwen3Model._forward_packed, src/helios/runtime/qwen3/model.py:97). */
+HB_API int hb_embedding(const int64_t* ids, const void* table, int64_t vocab, void* out, int64_t tokens,
+                        int32_t hidden, cudaStream_t stream);
+
+/*
+ * (d) Page copy: copy page src_pages[i] to dst_pages[i] in each of `tensors` pool
+ * tensors spaced tensor_stride_bytes apart (all layers' K and V). The device form of
+ * the dense snapshot/restore copies KVCache.snapshot_block / restore_blocks
+ * (src/helios/runtime/qwen3/cache.py:109-147) for a paged pool; the paged restore
+ * itself (PagedKVCache.restore_blocks, paged_cache.py:142-163) aliases pages and is
+ * served by hb_tick_pack's arena updates.
+ */
+HB_API int hb_page_copy(void* pool_base, int64_t tensor_stride_bytes, int32_t tensors, int64_t page_bytes,
+                        int64_t num_pages, const int32_t* src_pages, const int32_t* dst_pages, int32_t pairs,
+                        cudaStream_t stream);
+
+/*
+ * (d) Fused sampler. Replaces Decoder._sample (src/helios/runtime/qwen3/decode.py:457-473)
+ * and the batched sampling in Engine._execute_batch (src/helios/runtime/engine.py:470-492):
+ * temperature 0 -> argmax (first index); otherwise temperature softmax with the
+ * reference's top-p keep rule, drawn by inverse CDF over kept tokens in index order
+ * with the caller's uniforms[rows] in [0, 1). logits bf16 [rows][row_stride].
+ */
+HB_API int hb_sample(const void* logits, int64_t row_stride, int32_t rows, int32_t vocab, const float* temperature,
+                     const float* top_p, const float* uniforms, int64_t* out_ids, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HELIOS_B200_H_ */
