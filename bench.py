@@ -1,0 +1,448 @@
+"""Benchmark of the B200 packed mixed-batch tick (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload: Qwen3-4B architecture, random-init bf16 weights;
+one tick = 32 decode rows (contexts uniform in [1024, 4096], their K/V already
+in the paged pool) + one 2048-token prefill chunk at offset 0 = 2080 tokens.
+A step is one tick: tick packing, 36 layers, logits for the 33 trailing rows and
+greedy sampling. Each tick starts a fresh prefill request (its pages are
+recycled afterwards) and advances every decode row by one token.
+
+  value   tokens/s with the step's token ids already on the device, timed with
+          CUDA events over K steps (max over ranks), summed over replicas.
+  e2e     the same ticks through the public API (``Decoder.packed_caches`` with
+          host token lists, fused sampler, device->host read of the sampled ids).
+  roofline  the split-K decode attention kernel at BASELINE config 2 (64 rows,
+          contexts U[512, 8192], 32/8 heads, d=128, 4096-page pool), HBM-bound:
+          algorithmic bytes / CUDA-event time against the measured copy peak.
+  cpu_baseline  the oracle's CPU restatement of the same tick (the reference's
+          algorithm, PyTorch on the host cores), timed on a bounded sample of
+          decoder layers and scaled to 36 (rank 0, N=1 only).
+
+Multi-GPU: one process per GPU (torchrun), independent replicas, no collective
+on the data path; the process group only aligns the ranks and takes max time.
+``--impl reference`` times the CPU oracle of the same tick on rank 0 (other
+ranks exit) and prints the same metric with ``"impl": "reference"``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "packed-tick tokens/s (Qwen3-4B shape, 32 decode rows + 2048-token prefill chunk)"
+UNIT = "tokens/s"
+DECODE_ROWS = 32
+PREFILL = 2048
+CONTEXT = (1024, 4096)
+TOKENS_PER_STEP = DECODE_ROWS + PREFILL
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+DATA = "synthetic: random-init weights, uniform token ids, random K/V standing in for the decode rows' prefill"
+
+
+def peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self) -> dict:
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9 and parts[0] == str(self.gpu_index):
+                rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() in ("active", "1")})
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [v for v in (num(r[1]) for r in rows) if v is not None]
+        mx = [v for v in (num(r[2]) for r in rows) if v is not None]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------------- B200 arm
+def build_replica(device: torch.device, seed: int, steps_total: int):
+    from helios_b200.config import qwen3_4b_config
+    from helios_b200.decode import Decoder
+    from helios_b200.model import Qwen3Model
+    from helios_b200.paged_cache import KVPagePool, PagedKVCache
+
+    cfg = qwen3_4b_config()
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = Qwen3Model(cfg).eval()
+    g = torch.Generator().manual_seed(seed)
+    contexts = torch.randint(CONTEXT[0], CONTEXT[1] + 1, (DECODE_ROWS,), generator=g).tolist()
+    pages = sum(math.ceil((c + steps_total + 1) / 256) for c in contexts) + math.ceil(PREFILL / 256) + 8
+    pool = KVPagePool(cfg, pages, device=device)
+    # The decode rows' context K/V: finite random values in every page (stands in for their prefill).
+    gen = torch.Generator(device=device).manual_seed(seed)
+    for layer in range(cfg.n_layers):
+        pool.storage[layer].normal_(0.0, 0.3, generator=gen)
+    decoder = Decoder(model)
+    decoder.page_pool = pool
+    caches = []
+    for ctx in contexts:
+        cache = PagedKVCache(pool, ctx + steps_total + 1)
+        cache.pages.extend(pool.acquire(math.ceil((ctx - 1) / 256)))
+        cache.length = ctx - 1
+        caches.append(cache)
+    pending = torch.randint(0, cfg.vocab_size, (DECODE_ROWS,), generator=g).tolist()
+    chunk = torch.randint(0, cfg.vocab_size, (PREFILL,), generator=g).tolist()
+    return model, decoder, pool, caches, pending, chunk
+
+
+class TickRunner:
+    """Runs ticks either through the public API (host lists) or with device-resident ids."""
+
+    def __init__(self, device, model, decoder, pool, caches, pending, chunk):
+        from helios_b200.config import Sampling
+        from helios_b200.paged_cache import PackedBatchCache
+
+        self.device, self.model, self.decoder, self.pool = device, model, decoder, pool
+        self.caches, self.pending, self.chunk = caches, pending, chunk
+        self.samplings = [Sampling(temperature=0, top_p=1, max_new_tokens=1)] * (DECODE_ROWS + 1)
+        self.batch = PackedBatchCache(caches)
+        self.chunk_dev = torch.tensor(chunk, dtype=torch.long, device=device)
+        self.pending_dev = torch.tensor(pending, dtype=torch.long, device=device)
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+        self.launches = 0
+
+    def _fresh_prefill(self):
+        from helios_b200.paged_cache import PagedKVCache
+
+        return PagedKVCache(self.pool, PREFILL + 64)
+
+    def device_step(self):
+        """Token ids stay on the device; metadata still goes through tick packing."""
+        from helios_b200.decode import sample_rows
+
+        prefill = self._fresh_prefill()
+        batch = self.batch
+        batch.caches, batch.batch_size = tuple(self.caches) + (prefill,), DECODE_ROWS + 1
+        with torch.inference_mode():
+            ids = torch.cat([self.pending_dev, self.chunk_dev]).unsqueeze(0)
+            batch.prepare_packed([1] * DECODE_ROWS + [PREFILL])
+            logits = self.model(ids, cache=batch)
+            sampled = sample_rows(logits, self.samplings)
+            self.pending_dev = sampled[:DECODE_ROWS]
+        self.launches = self._count_launches(batch)
+        batch.caches = ()
+        prefill.close()
+
+    def api_step(self):
+        """Public API with host buffers: token lists in, sampled ids back on the host."""
+        from helios_b200.decode import sample_rows
+
+        prefill = self._fresh_prefill()
+        chunks = [[t] for t in self.pending] + [self.chunk]
+        with torch.inference_mode():
+            logits = self.decoder.packed_caches(self.caches + [prefill], chunks)
+            ids = sample_rows(logits, self.samplings).cpu().tolist()
+        self.pending = ids[:DECODE_ROWS]
+        batch = self.decoder._packed_batch
+        # token ids + tick descriptor (rows and new arena entries) + per-row sampling settings
+        self.h2d_bytes = 8 * TOKENS_PER_STEP + batch.uploaded_bytes + 4 * 2 * (DECODE_ROWS + 1)
+        self.d2h_bytes = 8 * (DECODE_ROWS + 1)
+        self.launches = self._count_launches(batch)
+        prefill.close()
+
+    def _count_launches(self, batch) -> int:
+        attention = (batch.num_decode_items > 0) + (batch.num_decode_items > 0 and batch.partial_records > 0) \
+            + (batch.num_prefill_items > 0)
+        per_layer = 1 + attention + 2 + 1  # norm/rope/append, attention, add_rmsnorm x2, swiglu
+        return 3 + per_layer * self.model.config.n_layers + 1  # tick pack, embed, first norm, ..., sampler
+
+
+def time_steps(step, steps: int, device: torch.device) -> float:
+    from helios_b200 import replicas
+
+    torch.cuda.synchronize(device)
+    replicas.barrier(device)
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize(device)
+    replicas.barrier(device)
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(end) / 1000.0
+
+
+def decode_attention_roofline(device: torch.device, peak_gbs: float, iters: int = 20) -> dict:
+    """BASELINE config 2 through the C ABI: 64 rows x 1 query, contexts U[512, 8192], 4096 pages."""
+    from helios_b200 import ops
+    from helios_b200.config import Qwen3Config
+    from helios_b200.paged_cache import KVPagePool, PackedBatchCache, PagedKVCache
+
+    cfg = Qwen3Config(n_layers=1, context_length=8192 + 64)
+    g = torch.Generator().manual_seed(1)
+    pool = KVPagePool(cfg, 4096, device=device)
+    gen = torch.Generator(device=device).manual_seed(1)
+    pool.storage.normal_(0.0, 1.0 / math.sqrt(128), generator=gen)
+    contexts = torch.randint(512, 8193, (64,), generator=g).tolist()
+    perm = torch.randperm(4096, generator=g).tolist()
+    pool._free = list(reversed(perm))  # acquire() pops: pages come in permutation order
+    caches = []
+    for ctx in contexts:
+        cache = PagedKVCache(pool, ctx)
+        cache.pages.extend(pool.acquire(math.ceil((ctx - 1) / 256)))
+        cache.length = ctx - 1
+        caches.append(cache)
+    batch = PackedBatchCache(caches)
+    with torch.inference_mode():
+        batch.prepare_packed([1] * 64)
+        q = (torch.randn(64, 32, 128, generator=g) / math.sqrt(128)).to(torch.bfloat16).to(device)
+        out = torch.empty_like(q)
+        for _ in range(3):
+            ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out)
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(iters):
+            ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out)
+        end.record()
+        torch.cuda.synchronize(device)
+    seconds = start.elapsed_time(end) / 1000.0 / iters
+    kv_bytes = sum(contexts) * 8 * 128 * 2 * 2
+    io_bytes = 2 * 64 * 32 * 128 * 2 + 64 * batch.block_table.shape[1] * 4
+    achieved = (kv_bytes + io_bytes) / seconds / 1e9
+    info = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+            "frac": round(achieved / peak_gbs, 4), "traffic": None,
+            "kernel": "decode_attention_kernel (+ decode_combine_kernel), hb_paged_attention on decode rows",
+            "workload": "BASELINE config 2: 64 rows x 1 query, context U[512,8192], 32/8 heads, d=128, 4096 pages",
+            "algorithmic_bytes_per_call": kv_bytes + io_bytes, "us_per_call": round(seconds * 1e6, 2),
+            "split_keys": batch.split_keys, "decode_items": batch.num_decode_items}
+    del pool, batch, caches
+    torch.cuda.empty_cache()
+    return info
+
+
+# ------------------------------------------------------------------------- CPU (oracle) tick
+def cpu_tick_sample(layers: int, seed: int = 0, threads: int | None = None) -> dict:
+    """The oracle's dense CPU restatement of the same tick on ``layers`` decoder layers.
+
+    Returns the seconds per sampled layer and of the rest of the tick (embedding,
+    final norm, logits of the 33 trailing rows), so the 36-layer tick can be scaled.
+    """
+    from oracle.metadata import pack_tick
+    from oracle.model import OracleConfig, OracleModel, build_state_dict
+    from oracle.numerics import rms_norm
+
+    threads = threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = OracleConfig()
+    sd = build_state_dict(cfg, seed, layers=layers)
+    model = OracleModel(cfg, sd, layers=layers)
+    g = torch.Generator().manual_seed(seed)
+    contexts = torch.randint(CONTEXT[0], CONTEXT[1] + 1, (DECODE_ROWS,), generator=g).tolist()
+    lengths = [c - 1 for c in contexts] + [0]
+    counts = [1] * DECODE_ROWS + [PREFILL]
+    tables, at = [], 0
+    for length, count in zip(lengths, counts):
+        n = math.ceil((length + count) / 256)
+        tables.append(list(range(at, at + n)))
+        at += n
+    meta = pack_tick(lengths, counts, tables, [l + c + 8 for l, c in zip(lengths, counts)])
+    kp = [(torch.randn(at, 256, 8, 128, generator=g) * 0.3).to(torch.bfloat16) for _ in range(layers)]
+    vp = [(torch.randn(at, 256, 8, 128, generator=g) * 0.3).to(torch.bfloat16) for _ in range(layers)]
+    ids = torch.randint(0, cfg.vocab_size, (TOKENS_PER_STEP,), generator=g)
+    with torch.inference_mode():
+        t0 = time.perf_counter()
+        x = sd["token_embedding.weight"][ids]
+        t1 = time.perf_counter()
+        for i in range(layers):
+            x = model._block(i, x, kp[i], vp[i], meta)
+        t2 = time.perf_counter()
+        rows = x[torch.as_tensor(meta["logit_indices"])]
+        logits = torch.nn.functional.linear(rms_norm(rows, sd["final_norm.scale"], cfg.rms_norm_eps),
+                                            sd["output.weight"])
+        logits.float().argmax(-1)
+        t3 = time.perf_counter()
+    return {"layer_seconds": (t2 - t1) / layers, "rest_seconds": (t1 - t0) + (t3 - t2), "threads": threads,
+            "layers": layers}
+
+
+def cpu_tokens_per_s(sample: dict, layers_total: int = 36) -> float:
+    return TOKENS_PER_STEP / (sample["layer_seconds"] * layers_total + sample["rest_seconds"])
+
+
+def cpu_baseline() -> dict:
+    first = cpu_tick_sample(1)
+    # Grow the sample toward ~10 s of CPU work, capped at 4 layers.
+    layers = int(max(1, min(4, 10.0 // max(first["layer_seconds"], 1e-3))))
+    sample = cpu_tick_sample(layers) if layers > 1 else first
+    value = cpu_tokens_per_s(sample)
+    return {"value": round(value, 2), "unit": UNIT, "cores": sample["threads"], "kind": "port",
+            "sample": f"{sample['layers']} of 36 decoder layers of the full 2080-token tick (+ embedding and "
+                      f"33 logit rows), scaled to 36 layers; oracle dense restatement, bf16 on CPU"}
+
+
+def workload_config(n: int) -> dict:
+    return {"workload": "BASELINE config 3: full mixed packed tick", "model": "Qwen3-4B architecture, random init",
+            "global_batch": (DECODE_ROWS + 1) * n, "seq_len": PREFILL, "decode_rows": DECODE_ROWS,
+            "decode_context": f"U[{CONTEXT[0]},{CONTEXT[1]}]", "prefill_chunk": PREFILL,
+            "tokens_per_step": TOKENS_PER_STEP, "parallelism": f"replicas x{n} (no data-path collective)",
+            "l2": "inputs larger than L2: each step streams ~8 GB of weights and ~12 GB of KV"}
+
+
+def run_reference(args) -> None:
+    from helios_b200 import replicas
+
+    rank, _, _ = replicas.world()
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_tick_sample(1)
+    times, sample = [], None
+    for _ in range(args.steps):
+        sample = cpu_tick_sample(1)
+        times.append(TOKENS_PER_STEP / cpu_tokens_per_s(sample))
+    value = TOKENS_PER_STEP / statistics.mean(times)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * statistics.mean(times), 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": DATA,
+        "config": workload_config(args.gpus),
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": sample["threads"], "kind": "port",
+                         "sample": "each step: 1 of 36 decoder layers of the full tick (+ embedding and logit rows), "
+                                   "scaled to 36 layers; the oracle's CPU restatement of the reference algorithm"},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args) -> None:
+    from helios_b200 import replicas
+
+    rank, size, local = replicas.world()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    replicas.init("nccl" if size > 1 else "gloo")
+    steps_total = args.warmup * 2 + args.steps * 2 + 4
+    model, decoder, pool, caches, pending, chunk = build_replica(device, seed=1000 + rank, steps_total=steps_total)
+    runner = TickRunner(device, model, decoder, pool, caches, pending, chunk)
+    for _ in range(args.warmup):
+        runner.device_step()
+    torch.cuda.synchronize(device)
+    with ClockSampler(local) as clocks:
+        seconds = time_steps(runner.device_step, args.steps, device)
+    seconds = replicas.max_over_ranks(seconds, device)
+    value = size * TOKENS_PER_STEP * args.steps / seconds
+    # End to end through the public API, host token lists in, sampled ids out.
+    for _ in range(max(1, args.warmup // 2)):
+        runner.api_step()
+    e2e_seconds = replicas.max_over_ranks(time_steps(runner.api_step, args.steps, device), device)
+    e2e_value = size * TOKENS_PER_STEP * args.steps / e2e_seconds
+    h2d, d2h, launches = runner.h2d_bytes, runner.d2h_bytes, runner.launches
+    pk, pk_kind = peaks()
+    flops = 2 * 3.633e9 * TOKENS_PER_STEP  # dense projections + MLP, all layers
+    del runner, model, decoder, pool, caches
+    torch.cuda.empty_cache()
+    roof = decode_attention_roofline(device, pk["hbm_gbs"]) if rank == 0 else None
+    if roof is not None:
+        roof["peak_kind"] = pk_kind
+    cpu = cpu_baseline() if (rank == 0 and size == 1 and not args.no_cpu) else None
+    if rank == 0:
+        step_s = seconds / args.steps
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": size, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(1000 * step_s, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": DATA,
+            "config": workload_config(size),
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(1000 * e2e_seconds / args.steps, 3)},
+            "gpu_launches": args.steps * launches,
+            "clocks": clocks.summary(),
+            "tick_tensor_roofline": {"bound": "tensor", "flops_per_step": flops,
+                                     "achieved_tflops": round(flops / step_s / 1e12, 1),
+                                     "peak_tflops": pk["bf16_tflops_sustained"], "peak_kind": pk_kind,
+                                     "frac": round(flops / step_s / 1e12 / pk["bf16_tflops_sustained"], 4)},
+        }
+        print(json.dumps(line), flush=True)
+    replicas.shutdown()
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("at least 3 warm-up steps")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,130 @@
+"""Kernel (c) parity: paged varlen GQA attention (split-K decode + tcgen05 prefill).
+
+Checked against (1) the reference's own ``PackedBatchCache.attend`` output in
+``tests/golden/attention.npz`` and (2) the fp32 oracle on seeded cases covering
+decode rows with many splits, drafted rows, partial and multi-tile prefill
+rows, chunked-prefill continuation, several GQA group sizes and pools whose
+unused slots hold NaN. Tolerance: the reference's own CUDA test bound,
+``assert_close(rtol=2e-2, atol=2e-2)`` (tests/test_paged_attention.py:310-312).
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from helios_b200 import _native
+from helios_b200.paged_cache import KVPagePool, PackedBatchCache
+from oracle.attention import paged_attention, write_pool
+from tests.golden.inputs import attention_inputs, digest
+from tests.helpers import attn_config, cache_with_pages, queue_pages
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+
+
+def test_matches_reference_packed_attend(golden_dir):
+    g = np.load(golden_dir / "attention.npz")
+    lengths, counts = g["lengths"].tolist(), g["counts"].tolist()
+    key_pool, value_pool, q, k, v = attention_inputs(int(g["num_pages"]), sum(counts))
+    assert digest(key_pool, value_pool, q, k, v) == str(g["input_sha256"])
+    pool = KVPagePool(attn_config(heads=4, kv_heads=1), int(g["num_pages"]), device=DEV)
+    pool.keys[0].copy_(key_pool)
+    pool.values[0].copy_(value_pool)
+    table = g["block_table"].tolist()
+    caches = []
+    for row, (length, count) in enumerate(zip(lengths, counts)):
+        have = math.ceil(length / 256)
+        caches.append(cache_with_pages(pool, length + count + 8, length, table[row][:have]))
+    # Hand out the remaining pages exactly as the reference did.
+    queue_pages(pool, [p for row, length, count in zip(table, lengths, counts)
+                       for p in row[math.ceil(length / 256): math.ceil((length + count) / 256)]])
+    batch = PackedBatchCache(caches)
+    batch.prepare_packed(counts)
+    assert batch.write_slots.tolist() == g["write_slots"].tolist()
+    out = batch.attend(0, q.to(DEV), k.to(DEV), v.to(DEV))
+    expected = torch.from_numpy(g["out"]).view(torch.bfloat16)
+    torch.testing.assert_close(out.cpu().float(), expected.float(), rtol=2e-2, atol=2e-2)
+    assert _native.device_status() == 0
+
+
+def _run(lengths, counts, heads=32, kv_heads=8, seed=0, nan_fill=False):
+    g = torch.Generator().manual_seed(seed)
+    cfg = attn_config(heads=heads, kv_heads=kv_heads)
+    need = sum(math.ceil((l + c) / 256) for l, c in zip(lengths, counts))
+    num_pages = need + 4
+    pool = KVPagePool(cfg, num_pages, device=DEV)
+    fill_k = (torch.randn(pool.keys[0].shape, generator=g) / 3).to(torch.bfloat16)
+    fill_v = torch.randn(pool.values[0].shape, generator=g).to(torch.bfloat16)
+    order = torch.randperm(num_pages, generator=g).tolist()
+    caches, at = [], 0
+    for length, count in zip(lengths, counts):
+        n = math.ceil(length / 256)
+        caches.append(cache_with_pages(pool, length + count + 300, length, order[at: at + n]))
+        at += n
+    if nan_fill:  # every slot beyond a row's committed context holds NaN
+        valid = torch.zeros(num_pages * 256, dtype=torch.bool)
+        for c in caches:
+            for pos in range(c.length):
+                valid[c.pages[pos // 256].index * 256 + pos % 256] = True
+        fill_k.view(-1, kv_heads, 128)[~valid] = float("nan")
+        fill_v.view(-1, kv_heads, 128)[~valid] = float("nan")
+    pool.keys[0].copy_(fill_k)
+    pool.values[0].copy_(fill_v)
+    batch = PackedBatchCache(caches)
+    batch.prepare_packed(counts)
+    T = sum(counts)
+    q = torch.randn(1, heads, T, 128, generator=g).to(torch.bfloat16)
+    k = (torch.randn(1, kv_heads, T, 128, generator=g) / 3).to(torch.bfloat16)
+    v = torch.randn(1, kv_heads, T, 128, generator=g).to(torch.bfloat16)
+    kp_cpu, vp_cpu = pool.keys[0].cpu(), pool.values[0].cpu()
+    out = batch.attend(0, q.to(DEV), k.to(DEV), v.to(DEV))[0].transpose(0, 1).cpu()
+    assert _native.device_status() == 0
+    slots = batch.write_slots.cpu().tolist()
+    write_pool(kp_cpu, slots, k[0].transpose(0, 1))
+    write_pool(vp_cpu, slots, v[0].transpose(0, 1))
+    expected = paged_attention(q[0].transpose(0, 1).contiguous(), kp_cpu, vp_cpu, batch.block_table.cpu().tolist(),
+                               batch.cu_seq_q.cpu().tolist(), batch.seqused_k.cpu().tolist())
+    assert torch.isfinite(out.float()).all()
+    torch.testing.assert_close(out.float(), expected.float(), rtol=2e-2, atol=2e-2)
+    return batch
+
+
+def test_decode_rows_split_k():
+    g = torch.Generator().manual_seed(1)
+    lengths = torch.randint(1, 9000, (48,), generator=g).tolist()
+    batch = _run(lengths, [1] * 48)
+    assert batch.num_decode_items > 48 and batch.num_prefill_items == 0  # rows were split
+
+
+def test_decode_rows_short_contexts_and_page_edges():
+    _run([0, 1, 63, 64, 65, 255, 256, 257, 511, 512], [1] * 10)
+
+
+def test_drafted_rows():
+    _run([10, 300, 700, 1500, 0, 4000], [2, 3, 5, 8, 16, 16])
+
+
+def test_prefill_single_row_2048():
+    batch = _run([0], [2048])
+    assert batch.num_prefill_items == 2048 // 32
+
+
+def test_prefill_partial_tiles_and_continuation():
+    _run([0, 0, 1000, 256, 77], [17, 33, 300, 150, 100])
+
+
+def test_mixed_tick():
+    g = torch.Generator().manual_seed(3)
+    lengths = torch.randint(1024, 4097, (32,), generator=g).tolist() + [0]
+    _run(lengths, [1] * 32 + [512])
+
+
+@pytest.mark.parametrize("heads,kv_heads", [(8, 8), (16, 8), (64, 8)])
+def test_other_group_sizes(heads, kv_heads):
+    _run([100, 1000, 0, 300], [1, 4, 200, 40], heads=heads, kv_heads=kv_heads)
+
+
+def test_stale_nan_slots_never_reach_the_output():
+    _run([5, 300, 0, 600], [1, 2, 70, 1], nan_fill=True)

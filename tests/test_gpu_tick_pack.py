@@ -1,0 +1,115 @@
+"""Kernel (a) parity: device tick packing vs the reference's metadata, bit for bit.
+
+Every case in ``tests/golden/metadata.json`` was produced by the reference's own
+``PagedBatchCache.prepare`` / ``PackedBatchCache.prepare_packed``. The pool is
+arranged to hand out the same pages, then the B200 cache's device-built
+metadata must equal the reference's lists exactly.
+"""
+
+import json
+import math
+
+import pytest
+import torch
+
+from helios_b200 import _native
+from helios_b200.paged_cache import KVPagePool, PackedBatchCache, PagedBatchCache, PagedKVCache
+from oracle.metadata import pack_tick
+from tests.helpers import attn_config, cache_with_pages, queue_pages
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+
+
+def _build(case):
+    pages_after = case["page_tables"]
+    lengths = case["lengths"]
+    before = case.get("pages_before") or [t[: math.ceil(l / 256)] for t, l in zip(pages_after, lengths)]
+    num_pages = max([p for t in pages_after for p in t] + [0]) + 8
+    pool = KVPagePool(attn_config(heads=4, kv_heads=1), num_pages, device=DEV)
+    caches = [cache_with_pages(pool, cap, length, b) for cap, length, b in zip(case["capacities"], lengths, before)]
+    queue_pages(pool, [p for t, b in zip(pages_after, before) for p in t[len(b):]])
+    return pool, caches
+
+
+@pytest.mark.parametrize("name", ["ref_mixed_lengths", "ref_prefill_two", "page_boundary", "config1_tick",
+                                  "config3_tick", "drafted_rows", "chunked_prefill", "restored_prefix"])
+def test_metadata_matches_reference(golden_dir, name):
+    case = {c["name"]: c for c in json.loads((golden_dir / "metadata.json").read_text())}[name]
+    pool, caches = _build(case)
+    if case["mode"] == "uniform":
+        batch = PagedBatchCache(caches)
+        batch.prepare(case["tokens"])
+        keys = ["block_table", "seqused_k", "cu_seq_q", "cu_seq_k", "write_slots"]
+    else:
+        batch = PackedBatchCache(caches)
+        batch.prepare_packed(case["counts"], case["logit_counts"])
+        keys = ["block_table", "cu_seq_q", "cu_seq_k", "seqused_k", "positions", "logit_indices", "write_slots"]
+    assert [[p.index for p in c.pages] for c in caches] == case["page_tables"]
+    for key in keys:
+        got = getattr(batch, key)
+        expected = case["expected"][key]
+        assert got.tolist() == expected, key
+        ref_dtype = torch.long if key in ("positions", "logit_indices", "write_slots") else torch.int32
+        assert got.dtype == ref_dtype, key
+    assert batch.max_q == case["expected"]["max_q"]
+    assert batch.max_k == case["expected"]["max_k"]
+    assert _native.device_status() == 0
+
+
+def test_work_items_cover_every_row_once():
+    """Decode items tile each decode row's keys by split_keys; prefill items tile queries."""
+    g = torch.Generator().manual_seed(11)
+    pool = KVPagePool(attn_config(heads=32, kv_heads=8), 900, device=DEV)
+    lengths = torch.randint(0, 4000, (40,), generator=g).tolist()
+    counts = [1] * 30 + [3, 16, 17, 100, 2048, 5, 1, 1, 64, 300]
+    caches = []
+    for length, count in zip(lengths, counts):
+        n = math.ceil(length / 256)
+        caches.append(cache_with_pages(pool, length + count + 10, length, [pool._free[-1 - i] for i in range(n)]))
+    batch = PackedBatchCache(caches)
+    batch.prepare_packed(counts)
+    dec = batch.decode_items[: 4 * batch.num_decode_items].view(-1, 4).tolist()
+    pre = batch.prefill_items[: 2 * batch.num_prefill_items].view(-1, 2).tolist()
+    group = 4
+    seen = {}
+    for row, split, base, n in dec:
+        assert counts[row] <= 64 // group
+        seen.setdefault(row, []).append((split, base, n))
+    record = 0
+    for row, count in enumerate(counts):
+        end = lengths[row] + count
+        if count <= 64 // group:
+            items = seen[row]
+            n = math.ceil(end / batch.split_keys)
+            assert [s for s, _, _ in items] == list(range(n))
+            assert all(k == n for _, _, k in items)
+            assert [b for _, b, _ in items] == [record + s * count for s in range(n)]
+            record += n * count
+        else:
+            starts = [q for r, q in pre if r == row]
+            assert starts == list(range(0, count, 128 // group))
+    assert record == batch.partial_records
+    meta = pack_tick(lengths, counts, [[p.index for p in c.pages] for c in caches], [c.capacity for c in caches])
+    assert batch.write_slots.tolist() == meta["write_slots"]
+    assert batch.token_row.tolist() == [r for r, c in enumerate(counts) for _ in range(c)]
+    assert _native.device_status() == 0
+
+
+def test_second_tick_uploads_only_new_pages_and_restore_resyncs():
+    pool = KVPagePool(attn_config(heads=4, kv_heads=1), 16, device=DEV)
+    a, b = PagedKVCache(pool, 2000), PagedKVCache(pool, 2000)
+    batch = PackedBatchCache([a, b])
+    batch.prepare_packed([300, 10])
+    batch.advance_packed()
+    assert batch._host_descriptor([1, 1], [1, 1])["updates"].size == 0  # no new pages: nothing to upload
+    batch.prepare_packed([1, 300])
+    assert batch.block_table.tolist() == [[p.index for p in a.pages] + [0] * 6, [p.index for p in b.pages] + [0] * 6]
+    batch.advance_packed()
+    snap = a.snapshot_block(0, 256)
+    c = PagedKVCache(pool, 1000)
+    c.restore_blocks([snap])
+    batch2 = PackedBatchCache([c])
+    batch2.prepare_packed([5])
+    assert batch2.block_table.tolist()[0][:2] == [snap.pages[0].index, c.pages[1].index]
+    assert batch2.write_slots.tolist() == [c.pages[1].index * 256 + i for i in range(5)]
