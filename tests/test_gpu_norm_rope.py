@@ -20,8 +20,7 @@ def _ulps(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return (a.contiguous().view(torch.int16).int() - b.contiguous().view(torch.int16).int()).abs()
 
 
-@pytest.mark.parametrize("dim", [128, 64])
-def test_norm_rope_append_matches_oracle(dim):
+def _run_kernel(dim, rope: bool):
     heads, kv_heads, tokens, pages = 8, 2, 300, 8
     g = torch.Generator().manual_seed(0)
     qkv = torch.randn(tokens, (heads + 2 * kv_heads) * dim, generator=g).to(torch.bfloat16)
@@ -37,25 +36,46 @@ def test_norm_rope_append_matches_oracle(dim):
     k = d_qkv[:, heads * dim: (heads + kv_heads) * dim].view(tokens, kv_heads, dim)
     v = d_qkv[:, (heads + kv_heads) * dim:].view(tokens, kv_heads, dim)
     q_out = torch.empty(tokens, heads, dim, dtype=torch.bfloat16, device=DEV)
-    ops.qk_norm_rope_append(q, k, v, q_scale=q_scale.to(DEV), k_scale=k_scale.to(DEV), eps=1e-6, cos=cos.to(DEV),
-                            sin=sin.to(DEV), positions=positions.to(DEV), write_slots=slots.to(DEV), q_out=q_out,
+    ops.qk_norm_rope_append(q, k, v, q_scale=q_scale.to(DEV), k_scale=k_scale.to(DEV), eps=1e-6,
+                            cos=cos.to(DEV) if rope else None, sin=sin.to(DEV) if rope else None,
+                            positions=positions.to(DEV), write_slots=slots.to(DEV), q_out=q_out,
                             key_pool=key_pool, value_pool=value_pool)
     assert _native.device_status() == 0
     qh = qkv[:, : heads * dim].view(tokens, heads, dim).transpose(0, 1)
     kh = qkv[:, heads * dim: (heads + kv_heads) * dim].view(tokens, kv_heads, dim).transpose(0, 1)
     vh = qkv[:, (heads + kv_heads) * dim:].view(tokens, kv_heads, dim)
-    q_ref = apply_rope(rms_norm(qh, q_scale, 1e-6), cos, sin, positions).transpose(0, 1)
-    k_ref = apply_rope(rms_norm(kh, k_scale, 1e-6), cos, sin, positions).transpose(0, 1)
-    uq = _ulps(q_out.cpu(), q_ref)
-    assert uq.max().item() <= 1 and (uq == 0).float().mean().item() > 0.98
+    q_ref = rms_norm(qh, q_scale, 1e-6)
+    k_ref = rms_norm(kh, k_scale, 1e-6)
+    if rope:
+        q_ref = apply_rope(q_ref, cos, sin, positions)
+        k_ref = apply_rope(k_ref, cos, sin, positions)
     flat_k = key_pool.view(-1, kv_heads, dim).cpu()
     flat_v = value_pool.view(-1, kv_heads, dim).cpu()
-    uk = _ulps(flat_k[slots], k_ref)
-    assert uk.max().item() <= 1 and (uk == 0).float().mean().item() > 0.98
     assert torch.equal(flat_v[slots], vh)
     untouched = torch.ones(pages * 256, dtype=torch.bool)
     untouched[slots] = False
     assert not flat_k[untouched].any() and not flat_v[untouched].any()
+    return (q_out.cpu(), q_ref.transpose(0, 1)), (flat_k[slots], k_ref.transpose(0, 1))
+
+
+@pytest.mark.parametrize("dim", [128, 64])
+def test_norm_matches_oracle_within_one_ulp(dim):
+    """The per-head RMSNorm alone: at most one bf16 ulp (fp32 reduction order, rsqrtf)."""
+    for got, want in _run_kernel(dim, rope=False):
+        ulps = _ulps(got, want)
+        assert ulps.max().item() <= 1 and (ulps == 0).float().mean().item() > 0.98
+
+
+@pytest.mark.parametrize("dim", [128, 64])
+def test_norm_rope_append_matches_oracle(dim):
+    """Norm + RoPE: x*cos + rot(x)*sin near cancellation can turn a one-ulp difference of the
+    normalised input into several ulps of a small result, so the bound is two bf16 ulps of
+    max(|result|, 1) -- the scale of the terms being added -- and almost every element exact."""
+    for got, want in _run_kernel(dim, rope=True):
+        diff = (got.float() - want.float()).abs()
+        bound = 2 ** -6 * want.float().abs().clamp(min=1.0)
+        assert (diff <= bound).all(), diff.max().item()
+        assert (diff == 0).float().mean().item() > 0.97
 
 
 def test_plain_append_is_exact_and_bad_slots_are_flagged():
