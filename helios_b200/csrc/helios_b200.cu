@@ -89,6 +89,14 @@ int ensure_smem(K kernel, int bytes, bool (&done)[64]) {
 
 bool g_dec_smem[4][64], g_pre_smem[4][64], g_tick_smem[64];
 
+// Split-K workspace of hb_paged_attention_static_workspace: one fixed array per GPU,
+// for callers that cannot allocate device memory. In host code the name stands for a
+// host-side shadow, so its device address is looked up once per device.
+constexpr size_t kStaticWorkspaceFloats = HB_STATIC_WORKSPACE_BYTES / sizeof(float);
+static __device__ __align__(256) float g_static_workspace[kStaticWorkspaceFloats];
+std::mutex g_static_ws_mutex;
+void* g_static_ws_ptr[64];
+
 int group_slot(int group) { return group == 1 ? 0 : group == 2 ? 1 : group == 4 ? 2 : 3; }
 
 }  // namespace
@@ -283,6 +291,41 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
 #undef HB_PREFILL
   }
   return HB_OK;
+}
+
+int hb_paged_attention_static_workspace(const void* q, const void* key_pool, const void* value_pool,
+                                       int64_t num_pages, int32_t page_size, const int32_t* block_table,
+                                       int32_t width, const int32_t* cu_seq_q, const int32_t* seqused_k,
+                                       const int32_t* decode_items, int32_t num_decode_items,
+                                       const int32_t* prefill_items, int32_t num_prefill_items,
+                                       int32_t partial_records, int32_t split_keys, int32_t total_tokens,
+                                       int32_t heads, int32_t kv_heads, int32_t head_dim, float scale, void* out,
+                                       cudaStream_t stream) {
+  const size_t need = hb_attention_workspace_bytes(partial_records, heads, head_dim);
+  if (need > HB_STATIC_WORKSPACE_BYTES)
+    return fail(HB_ERR_INVALID,
+                "split-K partials need %zu bytes, more than the built-in %u-byte workspace; "
+                "use hb_paged_attention with a caller workspace or larger split_keys",
+                need, HB_STATIC_WORKSPACE_BYTES);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(HB_ERR_CUDA, "cudaGetDevice failed");
+  void* ws = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_static_ws_mutex);
+    if (g_static_ws_ptr[dev] == nullptr) {
+      // Once per device, with that device current: the array's device address.
+      const cudaError_t e = cudaGetSymbolAddress(&g_static_ws_ptr[dev], g_static_workspace);
+      if (e != cudaSuccess) {
+        g_static_ws_ptr[dev] = nullptr;
+        return fail(HB_ERR_CUDA, "cudaGetSymbolAddress(static workspace): %s", cudaGetErrorString(e));
+      }
+    }
+    ws = g_static_ws_ptr[dev];
+  }
+  return hb_paged_attention(q, key_pool, value_pool, num_pages, page_size, block_table, width, cu_seq_q, seqused_k,
+                            decode_items, num_decode_items, prefill_items, num_prefill_items, partial_records,
+                            split_keys, total_tokens, heads, kv_heads, head_dim, scale, ws, HB_STATIC_WORKSPACE_BYTES,
+                            out, stream);
 }
 
 int hb_rmsnorm(const void* x, int64_t rows_in, const int64_t* row_index, const float* scale, float eps, void* out,

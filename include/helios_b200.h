@@ -120,6 +120,31 @@ HB_API int hb_paged_attention(const void* q, const void* key_pool, const void* v
                               cudaStream_t stream);
 
 /*
+ * Paged attention with a built-in workspace (no counterpart in the reference).
+ * Same arguments and results as hb_paged_attention, minus the workspace: the split-K
+ * partials go to a fixed device array inside this library (HB_STATIC_WORKSPACE_BYTES,
+ * 8 MiB, held on every GPU that loads the library until the process exits). It is for
+ * callers that cannot allocate device memory: hosts that hand the whole GPU to their
+ * own pool up front (so a cudaMalloc would fail or break their accounting) and
+ * latency-bound callers that must not pay cudaMalloc's implicit synchronisation.
+ * It allocates nothing. A call whose partial_records * heads * (head_dim + 1) floats
+ * exceed the array is rejected with HB_ERR_INVALID. The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress) with that device current; make
+ * that first call before any stream capture. Every call shares the one array and leaves
+ * its contents behind (nothing in it needs to start at zero): calls that overlap on the
+ * GPU, from different streams or threads, race on it.
+ */
+#define HB_STATIC_WORKSPACE_BYTES (8u << 20)
+HB_API int hb_paged_attention_static_workspace(const void* q, const void* key_pool, const void* value_pool,
+                                               int64_t num_pages, int32_t page_size, const int32_t* block_table,
+                                               int32_t width, const int32_t* cu_seq_q, const int32_t* seqused_k,
+                                               const int32_t* decode_items, int32_t num_decode_items,
+                                               const int32_t* prefill_items, int32_t num_prefill_items,
+                                               int32_t partial_records, int32_t split_keys, int32_t total_tokens,
+                                               int32_t heads, int32_t kv_heads, int32_t head_dim, float scale,
+                                               void* out, cudaStream_t stream);
+
+/*
  * Hidden-size RMSNorm (RMSNorm.forward, src/helios/runtime/qwen3/layers.py:36-40).
  * With row_index (int64 [rows]) the rows are gathered first, as the logit-row
  * index_select before the final norm (src/helios/runtime/qwen3/model.py:108-110).
