@@ -37,6 +37,7 @@ struct AttentionParams {
   float* ws_out;   // [records, H, D]
   float* ws_lse;   // [records, H]
   int32_t width, num_pages, page_size, heads, kv_heads, split_keys, tokens;
+  int32_t num_prefill;  // prefill items (the kernel walks them from the last, heaviest, first)
   float scale_log2;  // softmax scale * log2(e)
 };
 
@@ -48,9 +49,11 @@ constexpr uint32_t kDecHalfBytes = kDecTileKeys * 128;                 // one [6
 constexpr uint32_t kDecTileBytes = 2 * kDecHalfBytes;                  // K or V tile, D = 128
 constexpr uint32_t kDecStageBytes = 2 * kDecTileBytes;                 // K + V
 constexpr uint32_t kDecSmemBytes = kDecStages * kDecStageBytes + 1024;  // + alignment slack
+constexpr int kMergeStride = 132;  // floats per row of the split merge scratch (padded: no bank conflicts)
+static_assert(kDecConsumerWarps * 16 * kMergeStride * 4 <= kDecStages * kDecStageBytes, "merge scratch fits the ring");
 
 template <int GROUP>
-__global__ void __launch_bounds__(kDecThreads) decode_attention_kernel(AttentionParams p,
+__global__ void __launch_bounds__(kDecThreads, 2) decode_attention_kernel(AttentionParams p,
                                                                       const __grid_constant__ CUtensorMap kmap,
                                                                       const __grid_constant__ CUtensorMap vmap) {
   constexpr int D = 128;
@@ -259,12 +262,12 @@ __global__ void __launch_bounds__(kDecThreads) decode_attention_kernel(Attention
   asm volatile("bar.sync 1, %0;" ::"n"(kDecConsumerWarps * 32) : "memory");
   if (abort_flag) return;
   if (key_split > 1) {
-    float* scratch = reinterpret_cast<float*>(smem) + warp * (16 * 128);
+    float* scratch = reinterpret_cast<float*>(smem) + warp * (16 * kMergeStride);
 #pragma unroll
     for (int n = 0; n < 16; ++n) {
       const int col = n * 8 + 2 * c4;
-      *reinterpret_cast<float2*>(scratch + g4 * 128 + col) = make_float2(acc[n][0], acc[n][1]);
-      *reinterpret_cast<float2*>(scratch + (g4 + 8) * 128 + col) = make_float2(acc[n][2], acc[n][3]);
+      *reinterpret_cast<float2*>(scratch + g4 * kMergeStride + col) = make_float2(acc[n][0], acc[n][1]);
+      *reinterpret_cast<float2*>(scratch + (g4 + 8) * kMergeStride + col) = make_float2(acc[n][2], acc[n][3]);
     }
     if (c4 == 0) {
       merge_ml[warp][g4][0] = m_a; merge_ml[warp][g4][1] = l_a;
@@ -285,12 +288,12 @@ __global__ void __launch_bounds__(kDecThreads) decode_attention_kernel(Attention
       const float wa = exp2f(merge_ml[w][g4][0] - ba), wb = exp2f(merge_ml[w][g4 + 8][0] - bb);
       la += wa * merge_ml[w][g4][1];
       lb += wb * merge_ml[w][g4 + 8][1];
-      const float* sc = reinterpret_cast<const float*>(smem) + w * (16 * 128);
+      const float* sc = reinterpret_cast<const float*>(smem) + w * (16 * kMergeStride);
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
         const int col = n * 8 + 2 * c4;
-        const float2 xa = *reinterpret_cast<const float2*>(sc + g4 * 128 + col);
-        const float2 xb = *reinterpret_cast<const float2*>(sc + (g4 + 8) * 128 + col);
+        const float2 xa = *reinterpret_cast<const float2*>(sc + g4 * kMergeStride + col);
+        const float2 xb = *reinterpret_cast<const float2*>(sc + (g4 + 8) * kMergeStride + col);
         acc[n][0] += wa * xa.x; acc[n][1] += wa * xa.y;
         acc[n][2] += wb * xb.x; acc[n][3] += wb * xb.y;
       }
@@ -327,7 +330,10 @@ __global__ void __launch_bounds__(kDecThreads) decode_attention_kernel(Attention
 }
 
 // Merge the splits of every multi-split decode row: out = sum_s w_s o_s / sum_s w_s
-// with w_s = 2^(lse_s - max lse). One CTA per (split-0 item, KV head); thread = dim.
+// with w_s = 2^(lse_s - max lse). One CTA per (split-0 item, KV head); each warp merges
+// one query row, lane l owning dims 4l..4l+3, so every split's loads are in flight at once.
+constexpr int kCombineMaxSplits = 8;
+
 template <int GROUP>
 __global__ void __launch_bounds__(128) decode_combine_kernel(AttentionParams p) {
   constexpr int D = 128;
@@ -337,20 +343,44 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(AttentionParams p) 
   const int h = blockIdx.y;
   const int q0 = p.cu_seq_q[row];
   const int count = p.cu_seq_q[row + 1] - q0;
-  const int dim = threadIdx.x;
-  for (int j = 0; j < count * GROUP; ++j) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int j = warp; j < count * GROUP; j += 4) {
     const int tq = j / GROUP, head = h * GROUP + j % GROUP;
     float mx = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, p.ws_lse[static_cast<int64_t>(pbase + s * count + tq) * p.heads + head]);
-    const float base = mx == -INFINITY ? 0.f : mx;
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      const int64_t rec = static_cast<int64_t>(pbase + s * count + tq) * p.heads + head;
-      const float w = exp2f(p.ws_lse[rec] - base);
-      den += w;
-      num += w * p.ws_out[rec * D + dim];
+    for (int s0 = 0; s0 < nsplit; s0 += 32) {
+      const int s = s0 + lane;
+      const float v = s < nsplit ? p.ws_lse[static_cast<int64_t>(pbase + s * count + tq) * p.heads + head] : -INFINITY;
+      mx = fmaxf(mx, warp_max(v));
     }
-    p.out[(static_cast<int64_t>(q0 + tq) * p.heads + head) * D + dim] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
+    const float base = mx == -INFINITY ? 0.f : mx;
+    float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+    float den = 0.f;
+    for (int s0 = 0; s0 < nsplit; s0 += kCombineMaxSplits) {
+      const int n = min(kCombineMaxSplits, nsplit - s0);
+      float4 part[kCombineMaxSplits];
+      float w[kCombineMaxSplits];
+#pragma unroll
+      for (int i = 0; i < kCombineMaxSplits; ++i) {
+        if (i < n) {
+          const int64_t rec = static_cast<int64_t>(pbase + (s0 + i) * count + tq) * p.heads + head;
+          w[i] = p.ws_lse[rec];
+          part[i] = reinterpret_cast<const float4*>(p.ws_out + rec * D)[lane];
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kCombineMaxSplits; ++i) {
+        if (i < n) {
+          const float wi = exp2f(w[i] - base);
+          den += wi;
+          num.x += wi * part[i].x; num.y += wi * part[i].y; num.z += wi * part[i].z; num.w += wi * part[i].w;
+        }
+      }
+    }
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    uint2 packed;
+    packed.x = pack_bf16(num.x * inv, num.y * inv);
+    packed.y = pack_bf16(num.z * inv, num.w * inv);
+    reinterpret_cast<uint2*>(p.out + (static_cast<int64_t>(q0 + tq) * p.heads + head) * D)[lane] = packed;
   }
 }
 

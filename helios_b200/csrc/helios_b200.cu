@@ -80,8 +80,11 @@ int ensure_smem(K kernel, int bytes, bool (&done)[64]) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(HB_ERR_CUDA, "cudaGetDevice failed");
   if (!done[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return fail(HB_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    // Take the whole unified L1/shared array as shared memory, so two ~100 KB CTAs fit per SM.
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return fail(HB_ERR_CUDA, "cudaFuncSetAttribute(carveout): %s", cudaGetErrorString(e));
     done[dev] = true;
   }
   return HB_OK;
@@ -98,6 +101,23 @@ std::mutex g_static_ws_mutex;
 void* g_static_ws_ptr[64];
 
 int group_slot(int group) { return group == 1 ? 0 : group == 2 ? 1 : group == 4 ? 2 : 3; }
+
+// RMSNorm launch: warp per row up to hidden 4096, CTA per row beyond.
+int launch_rmsnorm(const hb::RowNormParams& p, cudaStream_t stream, const char* what) {
+  const int nvec = p.hidden / 8;
+  const unsigned warp_blocks = static_cast<unsigned>((p.rows + hb::kNormWarps - 1) / hb::kNormWarps);
+  if (nvec <= 32 * 4)
+    hb::rmsnorm_warp_kernel<4><<<warp_blocks, hb::kNormWarps * 32, 0, stream>>>(p);
+  else if (nvec <= 32 * 8)
+    hb::rmsnorm_warp_kernel<8><<<warp_blocks, hb::kNormWarps * 32, 0, stream>>>(p);
+  else if (nvec <= 32 * 10)  // hidden 2560 (Qwen3-4B)
+    hb::rmsnorm_warp_kernel<10><<<warp_blocks, hb::kNormWarps * 32, 0, stream>>>(p);
+  else if (nvec <= 32 * 16)
+    hb::rmsnorm_warp_kernel<16><<<warp_blocks, hb::kNormWarps * 32, 0, stream>>>(p);
+  else
+    hb::rmsnorm_kernel<<<p.rows, hb::kRowThreads, 0, stream>>>(p);
+  return check_launch(what);
+}
 
 }  // namespace
 
@@ -177,12 +197,12 @@ int hb_qk_norm_rope_append(const void* q, int64_t q_token_stride, int64_t q_head
                        positions, write_slots, static_cast<__nv_bfloat16*>(q_out),
                        static_cast<__nv_bfloat16*>(key_pool), static_cast<__nv_bfloat16*>(value_pool), pool_slots,
                        tokens, heads, kv_heads};
-  const int64_t items = static_cast<int64_t>(tokens) * (heads + 2 * kv_heads);
-  const unsigned blocks = static_cast<unsigned>((items + 7) / 8);
+  const int64_t groups = (heads + 2 * kv_heads + hb::kRopeRowsPerWarp - 1) / hb::kRopeRowsPerWarp;
+  const unsigned blocks = static_cast<unsigned>((static_cast<int64_t>(tokens) * groups + hb::kRopeWarps - 1) / hb::kRopeWarps);
   if (head_dim == 128)
-    hb::norm_rope_append_kernel<128><<<blocks, 256, 0, stream>>>(p);
+    hb::norm_rope_append_kernel<128><<<blocks, hb::kRopeWarps * 32, 0, stream>>>(p);
   else
-    hb::norm_rope_append_kernel<64><<<blocks, 256, 0, stream>>>(p);
+    hb::norm_rope_append_kernel<64><<<blocks, hb::kRopeWarps * 32, 0, stream>>>(p);
   return check_launch("norm_rope_append_kernel");
 }
 
@@ -235,6 +255,7 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
   p.kv_heads = kv_heads;
   p.split_keys = split_keys;
   p.tokens = total_tokens;
+  p.num_prefill = num_prefill_items;
   p.scale_log2 = scale * 1.4426950408889634f;
 
   const uint64_t pool_tokens = static_cast<uint64_t>(num_pages) * page_size;
@@ -339,8 +360,7 @@ int hb_rmsnorm(const void* x, int64_t rows_in, const int64_t* row_index, const f
     return fail(HB_ERR_INVALID, "rmsnorm pointers must be 16-byte aligned");
   hb::RowNormParams p{static_cast<const __nv_bfloat16*>(x), nullptr, row_index, scale, nullptr,
                       static_cast<__nv_bfloat16*>(out), rows, hidden, row_index ? rows_in : rows, eps};
-  hb::rmsnorm_kernel<<<rows, hb::kRowThreads, 0, stream>>>(p);
-  return check_launch("rmsnorm_kernel");
+  return launch_rmsnorm(p, stream, "rmsnorm_kernel");
 }
 
 int hb_add_rmsnorm(const void* x, const void* y, const float* scale, float eps, void* sum_out, void* norm_out,
@@ -356,8 +376,7 @@ int hb_add_rmsnorm(const void* x, const void* y, const float* scale, float eps, 
   hb::RowNormParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y), nullptr, scale,
                       static_cast<__nv_bfloat16*>(sum_out), static_cast<__nv_bfloat16*>(norm_out), rows, hidden,
                       rows, eps};
-  hb::rmsnorm_kernel<<<rows, hb::kRowThreads, 0, stream>>>(p);
-  return check_launch("add_rmsnorm_kernel");
+  return launch_rmsnorm(p, stream, "add_rmsnorm_kernel");
 }
 
 int hb_swiglu(const void* gate_up, void* out, int64_t rows, int64_t inter, cudaStream_t stream) {
@@ -368,7 +387,8 @@ int hb_swiglu(const void* gate_up, void* out, int64_t rows, int64_t inter, cudaS
     return fail(HB_ERR_INVALID, "swiglu pointers must be non-null and 16-byte aligned");
   hb::SwigluParams p{static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(out), rows, inter};
   const int64_t vecs = rows * inter / 8;
-  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((vecs + 255) / 256, 148 * 16));
+  const int64_t per_block = 256 * hb::kSwigluUnroll;
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((vecs + per_block - 1) / per_block, 148 * 8));
   hb::swiglu_kernel<<<blocks, 256, 0, stream>>>(p);
   return check_launch("swiglu_kernel");
 }

@@ -110,28 +110,112 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_kernel(RowNormParams p) {
   }
 }
 
+// Warp-per-row variant for hidden <= 32 * 8 * MAXV: every lane issues all of its
+// 16-byte loads before reducing, and the reduction stays inside the warp.
+constexpr int kNormWarps = 8;
+
+template <int MAXV>
+__global__ void __launch_bounds__(kNormWarps * 32) rmsnorm_warp_kernel(RowNormParams p) {
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kNormWarps + (threadIdx.x >> 5);
+  if (r >= p.rows) return;
+  int64_t src_row = r;
+  if (p.row_index != nullptr) {
+    src_row = p.row_index[r];
+    if (src_row < 0 || src_row >= p.rows_in) {
+      if (lane == 0) raise_status(kStatusBadRow);
+      src_row = 0;
+    }
+  }
+  const int nvec = p.hidden / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(p.x + src_row * p.hidden);
+  const uint4* yr = p.y ? reinterpret_cast<const uint4*>(p.y + static_cast<int64_t>(r) * p.hidden) : nullptr;
+  uint4 raw[MAXV], raw_y[MAXV];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nvec) {
+      raw[i] = xr[vi];
+      if (yr) raw_y[i] = yr[vi];
+    }
+  }
+  float v[MAXV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nvec) {
+      unpack8(raw[i], v[i]);
+      if (yr) {
+        float w[8];
+        unpack8(raw_y[i], w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[i][e] = __bfloat162float(__float2bfloat16_rn(__fadd_rn(v[i][e], w[e])));
+        reinterpret_cast<uint4*>(p.sum_out + static_cast<int64_t>(r) * p.hidden)[vi] = pack8(v[i]);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = __fmaf_rn(v[i][e], v[i][e], ss);
+    }
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(p.hidden)), p.eps));
+  const float4* sc = reinterpret_cast<const float4*>(p.scale);
+  uint4* out = reinterpret_cast<uint4*>(p.norm_out + static_cast<int64_t>(r) * p.hidden);
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nvec) {
+      const float4 s0 = sc[2 * vi], s1 = sc[2 * vi + 1];
+      const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = __fmul_rn(__fmul_rn(v[i][e], inv), s[e]);
+      out[vi] = pack8(o);
+    }
+  }
+}
+
 struct SwigluParams {
   const __nv_bfloat16* gate_up;  // [rows, 2 * inter]: gate then up
   __nv_bfloat16* out;            // [rows, inter]
   int64_t rows, inter;
 };
 
+constexpr int kSwigluUnroll = 4;  // independent 16-byte vectors per thread, loads issued together
+
 __global__ void __launch_bounds__(256) swiglu_kernel(SwigluParams p) {
   const int64_t nvec_row = p.inter / 8;
   const int64_t total = p.rows * nvec_row;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t r = i / nvec_row, c = i % nvec_row;
-    const uint4* row = reinterpret_cast<const uint4*>(p.gate_up + r * 2 * p.inter);
-    float g[8], u[8], o[8];
-    unpack8(row[c], g);
-    unpack8(row[nvec_row + c], u);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t first = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; first < total;
+       first += stride * kSwigluUnroll) {
+    uint4 g_raw[kSwigluUnroll], u_raw[kSwigluUnroll];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float sl = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(g[e], __fadd_rn(1.f, expf(-g[e])))));
-      o[e] = __fmul_rn(sl, u[e]);
+    for (int k = 0; k < kSwigluUnroll; ++k) {
+      const int64_t i = first + k * stride;
+      if (i < total) {
+        const int64_t r = i / nvec_row, c = i % nvec_row;
+        const uint4* row = reinterpret_cast<const uint4*>(p.gate_up + r * 2 * p.inter);
+        g_raw[k] = row[c];
+        u_raw[k] = row[nvec_row + c];
+      }
     }
-    reinterpret_cast<uint4*>(p.out + r * p.inter)[c] = pack8(o);
+#pragma unroll
+    for (int k = 0; k < kSwigluUnroll; ++k) {
+      const int64_t i = first + k * stride;
+      if (i < total) {
+        const int64_t r = i / nvec_row, c = i % nvec_row;
+        float g[8], u[8], o[8];
+        unpack8(g_raw[k], g);
+        unpack8(u_raw[k], u);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float sl = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(g[e], __fadd_rn(1.f, expf(-g[e])))));
+          o[e] = __fmul_rn(sl, u[e]);
+        }
+        reinterpret_cast<uint4*>(p.out + r * p.inter)[c] = pack8(o);
+      }
+    }
   }
 }
 

@@ -64,9 +64,11 @@ __device__ __forceinline__ void store_row(__nv_bfloat16* dst, int lane, const fl
   }
 }
 
+// Per-head RMSNorm then RoPE on one row held as d/32 values per lane. `scale`,
+// `cs` and `sn` are this lane's slices (null scale: no norm; null cs: no rotation).
 template <int D>
 __device__ __forceinline__ void norm_rope_row(float (&x)[D / 32], int lane, const float* scale, float eps,
-                                              const float* cos_row, const float* sin_row) {
+                                              const float* cs, const float* sn) {
   constexpr int E = D / 32;
   if (scale != nullptr) {
     float ss = 0.f;
@@ -75,74 +77,91 @@ __device__ __forceinline__ void norm_rope_row(float (&x)[D / 32], int lane, cons
     ss = warp_sum(ss);
     const float inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), eps));
 #pragma unroll
-    for (int e = 0; e < E; ++e)
-      x[e] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[e], inv), scale[lane * E + e])));
+    for (int e = 0; e < E; ++e) x[e] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[e], inv), scale[e])));
   }
-  if (cos_row != nullptr) {
+  if (cs != nullptr) {
     float partner[E];
 #pragma unroll
     for (int e = 0; e < E; ++e) partner[e] = __shfl_xor_sync(0xffffffffu, x[e], 16);
     const bool first_half = lane < 16;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      const int i = lane * E + e;
       const float rot = first_half ? -partner[e] : partner[e];
-      x[e] = __bfloat162float(
-          __float2bfloat16_rn(__fadd_rn(__fmul_rn(x[e], cos_row[i]), __fmul_rn(rot, sin_row[i]))));
+      x[e] = __bfloat162float(__float2bfloat16_rn(__fadd_rn(__fmul_rn(x[e], cs[e]), __fmul_rn(rot, sn[e]))));
     }
   }
 }
 
+// One warp per (token, group of kRopeRowsPerWarp head rows): the warp issues its
+// position, slot, row, scale and (after the position) cos/sin loads together, so a
+// warp pays about two dependent memory latencies; thousands of warps run at once.
+constexpr int kRopeWarps = 8;        // warps per CTA
+constexpr int kRopeRowsPerWarp = 4;  // head rows per warp
+
 template <int D>
-__global__ void __launch_bounds__(256) norm_rope_append_kernel(NormRopeParams p) {
+__global__ void __launch_bounds__(kRopeWarps * 32) norm_rope_append_kernel(NormRopeParams p) {
+  constexpr int E = D / 32;
   const int lane = threadIdx.x & 31;
-  const int rows_per_token = p.heads + 2 * p.kv_heads;
-  const int64_t item = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (item >= static_cast<int64_t>(p.tokens) * rows_per_token) return;
-  const int t = static_cast<int>(item / rows_per_token);
-  const int hr = static_cast<int>(item % rows_per_token);
-  float x[D / 32];
-  if (hr < p.heads) {  // query head
-    if (p.q_out == nullptr) return;
-    load_row<D>(p.q + t * p.q_tok + hr * p.q_head, lane, x);
-    const float *c = nullptr, *s = nullptr;
-    if (p.cos != nullptr) {
-      const int64_t pos = p.positions[t];
-      if (pos < 0 || pos >= p.rope_rows) {
-        if (lane == 0) raise_status(kStatusBadPosition);
-        return;
-      }
-      c = p.cos + pos * D;
-      s = p.sin + pos * D;
-    }
-    norm_rope_row<D>(x, lane, p.q_scale, p.eps, c, s);
-    store_row<D>(p.q_out + (static_cast<int64_t>(t) * p.heads + hr) * D, lane, x);
-    return;
-  }
+  const int rows = p.heads + 2 * p.kv_heads;
+  const int groups = (rows + kRopeRowsPerWarp - 1) / kRopeRowsPerWarp;
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kRopeWarps + (threadIdx.x >> 5);
+  if (gw >= static_cast<int64_t>(p.tokens) * groups) return;
+  const int t = static_cast<int>(gw / groups);
+  const int row0 = static_cast<int>(gw % groups) * kRopeRowsPerWarp;
   const int64_t slot = p.write_slots[t];
-  if (slot < 0 || slot >= p.pool_slots) {
-    if (lane == 0) raise_status(kStatusBadSlot);
-    return;
-  }
-  if (hr < p.heads + p.kv_heads) {  // key head: norm + rope, then into the pool
-    const int h = hr - p.heads;
-    load_row<D>(p.k + t * p.k_tok + h * p.k_head, lane, x);
-    const float *c = nullptr, *s = nullptr;
-    if (p.cos != nullptr) {
-      const int64_t pos = p.positions[t];
-      if (pos < 0 || pos >= p.rope_rows) {
-        if (lane == 0) raise_status(kStatusBadPosition);
-        return;
-      }
-      c = p.cos + pos * D;
-      s = p.sin + pos * D;
+  float x[kRopeRowsPerWarp][E];
+#pragma unroll
+  for (int i = 0; i < kRopeRowsPerWarp; ++i) {  // row loads first
+    const int hr = row0 + i;
+    if (hr >= rows) break;
+    if (hr < p.heads) {
+      if (p.q_out != nullptr) load_row<D>(p.q + t * p.q_tok + hr * p.q_head, lane, x[i]);
+    } else if (hr < p.heads + p.kv_heads) {
+      load_row<D>(p.k + t * p.k_tok + (hr - p.heads) * p.k_head, lane, x[i]);
+    } else {
+      load_row<D>(p.v + t * p.v_tok + (hr - p.heads - p.kv_heads) * p.v_head, lane, x[i]);
     }
-    norm_rope_row<D>(x, lane, p.k_scale, p.eps, c, s);
-    store_row<D>(p.key_pool + (slot * p.kv_heads + h) * D, lane, x);
-  } else {  // value head: copied as is
-    const int h = hr - p.heads - p.kv_heads;
-    load_row<D>(p.v + t * p.v_tok + h * p.v_head, lane, x);
-    store_row<D>(p.value_pool + (slot * p.kv_heads + h) * D, lane, x);
+  }
+  float qsc[E], ksc[E], cs[E], sn[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    qsc[e] = p.q_scale != nullptr ? p.q_scale[lane * E + e] : 1.f;
+    ksc[e] = p.k_scale != nullptr ? p.k_scale[lane * E + e] : 1.f;
+  }
+  bool rope_ok = p.cos == nullptr;
+  if (p.cos != nullptr) {
+    const int64_t pos = p.positions[t];
+    if (pos >= 0 && pos < p.rope_rows) {
+      rope_ok = true;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        cs[e] = p.cos[pos * D + lane * E + e];
+        sn[e] = p.sin[pos * D + lane * E + e];
+      }
+    } else if (lane == 0) {
+      raise_status(kStatusBadPosition);
+    }
+  }
+  const bool slot_ok = slot >= 0 && slot < p.pool_slots;
+  if (!slot_ok && lane == 0 && row0 + kRopeRowsPerWarp > p.heads) raise_status(kStatusBadSlot);
+  const float* rope_c = p.cos != nullptr ? cs : nullptr;
+  const float* rope_s = p.cos != nullptr ? sn : nullptr;
+#pragma unroll
+  for (int i = 0; i < kRopeRowsPerWarp; ++i) {
+    const int hr = row0 + i;
+    if (hr >= rows) break;
+    if (hr < p.heads) {  // query head
+      if (p.q_out == nullptr || !rope_ok) continue;
+      norm_rope_row<D>(x[i], lane, p.q_scale != nullptr ? qsc : nullptr, p.eps, rope_c, rope_s);
+      store_row<D>(p.q_out + (static_cast<int64_t>(t) * p.heads + hr) * D, lane, x[i]);
+    } else if (hr < p.heads + p.kv_heads) {  // key head: norm + rope, then into the pool
+      if (!slot_ok || !rope_ok) continue;
+      norm_rope_row<D>(x[i], lane, p.k_scale != nullptr ? ksc : nullptr, p.eps, rope_c, rope_s);
+      store_row<D>(p.key_pool + (slot * p.kv_heads + (hr - p.heads)) * D, lane, x[i]);
+    } else {  // value head: copied as is
+      if (!slot_ok) continue;
+      store_row<D>(p.value_pool + (slot * p.kv_heads + (hr - p.heads - p.kv_heads)) * D, lane, x[i]);
+    }
   }
 }
 

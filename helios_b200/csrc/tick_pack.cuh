@@ -15,7 +15,8 @@
 //     and the owning row;
 //   * logit_indices: the trailing logit_count_r tokens of each row;
 //   * the attention work lists: split-K items for decode-class rows
-//     (count <= decode_max_tokens) and query tiles for prefill-class rows.
+//     (count <= decode_max_tokens) and, for prefill-class rows, pairs of query tiles
+//     (i, m-1-i) of a row with m tiles, so every pair sees the same causal work.
 // Every output write is bounded by the capacity the host sized it for; an entry
 // that would fall outside is skipped and reported in the status word.
 #pragma once
@@ -39,13 +40,16 @@ struct TickPackParams {
   int32_t* token_row;      // [T]
   int64_t* logit_indices;  // [logit_capacity]
   int32_t* decode_items;   // [decode_capacity][4] row, split, partial_base, n_splits
-  int32_t* prefill_items;  // [prefill_capacity][2] row, query start
+  int32_t* prefill_items;  // [prefill_capacity][3] row, first tile start, second tile start or -1
   int32_t total_tokens, logit_capacity, decode_capacity, prefill_capacity;
 };
 
 constexpr int kTickThreads = 1024;
 
 __device__ __forceinline__ int row_splits(int end, int split_keys) { return (end + split_keys - 1) / split_keys; }
+__device__ __forceinline__ int row_prefill_items(int count, int tile_tokens) {
+  return ((count + tile_tokens - 1) / tile_tokens + 1) / 2;  // tiles, paired
+}
 
 __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams p) {
   extern __shared__ int32_t sm[];
@@ -85,7 +89,7 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
       s[3] += sp;
       s[4] += sp * cnt;
     } else {
-      s[5] += (cnt + p.prefill_tile_tokens - 1) / p.prefill_tile_tokens;
+      s[5] += row_prefill_items(cnt, p.prefill_tile_tokens);
     }
   }
   int32_t incl[6];
@@ -134,7 +138,7 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
       base[3] += sp;
       base[4] += sp * cnt;
     } else {
-      base[5] += (cnt + p.prefill_tile_tokens - 1) / p.prefill_tile_tokens;
+      base[5] += row_prefill_items(cnt, p.prefill_tile_tokens);
     }
   }
   if (tid == kTickThreads - 1) {
@@ -172,10 +176,13 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
       }
     } else {
       const int tiles = (cnt + p.prefill_tile_tokens - 1) / p.prefill_tile_tokens;
-      for (int t = 0; t < tiles; ++t) {
-        if (f_off[r] + t >= p.prefill_capacity) { raise_status(kStatusBadRow); break; }
-        p.prefill_items[2 * (f_off[r] + t)] = r;
-        p.prefill_items[2 * (f_off[r] + t) + 1] = t * p.prefill_tile_tokens;
+      for (int i = 0; i < (tiles + 1) / 2; ++i) {
+        if (f_off[r] + i >= p.prefill_capacity) { raise_status(kStatusBadRow); break; }
+        int32_t* it = p.prefill_items + 3 * (f_off[r] + i);
+        const int partner = tiles - 1 - i;
+        it[0] = r;
+        it[1] = i * p.prefill_tile_tokens;
+        it[2] = partner > i ? partner * p.prefill_tile_tokens : -1;
       }
     }
   }

@@ -51,7 +51,7 @@ def tick_pack(rows_dev: torch.Tensor, num_rows: int, updates_dev: torch.Tensor |
         out["seqused_k"].data_ptr(), out["positions"].data_ptr(), out["write_slots"].data_ptr(),
         out["token_row"].data_ptr(), out["logit_store"].data_ptr(), out["logit_store"].numel(),
         out["decode_items"].data_ptr(), out["decode_items"].numel() // 4,
-        out["prefill_items"].data_ptr(), out["prefill_items"].numel() // 2, _stream(rows_dev.device))
+        out["prefill_items"].data_ptr(), out["prefill_items"].numel() // 3, _stream(rows_dev.device))
     _native.check(rc, "hb_tick_pack")
 
 

@@ -38,7 +38,7 @@ from helios_b200 import ops
 from helios_b200.config import Qwen3Config
 
 DECODE_QUERY_ROWS = 64      # query rows (tokens x group heads) one decode CTA holds
-PREFILL_TILE_ROWS = 128     # query rows of one tcgen05 prefill tile
+PREFILL_TILE_ROWS = 128     # query rows of one tcgen05 prefill tile (a CTA takes a pair of tiles)
 NUM_SMS_B200 = 148
 
 
@@ -375,7 +375,7 @@ class PagedBatchCache:
             "rows": rows, "updates": np.asarray(updates, dtype=np.int32), "decode_max": decode_max,
             "tile_tokens": tile_tokens, "split_keys": split, "num_decode_items": int(splits.sum()),
             "partial_records": int((splits * cnts[is_decode]).sum()),
-            "num_prefill_items": int(((cnts[~is_decode] + tile_tokens - 1) // tile_tokens).sum()),
+            "num_prefill_items": int(((((cnts[~is_decode] + tile_tokens - 1) // tile_tokens) + 1) // 2).sum()),
             "total_tokens": int(cnts.sum()), "num_logits": int(rows[:, 3].sum()),
             "width": max(_pages_for(cache.capacity, page_size) for cache in self.caches),
         }
@@ -420,7 +420,7 @@ class PagedBatchCache:
         """Views of two reusable device buffers sized for this tick."""
         n_dec = max(1, self.num_decode_items)
         n_pre = max(1, self.num_prefill_items)
-        sizes32 = [rows * width, rows + 1, rows + 1, rows, max(tokens, 1), 4 * n_dec, 2 * n_pre]
+        sizes32 = [rows * width, rows + 1, rows + 1, rows, max(tokens, 1), 4 * n_dec, 3 * n_pre]
         sizes64 = [max(tokens, 1), max(tokens, 1), max(logits, 1)]
         dev = self.pool.device
         if self._i32 is None or self._i32.numel() < sum(sizes32):

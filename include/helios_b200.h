@@ -68,8 +68,9 @@ HB_API int hb_device_status(uint32_t* status, int clear);
  * write_slots int64 [total_tokens], token_row int32 [total_tokens], logit_indices
  * int64 [logit_capacity], decode_items int32 [decode_capacity][4] (row, split,
  * partial base, splits) for rows with count <= decode_max_tokens, split every
- * split_keys keys, prefill_items int32 [prefill_capacity][2] (row, query start)
- * every prefill_tile_tokens queries. Entries past a capacity are not written.
+ * split_keys keys, prefill_items int32 [prefill_capacity][3] (row, start of query
+ * tile i, start of tile m-1-i or -1) pairing the m tiles of prefill_tile_tokens
+ * queries of a row. Entries past a capacity are not written.
  */
 HB_API int hb_tick_pack(const int32_t* rows, int32_t num_rows, const int32_t* updates, int32_t num_updates,
                         int32_t* arena, int32_t arena_slots, int32_t arena_width, int32_t page_size, int32_t width,

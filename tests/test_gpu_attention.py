@@ -108,7 +108,7 @@ def test_drafted_rows():
 
 def test_prefill_single_row_2048():
     batch = _run([0], [2048])
-    assert batch.num_prefill_items == 2048 // 32
+    assert batch.num_prefill_items == 2048 // 32 // 2  # 64 tiles of 32 tokens, paired
 
 
 def test_prefill_partial_tiles_and_continuation():

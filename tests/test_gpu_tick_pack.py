@@ -58,7 +58,7 @@ def test_metadata_matches_reference(golden_dir, name):
 
 
 def test_work_items_cover_every_row_once():
-    """Decode items tile each decode row's keys by split_keys; prefill items tile queries."""
+    """Decode items tile each decode row's keys by split_keys; prefill items pair query tiles."""
     g = torch.Generator().manual_seed(11)
     pool = KVPagePool(attn_config(heads=32, kv_heads=8), 900, device=DEV)
     lengths = torch.randint(0, 4000, (40,), generator=g).tolist()
@@ -70,7 +70,7 @@ def test_work_items_cover_every_row_once():
     batch = PackedBatchCache(caches)
     batch.prepare_packed(counts)
     dec = batch.decode_items[: 4 * batch.num_decode_items].view(-1, 4).tolist()
-    pre = batch.prefill_items[: 2 * batch.num_prefill_items].view(-1, 2).tolist()
+    pre = batch.prefill_items[: 3 * batch.num_prefill_items].view(-1, 3).tolist()
     group = 4
     seen = {}
     for row, split, base, n in dec:
@@ -87,8 +87,11 @@ def test_work_items_cover_every_row_once():
             assert [b for _, b, _ in items] == [record + s * count for s in range(n)]
             record += n * count
         else:
-            starts = [q for r, q in pre if r == row]
-            assert starts == list(range(0, count, 128 // group))
+            # Query tiles of 128 // group tokens, tile i paired with tile m-1-i (equal causal work).
+            tile = 128 // group
+            m = math.ceil(count / tile)
+            pairs = [(a, b) for r, a, b in pre if r == row]
+            assert pairs == [(i * tile, (m - 1 - i) * tile if m - 1 - i > i else -1) for i in range((m + 1) // 2)]
     assert record == batch.partial_records
     meta = pack_tick(lengths, counts, [[p.index for p in c.pages] for c in caches], [c.capacity for c in caches])
     assert batch.write_slots.tolist() == meta["write_slots"]

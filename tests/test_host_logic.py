@@ -146,7 +146,7 @@ def test_descriptor_partitions_attention_work():
     assert split % 256 == 0 and split >= 256
     assert d["num_decode_items"] == math.ceil(1001 / split) + math.ceil(3016 / split)
     assert d["partial_records"] == math.ceil(1001 / split) * 1 + math.ceil(3016 / split) * 16
-    assert d["num_prefill_items"] == 2048 // 32
+    assert d["num_prefill_items"] == 2048 // 32 // 2  # tiles of 32 tokens, paired
     assert d["total_tokens"] == 2065 and d["num_logits"] == 3 and d["width"] == 16
 
 
