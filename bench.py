@@ -29,6 +29,7 @@ ranks exit) and prints the same metric with ``"impl": "reference"``.
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import math
 import os
@@ -63,9 +64,10 @@ def peaks() -> tuple[dict, str]:
 
 # ------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during a region."""
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms; the summary keeps the
+    samples taken between mark_start() and mark_end() (the timed region)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -73,16 +75,28 @@ class ClockSampler:
         self.gpu_index = gpu_index
         self.proc = None
         self.file = None
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return self
+        deadline = time.time() + 5.0  # wait for the first sample so the region is covered
+        while time.time() < deadline and self.proc.poll() is None and not Path(self.file.name).read_text():
+            time.sleep(0.02)
         return self
+
+    def mark_start(self) -> None:
+        self.t0 = time.time()
+
+    def mark_end(self) -> None:
+        self.t1 = time.time()
+        time.sleep(0.06)  # let the sample after the region land
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -100,13 +114,23 @@ class ClockSampler:
         rows = []
         for line in Path(self.file.name).read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9 and parts[0] == str(self.gpu_index):
+            if len(parts) >= 10 and parts[1] == str(self.gpu_index):
                 rows.append(parts)
         os.unlink(self.file.name)
+
+        def stamp(text):
+            try:
+                return datetime.datetime.strptime(text, "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except ValueError:
+                return None
+
+        if self.t0 is not None and self.t1 is not None:
+            inside = [r for r in rows if (t := stamp(r[0])) is not None and self.t0 - 0.05 <= t <= self.t1 + 0.05]
+            rows = inside or rows
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() in ("active", "1")})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].lower() in ("active", "1")})
 
         def num(x):
             try:
@@ -114,8 +138,8 @@ class ClockSampler:
             except ValueError:
                 return None
 
-        sm = [v for v in (num(r[1]) for r in rows) if v is not None]
-        mx = [v for v in (num(r[2]) for r in rows) if v is not None]
+        sm = [v for v in (num(r[2]) for r in rows) if v is not None]
+        mx = [v for v in (num(r[3]) for r in rows) if v is not None]
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(rows)}
 
@@ -387,11 +411,13 @@ def run_b200(args) -> None:
     steps_total = args.warmup * 2 + args.steps * 2 + 4
     model, decoder, pool, caches, pending, chunk = build_replica(device, seed=1000 + rank, steps_total=steps_total)
     runner = TickRunner(device, model, decoder, pool, caches, pending, chunk)
-    for _ in range(args.warmup):
-        runner.device_step()
-    torch.cuda.synchronize(device)
     with ClockSampler(local) as clocks:
+        for _ in range(args.warmup):
+            runner.device_step()
+        torch.cuda.synchronize(device)
+        clocks.mark_start()
         seconds = time_steps(runner.device_step, args.steps, device)
+        clocks.mark_end()
     seconds = replicas.max_over_ranks(seconds, device)
     value = size * TOKENS_PER_STEP * args.steps / seconds
     # End to end through the public API, host token lists in, sampled ids out.

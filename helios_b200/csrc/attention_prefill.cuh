@@ -6,27 +6,29 @@
 //
 // One CTA owns two query tiles of 128 rows each; a tile is (128 / GROUP)
 // consecutive tokens of one sequence x the GROUP query heads that share KV head h.
-// The two tiles are tile i and tile m-1-i of a row with m tiles, so every CTA sees
-// the same causal work, and every K/V tile is read once for both. Roles (320 threads):
+// The two tiles are adjacent (2i and 2i+1 of a row), so they need the same key
+// tiles (up to two more for the second when a tile exceeds 32 tokens), both stay
+// busy for the CTA's whole life, and every K/V tile is read once for both. Roles (320 threads):
 //   warp 0     TMA producer: both Q tiles once, then 64-key K and V tiles (two
 //              128B-swizzled [64][64] boxes each) from the pages the block table
 //              names, into separate 3-stage K and V rings;
 //   warp 1     owns the TMEM allocation (512 columns: S0, S1 at 0/64, O0, O1 at
-//              128/256); lane 0 issues tcgen05.mma: S_t = Q_t K^T (M=128, N=64,
-//              K=128) and O_t += P_t V (M=128, N=128, K=64), committing to mbarriers;
+//              128/256, P buffers at 384..511); lane 0 issues tcgen05.mma:
+//              S_t = Q_t K^T (M=128, N=64, K=128, both operands in shared memory)
+//              and O_t += P_t V (M=128, N=128, K=64, P read from TMEM),
+//              committing to mbarriers;
 //   warps 2-5  softmax for tile 0, warps 6-9 softmax for tile 1: thread i owns
 //              accumulator row i (TMEM lane i), so row max and sum need no
-//              shuffles; P is written as bf16 into the tile's own P buffer in the
-//              canonical 128B-swizzled K-major layout the next MMA reads; P is
-//              double-buffered, so the softmax of key tile j waits only for the
-//              P V of key tile j-2 (or j-1 when O must be rescaled).
+//              shuffles; P is stored as bf16 pairs into one of the tile's two TMEM
+//              P buffers (tcgen05.st), so the softmax of key tile j waits only for
+//              the P V of key tile j-2 (or j-1 when O must be rescaled).
 // The MMA thread polls both tiles' barriers and issues whichever S or P V is
 // ready, so the tensor pipe works on one tile while the softmax warps work on
 // the other. O is rescaled (in TMEM) only when a row's
 // running max grows by more than 2^8; exponents stay relative to the max in use,
 // so P <= 2^8 and the final O / l is unchanged. Keys at or beyond seqused_k get
 // their V rows zeroed so stale pool memory cannot reach the accumulator. The
-// longest query tiles (the last of a row) are scheduled first.
+// longest pairs (the last of a row) of every KV head are launched first.
 #pragma once
 
 #include "hb_common.cuh"
@@ -42,10 +44,10 @@ constexpr int kPreVStages = 3;
 constexpr int kPreThreads = 320;
 constexpr uint32_t kPreQBytes = kPreRows * 128 * 2;   // [128][128] bf16 as two [128][64] boxes
 constexpr uint32_t kPreKVBytes = kPreKeys * 128 * 2;  // [64][128] as two [64][64] boxes
-constexpr uint32_t kPrePBytes = kPreRows * kPreKeys * 2;
-constexpr uint32_t kPreSmemBytes =
-    kPreTiles * kPreQBytes + (kPreKStages + kPreVStages) * kPreKVBytes + 2 * kPreTiles * kPrePBytes + 1024;
+constexpr uint32_t kPreSmemBytes = kPreTiles * kPreQBytes + (kPreKStages + kPreVStages) * kPreKVBytes + 1024;
+// TMEM columns: S_t at 64 t, O_t at 128 + 128 t, P_{t,b} (bf16 pairs) at 384 + 32 (2 t + b).
 constexpr uint32_t kPreTmemCols = 512;
+constexpr uint32_t kPreTmemP = 384;
 constexpr float kRescaleThreshold = 8.f;  // log2 units: rescale O when the max grows by more than 2^8
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -66,7 +68,6 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
   uint8_t* q_s = smem;                                   // tile t at t * kPreQBytes
   uint8_t* k_s = q_s + kPreTiles * kPreQBytes;           // stage s at s * kPreKVBytes
   uint8_t* v_s = k_s + kPreKStages * kPreKVBytes;
-  uint8_t* p_s = v_s + kPreVStages * kPreKVBytes;        // tile t, buffer b at (2 t + b) * kPrePBytes
 
   __shared__ uint64_t q_full, k_full[kPreKStages], k_empty[kPreKStages], v_full[kPreVStages], v_empty[kPreVStages];
   __shared__ uint64_t s_full[kPreTiles], s_free[kPreTiles], p_full[kPreTiles][2], o_done[kPreTiles][2], drain_bar;
@@ -74,8 +75,9 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h = blockIdx.y;
-  const int32_t* item = p.prefill_items + 3 * (p.num_prefill - 1 - static_cast<int>(blockIdx.x));
+  // KV head fastest, items last to first: the longest query tiles of every head launch first.
+  const int h = blockIdx.x;
+  const int32_t* item = p.prefill_items + 3 * (p.num_prefill - 1 - static_cast<int>(blockIdx.y));
   const int row = item[0];
   const int q0 = p.cu_seq_q[row];
   const int count = p.cu_seq_q[row + 1] - q0;
@@ -177,11 +179,11 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
         mma_commit(&s_full[t]);
       };
       auto issue_pv = [&](int t, int j) {
-        const uint32_t p_addr = smem_u32(p_s + (2 * t + (j & 1)) * kPrePBytes);
+        const uint32_t p_tmem = tmem + kPreTmemP + (2 * t + (j & 1)) * (kPreKeys / 2);
         const uint32_t v_addr = smem_u32(v_s + (j % kPreVStages) * kPreKVBytes);
 #pragma unroll
-        for (int kk = 0; kk < kPreKeys / 16; ++kk)
-          mma_ss(tmem + 128 + t * 128, smem_desc(p_addr + kk * 32, 16, 1024, kSwizzle128B),
+        for (int kk = 0; kk < kPreKeys / 16; ++kk)  // 16 keys = 8 columns of P per step
+          mma_ts(tmem + 128 + t * 128, p_tmem + kk * 8,
                  smem_desc(v_addr + kk * 2048, kPreKVBytes / 2, 1024, kSwizzle128B), idesc_pv, (j > 0 || kk > 0));
         mma_commit(&o_done[t][j & 1]);
       };
@@ -264,18 +266,24 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
       tc_fence_before();
       mbar_arrive(&s_free[t]);
       const int key0 = j * kPreKeys;
-      float mx = -INFINITY;
-      if (key0 + kPreKeys - 1 <= qpos && key0 + kPreKeys <= end) {  // whole tile visible to this row
-#pragma unroll
-        for (int c = 0; c < 64; ++c) mx = fmaxf(mx, s[c]);
-      } else {
+      if (!(key0 + kPreKeys - 1 <= qpos && key0 + kPreKeys <= end)) {  // edge tile: mask
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
           const int key = key0 + c;
           s[c] = (key <= qpos && key < end) ? s[c] : -INFINITY;
-          mx = fmaxf(mx, s[c]);
         }
       }
+      // Max and sum as 8 independent chains (fmaxf is exact in any order; the sum
+      // order only moves rounding of the normaliser).
+      float m8[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) m8[c] = fmaxf(s[c], s[c + 8]);
+#pragma unroll
+      for (int c = 16; c < 64; c += 8) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m8[e] = fmaxf(m8[e], s[c + e]);
+      }
+      float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       mx *= p.scale_log2;
       // Lazy rescale: keep the max in use unless this tile's max exceeds it by 2^8.
       const bool grow = mx > m_used + kRescaleThreshold;
@@ -283,13 +291,13 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
       const float alpha = grow ? fast_exp2(m_used - m_new) : 1.f;  // m_used = -inf gives 0
       m_used = m_new;
       const float neg = m_new == -INFINITY ? 0.f : -m_new;
-      float sum = 0.f;
+      float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
         s[c] = fast_exp2(fmaf(s[c], p.scale_log2, neg));
-        sum += s[c];
+        s8[c & 7] += s[c];
       }
-      l = l * alpha + sum;
+      l = l * alpha + (((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])));
       // P buffer j & 1 was last read by the P V of key tile j - 2.
       if (j >= 2 && !mbar_wait(&o_done[t][j & 1], ((j >> 1) - 1) & 1, &abort_flag)) { ok = false; break; }
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
@@ -309,15 +317,12 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
           tmem_wait_st();
         }
       }
-      uint8_t* ps = p_s + (2 * t + (j & 1)) * kPrePBytes;
+      {  // P as bf16 pairs into this tile's TMEM P buffer j & 1 (row r = lane r)
+        uint32_t pw[32];
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        uint4 v;
-        v.x = pack_bf16(s[c8 * 8 + 0], s[c8 * 8 + 1]);
-        v.y = pack_bf16(s[c8 * 8 + 2], s[c8 * 8 + 3]);
-        v.z = pack_bf16(s[c8 * 8 + 4], s[c8 * 8 + 5]);
-        v.w = pack_bf16(s[c8 * 8 + 6], s[c8 * 8 + 7]);
-        *reinterpret_cast<uint4*>(ps + sw128(r, c8)) = v;
+        for (int c = 0; c < 32; ++c) pw[c] = pack_bf16(s[2 * c], s[2 * c + 1]);
+        tmem_st32u(tmem + kPreTmemP + (2 * t + (j & 1)) * (kPreKeys / 2) + lane_base, pw);
+        tmem_wait_st();
       }
       // Stale pool rows past the sequence end are zeroed in this V stage by the first
       // query tile that uses key tile j: the MMA warp issues tile 0's P V before tile 1's,
@@ -332,8 +337,8 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
           *reinterpret_cast<uint4*>(vrow + sw128(r, c8)) = make_uint4(0, 0, 0, 0);
           *reinterpret_cast<uint4*>(vrow + kPreKVBytes / 2 + sw128(r, c8)) = make_uint4(0, 0, 0, 0);
         }
+        fence_proxy_async_smem();  // the zeros are read by the tensor core (async proxy)
       }
-      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[t][j & 1]);
     }

@@ -188,21 +188,26 @@ int hb_qk_norm_rope_append(const void* q, int64_t q_token_stride, int64_t q_head
   if (q_out != nullptr && q == nullptr) return fail(HB_ERR_INVALID, "q_out without q");
   if ((cos == nullptr) != (sin == nullptr) || (cos != nullptr && positions == nullptr))
     return fail(HB_ERR_INVALID, "rope tables need cos, sin and positions");
-  const uintptr_t vec = head_dim == 128 ? 8 : 4;
-  if (!aligned(k, vec) || !aligned(v, vec) || (q && !aligned(q, vec)) || (q_out && !aligned(q_out, vec)))
-    return fail(HB_ERR_INVALID, "q/k/v rows must be %d-byte aligned", static_cast<int>(vec));
+  // Every row is moved as 16-byte vectors: bases 16-byte aligned, strides multiples of 8 elements.
+  const bool strides_ok = k_token_stride % 8 == 0 && k_head_stride % 8 == 0 && v_token_stride % 8 == 0 &&
+                          v_head_stride % 8 == 0 && (q == nullptr || (q_token_stride % 8 == 0 && q_head_stride % 8 == 0));
+  if (!strides_ok || !aligned(k, 16) || !aligned(v, 16) || (q && !aligned(q, 16)) || (q_out && !aligned(q_out, 16)) ||
+      !aligned(key_pool, 16) || !aligned(value_pool, 16))
+    return fail(HB_ERR_INVALID, "q/k/v rows and pools must be 16-byte aligned (strides multiples of 8 elements)");
+  if ((q_scale && !aligned(q_scale, 16)) || (k_scale && !aligned(k_scale, 16)) || (cos && !aligned(cos, 16)) ||
+      (sin && !aligned(sin, 16)))
+    return fail(HB_ERR_INVALID, "norm scales and rope tables must be 16-byte aligned");
   hb::NormRopeParams p{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
                        static_cast<const __nv_bfloat16*>(v), q_token_stride, q_head_stride, k_token_stride,
                        k_head_stride, v_token_stride, v_head_stride, q_scale, k_scale, eps, cos, sin, rope_rows,
                        positions, write_slots, static_cast<__nv_bfloat16*>(q_out),
                        static_cast<__nv_bfloat16*>(key_pool), static_cast<__nv_bfloat16*>(value_pool), pool_slots,
                        tokens, heads, kv_heads};
-  const int64_t groups = (heads + 2 * kv_heads + hb::kRopeRowsPerWarp - 1) / hb::kRopeRowsPerWarp;
-  const unsigned blocks = static_cast<unsigned>((static_cast<int64_t>(tokens) * groups + hb::kRopeWarps - 1) / hb::kRopeWarps);
+  const unsigned blocks = static_cast<unsigned>(tokens);  // one CTA per token
   if (head_dim == 128)
-    hb::norm_rope_append_kernel<128><<<blocks, hb::kRopeWarps * 32, 0, stream>>>(p);
+    hb::norm_rope_append_kernel<128><<<blocks, hb::kRopeThreads, 0, stream>>>(p);
   else
-    hb::norm_rope_append_kernel<64><<<blocks, hb::kRopeWarps * 32, 0, stream>>>(p);
+    hb::norm_rope_append_kernel<64><<<blocks, hb::kRopeThreads, 0, stream>>>(p);
   return check_launch("norm_rope_append_kernel");
 }
 
@@ -268,9 +273,31 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
                          hb::kDecTileKeys))
     return rc;
   const int gs = group_slot(group);
+  if (num_decode_items > 0 && decode_items == nullptr) return fail(HB_ERR_INVALID, "null decode items");
+  if (num_prefill_items > 0 && prefill_items == nullptr) return fail(HB_ERR_INVALID, "null prefill items");
 
+  if (num_prefill_items > 0) {
+    if (num_prefill_items > 65535) return fail(HB_ERR_UNSUPPORTED, "more than 65535 prefill tile pairs in one call");
+    CUtensorMap qmap;
+    const dim3 grid(kv_heads, num_prefill_items);
+#define HB_PREFILL(G)                                                                                           \
+  do {                                                                                                          \
+    if (int rc = encode_3d(&qmap, q, head_dim, heads, total_tokens, head_dim * 2,                               \
+                           static_cast<uint64_t>(heads) * head_dim * 2, 64, G, hb::kPreRows / G))               \
+      return rc;                                                                                                \
+    if (int rc = ensure_smem(hb::prefill_attention_kernel<G>, hb::kPreSmemBytes, g_pre_smem[gs])) return rc;     \
+    hb::prefill_attention_kernel<G><<<grid, hb::kPreThreads, hb::kPreSmemBytes, stream>>>(p, qmap, kmap, vmap);  \
+    if (int rc = check_launch("prefill_attention_kernel")) return rc;                                           \
+  } while (0)
+    switch (group) {
+      case 1: HB_PREFILL(1); break;
+      case 2: HB_PREFILL(2); break;
+      case 4: HB_PREFILL(4); break;
+      default: HB_PREFILL(8); break;
+    }
+#undef HB_PREFILL
+  }
   if (num_decode_items > 0) {
-    if (decode_items == nullptr) return fail(HB_ERR_INVALID, "null decode items");
     const dim3 grid(num_decode_items, kv_heads);
 #define HB_DECODE(G)                                                                                          \
   do {                                                                                                        \
@@ -289,27 +316,6 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
       default: HB_DECODE(8); break;
     }
 #undef HB_DECODE
-  }
-  if (num_prefill_items > 0) {
-    if (prefill_items == nullptr) return fail(HB_ERR_INVALID, "null prefill items");
-    CUtensorMap qmap;
-    const dim3 grid(num_prefill_items, kv_heads);
-#define HB_PREFILL(G)                                                                                           \
-  do {                                                                                                          \
-    if (int rc = encode_3d(&qmap, q, head_dim, heads, total_tokens, head_dim * 2,                               \
-                           static_cast<uint64_t>(heads) * head_dim * 2, 64, G, hb::kPreRows / G))               \
-      return rc;                                                                                                \
-    if (int rc = ensure_smem(hb::prefill_attention_kernel<G>, hb::kPreSmemBytes, g_pre_smem[gs])) return rc;     \
-    hb::prefill_attention_kernel<G><<<grid, hb::kPreThreads, hb::kPreSmemBytes, stream>>>(p, qmap, kmap, vmap);  \
-    if (int rc = check_launch("prefill_attention_kernel")) return rc;                                           \
-  } while (0)
-    switch (group) {
-      case 1: HB_PREFILL(1); break;
-      case 2: HB_PREFILL(2); break;
-      case 4: HB_PREFILL(4); break;
-      default: HB_PREFILL(8); break;
-    }
-#undef HB_PREFILL
   }
   return HB_OK;
 }
@@ -386,10 +392,10 @@ int hb_swiglu(const void* gate_up, void* out, int64_t rows, int64_t inter, cudaS
   if (gate_up == nullptr || out == nullptr || !aligned(gate_up, 16) || !aligned(out, 16))
     return fail(HB_ERR_INVALID, "swiglu pointers must be non-null and 16-byte aligned");
   hb::SwigluParams p{static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(out), rows, inter};
-  const int64_t vecs = rows * inter / 8;
-  const int64_t per_block = 256 * hb::kSwigluUnroll;
-  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((vecs + per_block - 1) / per_block, 148 * 8));
-  hb::swiglu_kernel<<<blocks, 256, 0, stream>>>(p);
+  const int64_t per_block = hb::kSwigluThreads * hb::kSwigluVecs;
+  const dim3 grid(static_cast<unsigned>((inter / 8 + per_block - 1) / per_block),
+                  static_cast<unsigned>(std::min<int64_t>(rows, 65535)));
+  hb::swiglu_kernel<<<grid, hb::kSwigluThreads, 0, stream>>>(p);
   return check_launch("swiglu_kernel");
 }
 

@@ -20,23 +20,6 @@ namespace hb {
 constexpr int kRowThreads = 256;
 constexpr int kRowVecs = 8;  // up to 8 x 8 bf16 per thread: hidden <= 16384
 
-__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[2 * i] = __low2float(h[i]);
-    f[2 * i + 1] = __high2float(h[i]);
-  }
-}
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  uint4 v;
-  v.x = pack_bf16(f[0], f[1]);
-  v.y = pack_bf16(f[2], f[3]);
-  v.z = pack_bf16(f[4], f[5]);
-  v.w = pack_bf16(f[6], f[7]);
-  return v;
-}
-
 __device__ __forceinline__ float block_sum(float v, float* red) {
   v = warp_sum(v);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -181,30 +164,30 @@ struct SwigluParams {
   int64_t rows, inter;
 };
 
-constexpr int kSwigluUnroll = 4;  // independent 16-byte vectors per thread, loads issued together
+// Grid: (column blocks, rows); each thread owns two 16-byte vectors of one row, so
+// there is no per-element index division and four loads are in flight per thread.
+constexpr int kSwigluThreads = 128;
+constexpr int kSwigluVecs = 2;
 
-__global__ void __launch_bounds__(256) swiglu_kernel(SwigluParams p) {
+__global__ void __launch_bounds__(kSwigluThreads) swiglu_kernel(SwigluParams p) {
   const int64_t nvec_row = p.inter / 8;
-  const int64_t total = p.rows * nvec_row;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t first = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; first < total;
-       first += stride * kSwigluUnroll) {
-    uint4 g_raw[kSwigluUnroll], u_raw[kSwigluUnroll];
+  for (int64_t r = blockIdx.y; r < p.rows; r += gridDim.y) {
+    const uint4* row = reinterpret_cast<const uint4*>(p.gate_up + r * 2 * p.inter);
+    uint4* out = reinterpret_cast<uint4*>(p.out + r * p.inter);
+    const int64_t c0 = static_cast<int64_t>(blockIdx.x) * kSwigluThreads * kSwigluVecs + threadIdx.x;
+    uint4 g_raw[kSwigluVecs], u_raw[kSwigluVecs];
 #pragma unroll
-    for (int k = 0; k < kSwigluUnroll; ++k) {
-      const int64_t i = first + k * stride;
-      if (i < total) {
-        const int64_t r = i / nvec_row, c = i % nvec_row;
-        const uint4* row = reinterpret_cast<const uint4*>(p.gate_up + r * 2 * p.inter);
+    for (int k = 0; k < kSwigluVecs; ++k) {
+      const int64_t c = c0 + k * kSwigluThreads;
+      if (c < nvec_row) {
         g_raw[k] = row[c];
         u_raw[k] = row[nvec_row + c];
       }
     }
 #pragma unroll
-    for (int k = 0; k < kSwigluUnroll; ++k) {
-      const int64_t i = first + k * stride;
-      if (i < total) {
-        const int64_t r = i / nvec_row, c = i % nvec_row;
+    for (int k = 0; k < kSwigluVecs; ++k) {
+      const int64_t c = c0 + k * kSwigluThreads;
+      if (c < nvec_row) {
         float g[8], u[8], o[8];
         unpack8(g_raw[k], g);
         unpack8(u_raw[k], u);
@@ -213,7 +196,7 @@ __global__ void __launch_bounds__(256) swiglu_kernel(SwigluParams p) {
           const float sl = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(g[e], __fadd_rn(1.f, expf(-g[e])))));
           o[e] = __fmul_rn(sl, u[e]);
         }
-        reinterpret_cast<uint4*>(p.out + r * p.inter)[c] = pack8(o);
+        out[c] = pack8(o);
       }
     }
   }

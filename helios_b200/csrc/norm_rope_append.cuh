@@ -4,8 +4,7 @@
 //   q_norm/k_norm  (RMSNorm.forward, src/helios/runtime/qwen3/layers.py:36-40),
 //   apply_rope     (layers.py:54-72, with position_ids),
 //   _write         (two index_copy_ into the pool, paged_cache.py:335-345)
-// with one launch. One warp handles one (token, head) row of d elements; each
-// lane holds d/32 contiguous elements, so the RoPE partner (i +- d/2) is lane ^ 16.
+// with one launch (one CTA per token; layout below).
 //
 // Rounding points follow the reference exactly: the norm is fp32
 // (x * rsqrt(mean(x^2) + eps)) * scale_fp32, rounded to bf16; RoPE then computes
@@ -37,130 +36,100 @@ struct NormRopeParams {
   int32_t tokens, heads, kv_heads;
 };
 
-template <int D>
-__device__ __forceinline__ void load_row(const __nv_bfloat16* src, int lane, float (&x)[D / 32]) {
-  constexpr int E = D / 32;
-  if constexpr (E == 4) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(src + lane * E);
-    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-    x[0] = __low2float(a); x[1] = __high2float(a); x[2] = __low2float(b); x[3] = __high2float(b);
-  } else {
-    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(src + lane * E);
-    x[0] = __low2float(a); x[1] = __high2float(a);
-  }
-}
+// One CTA per token. A head row of D bf16 values is spread over D/8 lanes, 16 B per
+// lane (a 256 B row for D = 128 is one fully used 16-lane segment), so a warp moves
+// 2 (D = 128) or 4 (D = 64) rows per instruction. Every thread first issues the loads
+// of all its rows of the token (q, k and v rows are one contiguous span of the fused
+// projection output), together with the token's position and write slot; the cos/sin
+// slice of its lane and the norm scales follow. The RoPE partner of element i
+// (i +- D/2) sits D/16 lanes away, and the row's sum of squares is a shuffle
+// reduction within the row's lanes.
+constexpr int kRopeThreads = 256;
+constexpr int kRopeMaxRows = 3;  // rows one thread keeps in flight per pass (48 rows = one pass)
 
 template <int D>
-__device__ __forceinline__ void store_row(__nv_bfloat16* dst, int lane, const float (&x)[D / 32]) {
-  constexpr int E = D / 32;
-  if constexpr (E == 4) {
-    uint2 raw;
-    raw.x = pack_bf16(x[0], x[1]);
-    raw.y = pack_bf16(x[2], x[3]);
-    *reinterpret_cast<uint2*>(dst + lane * E) = raw;
-  } else {
-    *reinterpret_cast<uint32_t*>(dst + lane * E) = pack_bf16(x[0], x[1]);
-  }
-}
-
-// Per-head RMSNorm then RoPE on one row held as d/32 values per lane. `scale`,
-// `cs` and `sn` are this lane's slices (null scale: no norm; null cs: no rotation).
-template <int D>
-__device__ __forceinline__ void norm_rope_row(float (&x)[D / 32], int lane, const float* scale, float eps,
-                                              const float* cs, const float* sn) {
-  constexpr int E = D / 32;
-  if (scale != nullptr) {
-    float ss = 0.f;
-#pragma unroll
-    for (int e = 0; e < E; ++e) ss = __fmaf_rn(x[e], x[e], ss);
-    ss = warp_sum(ss);
-    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), eps));
-#pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[e], inv), scale[e])));
-  }
-  if (cs != nullptr) {
-    float partner[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e) partner[e] = __shfl_xor_sync(0xffffffffu, x[e], 16);
-    const bool first_half = lane < 16;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const float rot = first_half ? -partner[e] : partner[e];
-      x[e] = __bfloat162float(__float2bfloat16_rn(__fadd_rn(__fmul_rn(x[e], cs[e]), __fmul_rn(rot, sn[e]))));
-    }
-  }
-}
-
-// One warp per (token, group of kRopeRowsPerWarp head rows): the warp issues its
-// position, slot, row, scale and (after the position) cos/sin loads together, so a
-// warp pays about two dependent memory latencies; thousands of warps run at once.
-constexpr int kRopeWarps = 8;        // warps per CTA
-constexpr int kRopeRowsPerWarp = 4;  // head rows per warp
-
-template <int D>
-__global__ void __launch_bounds__(kRopeWarps * 32) norm_rope_append_kernel(NormRopeParams p) {
-  constexpr int E = D / 32;
-  const int lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(kRopeThreads, 4) norm_rope_append_kernel(NormRopeParams p) {
+  constexpr int kLanes = D / 8;                    // lanes per head row
+  constexpr int kSlots = kRopeThreads / kLanes;    // head rows handled side by side
+  const int t = blockIdx.x;
+  const int j = threadIdx.x % kLanes;              // this lane's 8 elements: 8j .. 8j+7
+  const int slot0 = threadIdx.x / kLanes;
+  // Rows of one warp may take different branches (q / k / v), so shuffles name only
+  // the lanes of this thread's row; each row's lanes always take the same path.
+  const unsigned row_mask = static_cast<unsigned>((1ull << kLanes) - 1) << ((threadIdx.x & 31) & ~(kLanes - 1));
   const int rows = p.heads + 2 * p.kv_heads;
-  const int groups = (rows + kRopeRowsPerWarp - 1) / kRopeRowsPerWarp;
-  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kRopeWarps + (threadIdx.x >> 5);
-  if (gw >= static_cast<int64_t>(p.tokens) * groups) return;
-  const int t = static_cast<int>(gw / groups);
-  const int row0 = static_cast<int>(gw % groups) * kRopeRowsPerWarp;
   const int64_t slot = p.write_slots[t];
-  float x[kRopeRowsPerWarp][E];
-#pragma unroll
-  for (int i = 0; i < kRopeRowsPerWarp; ++i) {  // row loads first
-    const int hr = row0 + i;
-    if (hr >= rows) break;
-    if (hr < p.heads) {
-      if (p.q_out != nullptr) load_row<D>(p.q + t * p.q_tok + hr * p.q_head, lane, x[i]);
-    } else if (hr < p.heads + p.kv_heads) {
-      load_row<D>(p.k + t * p.k_tok + (hr - p.heads) * p.k_head, lane, x[i]);
-    } else {
-      load_row<D>(p.v + t * p.v_tok + (hr - p.heads - p.kv_heads) * p.v_head, lane, x[i]);
-    }
-  }
-  float qsc[E], ksc[E], cs[E], sn[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    qsc[e] = p.q_scale != nullptr ? p.q_scale[lane * E + e] : 1.f;
-    ksc[e] = p.k_scale != nullptr ? p.k_scale[lane * E + e] : 1.f;
-  }
-  bool rope_ok = p.cos == nullptr;
-  if (p.cos != nullptr) {
-    const int64_t pos = p.positions[t];
-    if (pos >= 0 && pos < p.rope_rows) {
-      rope_ok = true;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        cs[e] = p.cos[pos * D + lane * E + e];
-        sn[e] = p.sin[pos * D + lane * E + e];
-      }
-    } else if (lane == 0) {
-      raise_status(kStatusBadPosition);
-    }
-  }
+  const int64_t pos = p.cos != nullptr ? p.positions[t] : 0;
   const bool slot_ok = slot >= 0 && slot < p.pool_slots;
-  if (!slot_ok && lane == 0 && row0 + kRopeRowsPerWarp > p.heads) raise_status(kStatusBadSlot);
-  const float* rope_c = p.cos != nullptr ? cs : nullptr;
-  const float* rope_s = p.cos != nullptr ? sn : nullptr;
+  const bool pos_ok = p.cos == nullptr || (pos >= 0 && pos < p.rope_rows);
+  if (threadIdx.x == 0) {
+    if (!slot_ok) raise_status(kStatusBadSlot);
+    if (!pos_ok) raise_status(kStatusBadPosition);
+  }
+  for (int base = slot0; base < rows; base += kSlots * kRopeMaxRows) {
+    uint4 raw[kRopeMaxRows];
 #pragma unroll
-  for (int i = 0; i < kRopeRowsPerWarp; ++i) {
-    const int hr = row0 + i;
-    if (hr >= rows) break;
-    if (hr < p.heads) {  // query head
-      if (p.q_out == nullptr || !rope_ok) continue;
-      norm_rope_row<D>(x[i], lane, p.q_scale != nullptr ? qsc : nullptr, p.eps, rope_c, rope_s);
-      store_row<D>(p.q_out + (static_cast<int64_t>(t) * p.heads + hr) * D, lane, x[i]);
-    } else if (hr < p.heads + p.kv_heads) {  // key head: norm + rope, then into the pool
-      if (!slot_ok || !rope_ok) continue;
-      norm_rope_row<D>(x[i], lane, p.k_scale != nullptr ? ksc : nullptr, p.eps, rope_c, rope_s);
-      store_row<D>(p.key_pool + (slot * p.kv_heads + (hr - p.heads)) * D, lane, x[i]);
-    } else {  // value head: copied as is
-      if (!slot_ok) continue;
-      store_row<D>(p.value_pool + (slot * p.kv_heads + (hr - p.heads - p.kv_heads)) * D, lane, x[i]);
+    for (int i = 0; i < kRopeMaxRows; ++i) {  // all row loads first
+      const int hr = base + i * kSlots;
+      raw[i] = make_uint4(0, 0, 0, 0);
+      if (hr >= rows) continue;
+      const __nv_bfloat16* src;
+      if (hr < p.heads) {
+        if (p.q_out == nullptr) continue;
+        src = p.q + t * p.q_tok + hr * p.q_head;
+      } else if (hr < p.heads + p.kv_heads) {
+        src = p.k + t * p.k_tok + (hr - p.heads) * p.k_head;
+      } else {
+        src = p.v + t * p.v_tok + (hr - p.heads - p.kv_heads) * p.v_head;
+      }
+      raw[i] = *reinterpret_cast<const uint4*>(src + 8 * j);
+    }
+    float cs[8], sn[8];
+    if (p.cos != nullptr && pos_ok) {
+      const float4* c4 = reinterpret_cast<const float4*>(p.cos + pos * D + 8 * j);
+      const float4* s4 = reinterpret_cast<const float4*>(p.sin + pos * D + 8 * j);
+      const float4 c0 = c4[0], c1 = c4[1], s0 = s4[0], s1 = s4[1];
+      cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w; cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+      sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+    }
+#pragma unroll
+    for (int i = 0; i < kRopeMaxRows; ++i) {
+      const int hr = base + i * kSlots;
+      if (hr >= rows) break;  // uniform over the row's lanes
+      if (hr >= p.heads + p.kv_heads) {  // value head: copied as is
+        if (slot_ok) *reinterpret_cast<uint4*>(p.value_pool + (slot * p.kv_heads + (hr - p.heads - p.kv_heads)) * D + 8 * j) = raw[i];
+        continue;
+      }
+      const bool is_q = hr < p.heads;
+      if (is_q ? (p.q_out == nullptr || !pos_ok) : (!slot_ok || !pos_ok)) continue;
+      float x[8];
+      unpack8(raw[i], x);
+      const float* scale = is_q ? p.q_scale : p.k_scale;
+      if (scale != nullptr) {  // RMSNorm over the row (fp32), rounded to bf16
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = __fmaf_rn(x[e], x[e], ss);
+#pragma unroll
+        for (int o = kLanes / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(row_mask, ss, o);
+        const float inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), p.eps));
+        const float4 g0 = reinterpret_cast<const float4*>(scale + 8 * j)[0];
+        const float4 g1 = reinterpret_cast<const float4*>(scale + 8 * j)[1];
+        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[e], inv), g[e])));
+      }
+      if (p.cos != nullptr) {  // fl(fl(x cos) + fl(rot(x) sin)), rot(x) = (-x2, x1)
+        const bool first_half = j < kLanes / 2;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float partner = __shfl_xor_sync(row_mask, x[e], kLanes / 2);
+          const float rot = first_half ? -partner : partner;
+          x[e] = __bfloat162float(__float2bfloat16_rn(__fadd_rn(__fmul_rn(x[e], cs[e]), __fmul_rn(rot, sn[e]))));
+        }
+      }
+      __nv_bfloat16* dst = is_q ? p.q_out + (static_cast<int64_t>(t) * p.heads + hr) * D
+                                : p.key_pool + (slot * p.kv_heads + (hr - p.heads)) * D;
+      *reinterpret_cast<uint4*>(dst + 8 * j) = pack8(x);
     }
   }
 }

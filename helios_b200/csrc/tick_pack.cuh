@@ -15,8 +15,10 @@
 //     and the owning row;
 //   * logit_indices: the trailing logit_count_r tokens of each row;
 //   * the attention work lists: split-K items for decode-class rows
-//     (count <= decode_max_tokens) and, for prefill-class rows, pairs of query tiles
-//     (i, m-1-i) of a row with m tiles, so every pair sees the same causal work.
+//     (count <= decode_max_tokens) and, for prefill-class rows, pairs of adjacent
+//     query tiles (2i, 2i+1) of a row with m tiles. Tiles of at most 32 tokens
+//     (GROUP >= 4) read the same 64-key tiles, so the two stay busy together; larger
+//     tiles differ by at most two key tiles.
 // Every output write is bounded by the capacity the host sized it for; an entry
 // that would fall outside is skipped and reported in the status word.
 #pragma once
@@ -179,10 +181,9 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
       for (int i = 0; i < (tiles + 1) / 2; ++i) {
         if (f_off[r] + i >= p.prefill_capacity) { raise_status(kStatusBadRow); break; }
         int32_t* it = p.prefill_items + 3 * (f_off[r] + i);
-        const int partner = tiles - 1 - i;
         it[0] = r;
-        it[1] = i * p.prefill_tile_tokens;
-        it[2] = partner > i ? partner * p.prefill_tile_tokens : -1;
+        it[1] = 2 * i * p.prefill_tile_tokens;
+        it[2] = 2 * i + 1 < tiles ? (2 * i + 1) * p.prefill_tile_tokens : -1;
       }
     }
   }

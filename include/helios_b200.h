@@ -69,7 +69,7 @@ HB_API int hb_device_status(uint32_t* status, int clear);
  * int64 [logit_capacity], decode_items int32 [decode_capacity][4] (row, split,
  * partial base, splits) for rows with count <= decode_max_tokens, split every
  * split_keys keys, prefill_items int32 [prefill_capacity][3] (row, start of query
- * tile i, start of tile m-1-i or -1) pairing the m tiles of prefill_tile_tokens
+ * tile 2i, start of tile 2i+1 or -1) pairing adjacent tiles of prefill_tile_tokens
  * queries of a row. Entries past a capacity are not written.
  */
 HB_API int hb_tick_pack(const int32_t* rows, int32_t num_rows, const int32_t* updates, int32_t num_updates,

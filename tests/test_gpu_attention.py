@@ -14,7 +14,7 @@ import numpy as np
 import pytest
 import torch
 
-from helios_b200 import _native
+from helios_b200 import _native, ops
 from helios_b200.paged_cache import KVPagePool, PackedBatchCache
 from oracle.attention import paged_attention, write_pool
 from tests.golden.inputs import attention_inputs, digest
@@ -119,6 +119,44 @@ def test_mixed_tick():
     g = torch.Generator().manual_seed(3)
     lengths = torch.randint(1024, 4097, (32,), generator=g).tolist() + [0]
     _run(lengths, [1] * 32 + [512])
+
+
+def test_mixed_tick_is_complete_for_work_queued_after_it():
+    """A tick with both halves of the work list, called on a non-default stream: work the
+    caller queues right behind it on that stream sees every output row written, call after call."""
+    g = torch.Generator().manual_seed(9)
+    lengths = torch.randint(1024, 4097, (32,), generator=g).tolist() + [0]
+    counts = [1] * 32 + [2048]
+    pages = sum(math.ceil((l + c) / 256) for l, c in zip(lengths, counts)) + 4
+    pool = KVPagePool(attn_config(heads=32, kv_heads=8), pages, device=DEV)
+    pool.storage.normal_(0.0, 0.3)
+    order = torch.randperm(pages, generator=g).tolist()
+    caches, at = [], 0
+    for length, count in zip(lengths, counts):
+        n = math.ceil(length / 256)
+        caches.append(cache_with_pages(pool, length + count + 8, length, order[at: at + n]))
+        at += n
+    batch = PackedBatchCache(caches)
+    batch.prepare_packed(counts)
+    assert batch.num_decode_items > 0 and batch.num_prefill_items > 0
+    q = torch.randn(sum(counts), 32, 128, device=DEV).to(torch.bfloat16)
+    want = torch.empty_like(q)
+    ops.paged_attention(q, pool.keys[0], pool.values[0], batch, want)
+    torch.cuda.synchronize()
+    assert torch.isfinite(want.float()).all()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    snaps = []
+    with torch.cuda.stream(stream):
+        out = torch.empty_like(q)
+        for _ in range(3):
+            out.fill_(float("nan"))
+            ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out)
+            snaps.append(out.clone())  # queued right behind the attention call
+    torch.cuda.synchronize()
+    for snap in snaps:
+        assert torch.equal(snap, want)
+    assert _native.device_status() == 0
 
 
 @pytest.mark.parametrize("heads,kv_heads", [(8, 8), (16, 8), (64, 8)])

@@ -87,11 +87,11 @@ def test_work_items_cover_every_row_once():
             assert [b for _, b, _ in items] == [record + s * count for s in range(n)]
             record += n * count
         else:
-            # Query tiles of 128 // group tokens, tile i paired with tile m-1-i (equal causal work).
+            # Query tiles of 128 // group tokens, adjacent tiles (2i, 2i+1) paired (same key tiles).
             tile = 128 // group
             m = math.ceil(count / tile)
             pairs = [(a, b) for r, a, b in pre if r == row]
-            assert pairs == [(i * tile, (m - 1 - i) * tile if m - 1 - i > i else -1) for i in range((m + 1) // 2)]
+            assert pairs == [(2 * i * tile, (2 * i + 1) * tile if 2 * i + 1 < m else -1) for i in range((m + 1) // 2)]
     assert record == batch.partial_records
     meta = pack_tick(lengths, counts, [[p.index for p in c.pages] for c in caches], [c.capacity for c in caches])
     assert batch.write_slots.tolist() == meta["write_slots"]
