@@ -93,13 +93,17 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_attention_kernel(Attent
     if (lane == 0) {
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
-      int issued = 0;
+      int issued = 0, cached_pidx = -1, cached_page = -1;
       for (int t = 0; t < n_tiles; ++t) {
         const int stage = t % kDecStages;
         if (t >= kDecStages && !mbar_wait(&empty_bar[stage], ((t / kDecStages) - 1) & 1, &abort_flag)) break;
         const int key = kb + t * kDecTileKeys;
         const int pidx = key / p.page_size;
-        int page = pidx < p.width ? p.block_table[static_cast<int64_t>(row) * p.width + pidx] : -1;
+        if (pidx != cached_pidx) {  // one block-table read per page, not per key tile
+          cached_page = pidx < p.width ? p.block_table[static_cast<int64_t>(row) * p.width + pidx] : -1;
+          cached_pidx = pidx;
+        }
+        const int page = cached_page;
         if (page < 0 || page >= p.num_pages) {
           raise_status(kStatusBadPage);
           abort_flag = 1;

@@ -7,28 +7,31 @@
 // One CTA owns two query tiles of 128 rows each; a tile is (128 / GROUP)
 // consecutive tokens of one sequence x the GROUP query heads that share KV head h.
 // The two tiles are adjacent (2i and 2i+1 of a row), so they need the same key
-// tiles (up to two more for the second when a tile exceeds 32 tokens), both stay
-// busy for the CTA's whole life, and every K/V tile is read once for both. Roles (320 threads):
-//   warp 0     TMA producer: both Q tiles once, then 64-key K and V tiles (two
-//              128B-swizzled [64][64] boxes each) from the pages the block table
-//              names, into separate 3-stage K and V rings;
-//   warp 1     owns the TMEM allocation (512 columns: S0, S1 at 0/64, O0, O1 at
-//              128/256, P buffers at 384..511); lane 0 issues tcgen05.mma:
-//              S_t = Q_t K^T (M=128, N=64, K=128, both operands in shared memory)
-//              and O_t += P_t V (M=128, N=128, K=64, P read from TMEM),
-//              committing to mbarriers;
-//   warps 2-5  softmax for tile 0, warps 6-9 softmax for tile 1: thread i owns
-//              accumulator row i (TMEM lane i), so row max and sum need no
-//              shuffles; P is stored as bf16 pairs into one of the tile's two TMEM
-//              P buffers (tcgen05.st), so the softmax of key tile j waits only for
-//              the P V of key tile j-2 (or j-1 when O must be rescaled).
-// The MMA thread polls both tiles' barriers and issues whichever S or P V is
-// ready, so the tensor pipe works on one tile while the softmax warps work on
-// the other. O is rescaled (in TMEM) only when a row's
-// running max grows by more than 2^8; exponents stay relative to the max in use,
-// so P <= 2^8 and the final O / l is unchanged. Keys at or beyond seqused_k get
-// their V rows zeroed so stale pool memory cannot reach the accumulator. The
-// longest pairs (the last of a row) of every KV head are launched first.
+// tiles (at most one more for the second), both stay busy for the CTA's whole
+// life, and every K/V tile is read once for both. Keys go in steps of 128, so
+// every tcgen05.mma is M128 x N128 x K16 (full rate) and each barrier handoff of
+// the MMA thread is paid once per 128 keys. Roles (576 threads):
+//   warp 0     TMA producer: both Q tiles once, then 128-key K and V tiles (four
+//              128B-swizzled [64 keys][64 d] boxes each, each 64-key half from the
+//              page the block table names) into 2-stage K and V rings;
+//   warp 1     owns the TMEM allocation (512 columns: the S/P buffer of tile t at
+//              128 t, its O accumulator at 256 + 128 t); lane 0 issues
+//              S_t = Q_t K^T (both operands in shared memory) and O_t += P_t V (P
+//              read from TMEM, where the softmax wrote it over S_t), in a fixed
+//              order with blocking waits: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1). So
+//              the tensor core computes one tile's P V and next S while the
+//              softmax warps work on the other tile;
+//   warps 2-9  softmax for tile 0, warps 10-17 for tile 1: the two warps of a
+//              TMEM lane quadrant split the 128 key columns of each accumulator
+//              row (thread = row, so no shuffles); they swap their half-row maxima
+//              through shared memory (an mbarrier per row pair, so the wait is
+//              bounded) and their row sums once at the end; each warp rescales and
+//              writes its 64 of the 128 output columns.
+// O is rescaled (in TMEM) only when a row's running max grows by more than 2^8;
+// exponents stay relative to the max in use, so P <= 2^8 and the final O / l is
+// unchanged. Keys at or beyond seqused_k get their V rows zeroed so stale pool
+// memory cannot reach the accumulator. The longest pairs (the last of a row) of
+// every KV head are launched first.
 #pragma once
 
 #include "hb_common.cuh"
@@ -38,16 +41,22 @@ namespace hb {
 
 constexpr int kPreRows = 128;     // rows per query tile
 constexpr int kPreTiles = 2;      // query tiles per CTA
-constexpr int kPreKeys = 64;      // keys per K/V tile
-constexpr int kPreKStages = 3;
-constexpr int kPreVStages = 3;
-constexpr int kPreThreads = 320;
-constexpr uint32_t kPreQBytes = kPreRows * 128 * 2;   // [128][128] bf16 as two [128][64] boxes
-constexpr uint32_t kPreKVBytes = kPreKeys * 128 * 2;  // [64][128] as two [64][64] boxes
+constexpr int kPreKeys = 128;     // keys per K/V tile (the N of S = Q K^T)
+constexpr int kPreBoxKeys = 64;   // keys per TMA box (the box of the shared K/V tensor maps)
+constexpr int kPreKStages = 2;
+constexpr int kPreVStages = 2;
+constexpr int kPreSoftmaxWarps = 8;  // per query tile: two warps per TMEM lane quadrant
+constexpr int kPreSoftmaxThreads = kPreSoftmaxWarps * 32;
+constexpr int kPreThreads = 64 + kPreTiles * kPreSoftmaxThreads;  // TMA warp, MMA warp, softmax
+constexpr uint32_t kPreQBytes = kPreRows * 128 * 2;    // [128 rows][128 d] as two [128][64] d-halves
+constexpr uint32_t kPreKVBytes = kPreKeys * 128 * 2;   // [128 keys][128 d] as two [128][64] d-halves
+constexpr uint32_t kPreKVHalf = kPreKVBytes / 2;       // one d-half: [128 keys][64 d], 128 B rows
+constexpr uint32_t kPreBoxBytes = kPreBoxKeys * 64 * 2;  // one TMA box: [64 keys][64 d]
 constexpr uint32_t kPreSmemBytes = kPreTiles * kPreQBytes + (kPreKStages + kPreVStages) * kPreKVBytes + 1024;
-// TMEM columns: S_t at 64 t, O_t at 128 + 128 t, P_{t,b} (bf16 pairs) at 384 + 32 (2 t + b).
+// TMEM columns: S/P buffer of tile t at 128 t (S as fp32, then P as bf16 pairs over
+// its first 64 columns once S has been read), O_t at 256 + 128 t.
 constexpr uint32_t kPreTmemCols = 512;
-constexpr uint32_t kPreTmemP = 384;
+constexpr uint32_t kPreTmemO = 256;
 constexpr float kRescaleThreshold = 8.f;  // log2 units: rescale O when the max grows by more than 2^8
 
 __device__ __forceinline__ float fast_exp2(float x) {
@@ -70,7 +79,11 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
   uint8_t* v_s = k_s + kPreKStages * kPreKVBytes;
 
   __shared__ uint64_t q_full, k_full[kPreKStages], k_empty[kPreKStages], v_full[kPreVStages], v_empty[kPreVStages];
-  __shared__ uint64_t s_full[kPreTiles], s_free[kPreTiles], p_full[kPreTiles][2], o_done[kPreTiles][2], drain_bar;
+  __shared__ uint64_t s_full[kPreTiles], p_full[kPreTiles], o_done[kPreTiles], drain_bar;
+  // Row max (per step parity) and final row sum exchanged by the two warps sharing a row.
+  __shared__ float xmax[kPreTiles][2][2][kPreRows];
+  __shared__ float xsum[kPreTiles][2][kPreRows];
+  __shared__ uint64_t xbar[kPreTiles][4][2], lbar[kPreTiles][4];
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_flag;
 
@@ -82,7 +95,7 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
   const int q0 = p.cu_seq_q[row];
   const int count = p.cu_seq_q[row + 1] - q0;
   const int end = p.seqused_k[row];
-  // Tile 0 starts at item[1]; tile 1 (if any) at item[2] > item[1], so n_kv0 <= n_kv1.
+  // Tile 0 starts at item[1]; tile 1 (if any) at item[2] > item[1], so nk0 <= nk1.
   const int qs0 = item[1], qs1 = item[2];
   const int tc0 = min(kTileTokens, count - qs0);
   const int tc1 = qs1 >= 0 ? min(kTileTokens, count - qs1) : 0;
@@ -95,12 +108,14 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
     for (int s = 0; s < kPreKStages; ++s) { mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1); }
     for (int s = 0; s < kPreVStages; ++s) { mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1); }
     for (int t = 0; t < kPreTiles; ++t) {
-      mbar_init(&s_full[t], 1);
-      mbar_init(&s_free[t], 128);
-      for (int b = 0; b < 2; ++b) {
-        mbar_init(&p_full[t][b], 128);
-        mbar_init(&o_done[t][b], 1);
+      for (int qd = 0; qd < 4; ++qd) {
+        mbar_init(&xbar[t][qd][0], 64);
+        mbar_init(&xbar[t][qd][1], 64);
+        mbar_init(&lbar[t][qd], 64);
       }
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], kPreSoftmaxThreads);
+      mbar_init(&o_done[t], 1);
     }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
@@ -129,27 +144,48 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
         tma_load_3d(qt, &qmap, &q_full, 0, h * GROUP, tok);
         tma_load_3d(qt + kPreQBytes / 2, &qmap, &q_full, 64, h * GROUP, tok);
       }
-      int k_issued = 0, v_issued = 0;
+      int k_issued = 0, v_issued = 0, cached_pidx = -1, cached_page = -1;
       for (int j = 0; j < n_all; ++j) {
-        const int key = j * kPreKeys;
-        const int pidx = key / p.page_size;
-        const int page = pidx < p.width ? p.block_table[static_cast<int64_t>(row) * p.width + pidx] : -1;
-        if (page < 0 || page >= p.num_pages) {
+        // Pool rows of the two 64-key halves of key tile j. A half that starts at or past
+        // the sequence end (its rows are masked and their V zeroed) re-reads the first
+        // half's rows, so no page beyond the row's block-table entries is named.
+        int tok[2];
+        bool bad = false;
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          const int key = j * kPreKeys + hb * kPreBoxKeys;
+          if (hb == 1 && key >= end) { tok[1] = tok[0]; continue; }
+          const int pidx = key / p.page_size;
+          if (pidx != cached_pidx) {  // one block-table read per page
+            cached_page = pidx < p.width ? p.block_table[static_cast<int64_t>(row) * p.width + pidx] : -1;
+            cached_pidx = pidx;
+          }
+          if (cached_page < 0 || cached_page >= p.num_pages) bad = true;
+          tok[hb] = cached_page * p.page_size + (key % p.page_size);
+        }
+        if (bad) {
           raise_status(kStatusBadPage);
           abort_flag = 1;
           break;
         }
-        const int tok = page * p.page_size + (key % p.page_size);
         const int ks = j % kPreKStages, vs = j % kPreVStages;
         if (j >= kPreKStages && !mbar_wait(&k_empty[ks], ((j / kPreKStages) - 1) & 1, &abort_flag)) break;
         mbar_expect_tx(&k_full[ks], kPreKVBytes);
-        tma_load_3d(k_s + ks * kPreKVBytes, &kmap, &k_full[ks], 0, h, tok);
-        tma_load_3d(k_s + ks * kPreKVBytes + kPreKVBytes / 2, &kmap, &k_full[ks], 64, h, tok);
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          uint8_t* dst = k_s + ks * kPreKVBytes + hb * kPreBoxBytes;
+          tma_load_3d(dst, &kmap, &k_full[ks], 0, h, tok[hb]);
+          tma_load_3d(dst + kPreKVHalf, &kmap, &k_full[ks], 64, h, tok[hb]);
+        }
         ++k_issued;
         if (j >= kPreVStages && !mbar_wait(&v_empty[vs], ((j / kPreVStages) - 1) & 1, &abort_flag)) break;
         mbar_expect_tx(&v_full[vs], kPreKVBytes);
-        tma_load_3d(v_s + vs * kPreKVBytes, &vmap, &v_full[vs], 0, h, tok);
-        tma_load_3d(v_s + vs * kPreKVBytes + kPreKVBytes / 2, &vmap, &v_full[vs], 64, h, tok);
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          uint8_t* dst = v_s + vs * kPreKVBytes + hb * kPreBoxBytes;
+          tma_load_3d(dst, &vmap, &v_full[vs], 0, h, tok[hb]);
+          tma_load_3d(dst + kPreKVHalf, &vmap, &v_full[vs], 64, h, tok[hb]);
+        }
         ++v_issued;
       }
       mbar_drain(&q_full, 0);
@@ -166,77 +202,75 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
       constexpr uint32_t idesc_s = idesc_bf16(kPreRows, kPreKeys, false, false);
       constexpr uint32_t idesc_pv = idesc_bf16(kPreRows, D, false, true);
       bool ok = mbar_wait(&q_full, 0, &abort_flag);
+      // Operand descriptors are built once; per K step and stage only their start-address
+      // field (low 14 bits, 16-byte units) moves, by offsets that never carry out of it
+      // (shared memory is below 256 KB), so each MMA costs one add per operand.
+      const uint64_t q_desc0 = smem_desc(smem_u32(q_s), 16, 1024, kSwizzle128B);
+      const uint64_t k_desc0 = smem_desc(smem_u32(k_s), 16, 1024, kSwizzle128B);
+      const uint64_t v_desc0 = smem_desc(smem_u32(v_s), kPreKVHalf, 1024, kSwizzle128B);
       auto issue_s = [&](int t, int j) {
-        const uint32_t q_addr = smem_u32(q_s + t * kPreQBytes);
-        const uint32_t k_addr = smem_u32(k_s + (j % kPreKStages) * kPreKVBytes);
+        const uint64_t a = q_desc0 + static_cast<uint64_t>(t * (kPreQBytes >> 4));
+        const uint64_t b = k_desc0 + static_cast<uint64_t>((j % kPreKStages) * (kPreKVBytes >> 4));
+        const uint32_t d = tmem + kPreKeys * t;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t qoff = (kk >> 2) * (kPreQBytes / 2) + (kk & 3) * 32;
-          const uint32_t koff = (kk >> 2) * (kPreKVBytes / 2) + (kk & 3) * 32;
-          mma_ss(tmem + t * kPreKeys, smem_desc(q_addr + qoff, 16, 1024, kSwizzle128B),
-                 smem_desc(k_addr + koff, 16, 1024, kSwizzle128B), idesc_s, kk > 0);
+        for (int kk = 0; kk < D / 16; ++kk) {  // 16 of the 128 head dims per step
+          const uint32_t qoff = ((kk >> 2) * (kPreQBytes / 2) + (kk & 3) * 32) >> 4;
+          const uint32_t koff = ((kk >> 2) * kPreKVHalf + (kk & 3) * 32) >> 4;
+          mma_ss(d, a + qoff, b + koff, idesc_s, kk > 0);
         }
         mma_commit(&s_full[t]);
       };
       auto issue_pv = [&](int t, int j) {
-        const uint32_t p_tmem = tmem + kPreTmemP + (2 * t + (j & 1)) * (kPreKeys / 2);
-        const uint32_t v_addr = smem_u32(v_s + (j % kPreVStages) * kPreKVBytes);
+        const uint32_t p_tmem = tmem + kPreKeys * t;
+        const uint64_t b = v_desc0 + static_cast<uint64_t>((j % kPreVStages) * (kPreKVBytes >> 4));
+        const uint32_t d = tmem + kPreTmemO + t * 128;
 #pragma unroll
-        for (int kk = 0; kk < kPreKeys / 16; ++kk)  // 16 keys = 8 columns of P per step
-          mma_ts(tmem + 128 + t * 128, p_tmem + kk * 8,
-                 smem_desc(v_addr + kk * 2048, kPreKVBytes / 2, 1024, kSwizzle128B), idesc_pv, (j > 0 || kk > 0));
-        mma_commit(&o_done[t][j & 1]);
+        for (int kk = 0; kk < kPreKeys / 16; ++kk)  // 16 keys = 8 columns of P, 16 rows of V per step
+          mma_ts(d, p_tmem + kk * 8, b + ((kk * 2048) >> 4), idesc_pv, (j > 0 || kk > 0));
+        mma_commit(&o_done[t]);
       };
-      bool issued_any = false;
-      // Non-blocking scheduler: issue whichever S or P V is ready for either query
-      // tile, so one tile's softmax never holds up the other's tensor work. K (V) stage
-      // j is released once every tile that needs key tile j has issued its S (P V).
+      // Fixed issue order with blocking waits (a poll of an mbarrier costs about as
+      // much as an MMA, so the thread never polls): S of key tile 0 for both tiles,
+      // then per key tile j: P V_0(j), S_0(j+1), P V_1(j), S_1(j+1). S_t(j+1)
+      // overwrites the S/P buffer that P V_t(j) reads: tcgen05.mma of one thread run in
+      // issue order, so it does so only after that P V has read it. Tile 0's P V of a
+      // key tile goes first, so the V rows its softmax zeroes are zero for tile 1 too.
       const int nk[2] = {nk0, nk1};
-      int ns[2] = {0, 0}, npv[2] = {0, 0};
-      int krel = 0, vrel = 0;
-      uint64_t idle_since = globaltimer_ns();
-      while (ok) {
-        bool progress = false;
+      bool issued_any = false;
+      int k_have = -1;  // highest key tile whose K stage is known to have landed
+      auto need_k = [&](int x) -> bool {
+        if (k_have >= x) return true;
+        if (!mbar_wait(&k_full[x % kPreKStages], (x / kPreKStages) & 1, &abort_flag)) return false;
+        k_have = x;
+        tc_fence_after();
+        return true;
+      };
+      if (ok && n_all > 0) {
+        ok = need_k(0);
+        if (ok) {
+#pragma unroll
+          for (int t = 0; t < kPreTiles; ++t)
+            if (nk[t] > 0) issue_s(t, 0);
+          mma_commit(&k_empty[0]);
+          issued_any = true;
+        }
+      }
+      for (int j = 0; ok && j < n_all; ++j) {
+        if (!mbar_wait(&v_full[j % kPreVStages], (j / kPreVStages) & 1, &abort_flag)) { ok = false; break; }
 #pragma unroll
         for (int t = 0; t < kPreTiles; ++t) {
-          const int j = ns[t];
-          if (j < nk[t] && mbar_test(&k_full[j % kPreKStages], (j / kPreKStages) & 1) &&
-              (j == 0 || mbar_test(&s_free[t], (j - 1) & 1))) {
-            tc_fence_after();
-            issue_s(t, j);
-            ns[t] = j + 1;
-            progress = issued_any = true;
+          if (j >= nk[t]) continue;
+          if (!mbar_wait(&p_full[t], j & 1, &abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(t, j);
+          if (j + 1 < nk[t]) {
+            if (!need_k(j + 1)) { ok = false; break; }
+            issue_s(t, j + 1);
           }
         }
-        while (krel < n_all && (krel < ns[0] || krel >= nk[0]) && (krel < ns[1] || krel >= nk[1])) {
-          mma_commit(&k_empty[krel % kPreKStages]);
-          ++krel;
-        }
-#pragma unroll
-        for (int t = 0; t < kPreTiles; ++t) {
-          const int j = npv[t];
-          if (j < nk[t] && mbar_test(&v_full[j % kPreVStages], (j / kPreVStages) & 1) &&
-              mbar_test(&p_full[t][j & 1], (j >> 1) & 1)) {
-            tc_fence_after();
-            issue_pv(t, j);
-            npv[t] = j + 1;
-            progress = issued_any = true;
-          }
-        }
-        while (vrel < n_all && (vrel < npv[0] || vrel >= nk[0]) && (vrel < npv[1] || vrel >= nk[1])) {
-          mma_commit(&v_empty[vrel % kPreVStages]);
-          ++vrel;
-        }
-        if (npv[0] == nk[0] && npv[1] == nk[1] && krel == n_all && vrel == n_all) break;
-        if (progress) {
-          idle_since = globaltimer_ns();
-        } else if (*reinterpret_cast<volatile int*>(&abort_flag)) {
-          ok = false;
-        } else if (globaltimer_ns() - idle_since > kWaitLimitNs) {
-          abort_flag = 1;
-          raise_status(kStatusWaitTimeout);
-          ok = false;
-        }
+        if (!ok) break;
+        mma_commit(&v_empty[j % kPreVStages]);  // V_j is free once these P V complete
+        if (j + 1 < n_all) mma_commit(&k_empty[(j + 1) % kPreKStages]);
       }
       if (issued_any) {  // nothing may still write TMEM when it is freed
         mma_commit(&drain_bar);
@@ -244,12 +278,15 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax warpgroups
-    const int t = (warp - 2) >> 2;   // query tile of this warpgroup
-    const int quad = warp & 3;       // TMEM lane quadrant this warp may access
-    const int r = quad * 32 + lane;  // accumulator row == TMEM lane
+    // ------------------------------------------------------------ softmax warps
+    const int sw = warp - 2;
+    const int t = sw / kPreSoftmaxWarps;            // query tile of this warp
+    const int half = (sw % kPreSoftmaxWarps) >> 2;  // key columns 64 half .. 64 half + 63 of S
+    const int quad = warp & 3;                      // TMEM lane quadrant this warp may access
+    const int r = quad * 32 + lane;                 // accumulator row == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
-    const uint32_t tS = tmem + t * kPreKeys + lane_base, tO = tmem + 128 + t * 128 + lane_base;
+    const uint32_t tSP = tmem + kPreKeys * t + lane_base;
+    const uint32_t tO = tmem + kPreTmemO + t * 128 + half * 64 + lane_base;  // this warp's 64 output columns
     const int tok = r / GROUP;
     const int qs = t ? qs1 : qs0;
     const bool row_valid = tok < (t ? tc1 : tc0);
@@ -261,107 +298,116 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
       if (!mbar_wait(&s_full[t], j & 1, &abort_flag)) { ok = false; break; }
       tc_fence_after();
       float s[64];
-      tmem_ld64(tS, s);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&s_free[t]);
-      const int key0 = j * kPreKeys;
-      if (!(key0 + kPreKeys - 1 <= qpos && key0 + kPreKeys <= end)) {  // edge tile: mask
+      {
+        float* s0 = s;
+        float* s1 = s + 32;
+        tmem_ld32(tSP + half * 64, *reinterpret_cast<float(*)[32]>(s0));
+        tmem_ld32(tSP + half * 64 + 32, *reinterpret_cast<float(*)[32]>(s1));
+        tmem_wait_ld();
+      }
+      const int key0 = j * kPreKeys + half * 64;
+      if (!(key0 + 63 <= qpos && key0 + 64 <= end)) {  // edge of the causal or sequence range: mask
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
           const int key = key0 + c;
           s[c] = (key <= qpos && key < end) ? s[c] : -INFINITY;
         }
       }
-      // Max and sum as 8 independent chains (fmaxf is exact in any order; the sum
-      // order only moves rounding of the normaliser).
+      // Row max as 8 independent chains (fmaxf is exact in any order), then the
+      // partner warp's half through shared memory.
       float m8[8];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) m8[c] = fmaxf(s[c], s[c + 8]);
-#pragma unroll
-      for (int c = 16; c < 64; c += 8) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) m8[e] = fmaxf(m8[e], s[c + e]);
-      }
-      float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-      mx *= p.scale_log2;
+      for (int c = 0; c < 8; ++c)
+        m8[c] = fmaxf(fmaxf(fmaxf(s[c], s[c + 8]), fmaxf(s[c + 16], s[c + 24])),
+                      fmaxf(fmaxf(s[c + 32], s[c + 40]), fmaxf(s[c + 48], s[c + 56])));
+      const float mine = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      xmax[t][j & 1][half][r] = mine;
+      mbar_arrive(&xbar[t][quad][j & 1]);
+      if (!mbar_wait(&xbar[t][quad][j & 1], (j >> 1) & 1, &abort_flag)) { ok = false; break; }
+      const float mx = fmaxf(mine, xmax[t][j & 1][half ^ 1][r]) * p.scale_log2;
       // Lazy rescale: keep the max in use unless this tile's max exceeds it by 2^8.
       const bool grow = mx > m_used + kRescaleThreshold;
       const float m_new = grow ? mx : m_used;
       const float alpha = grow ? fast_exp2(m_used - m_new) : 1.f;  // m_used = -inf gives 0
       m_used = m_new;
       const float neg = m_new == -INFINITY ? 0.f : -m_new;
-      float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        s[c] = fast_exp2(fmaf(s[c], p.scale_log2, neg));
-        s8[c & 7] += s[c];
-      }
-      l = l * alpha + (((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])));
-      // P buffer j & 1 was last read by the P V of key tile j - 2.
-      if (j >= 2 && !mbar_wait(&o_done[t][j & 1], ((j >> 1) - 1) & 1, &abort_flag)) { ok = false; break; }
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
         // O must hold every P V so far before it is rescaled (tcgen05.ld/st are warp-collective).
-        if (!mbar_wait(&o_done[t][(j - 1) & 1], ((j - 1) >> 1) & 1, &abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&o_done[t], (j - 1) & 1, &abort_flag)) { ok = false; break; }
         tc_fence_after();
-        {
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          float o[16];
+          tmem_ld16(tO + cc * 16, o);
+          tmem_wait_ld();
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            float o[32];
-            tmem_ld32(tO + cc * 32, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] *= alpha;
-            tmem_st32(tO + cc * 32, o);
-          }
-          tmem_wait_st();
+          for (int c = 0; c < 16; ++c) o[c] *= alpha;
+          tmem_st16(tO + cc * 16, o);
         }
-      }
-      {  // P as bf16 pairs into this tile's TMEM P buffer j & 1 (row r = lane r)
-        uint32_t pw[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) pw[c] = pack_bf16(s[2 * c], s[2 * c + 1]);
-        tmem_st32u(tmem + kPreTmemP + (2 * t + (j & 1)) * (kPreKeys / 2) + lane_base, pw);
         tmem_wait_st();
       }
+      // P = exp2(S scale - max) as bf16 pairs over the first 64 columns of the S/P
+      // buffer (this warp's 64 keys -> columns 32 half .. 32 half + 31). Both warps of
+      // the row pair read their S before the max exchange above, so writing over it
+      // is safe.
+      float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int chunk = 0; chunk < 2; ++chunk) {
+        uint32_t pw[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float e0 = fast_exp2(fmaf(s[chunk * 32 + 2 * c], p.scale_log2, neg));
+          const float e1 = fast_exp2(fmaf(s[chunk * 32 + 2 * c + 1], p.scale_log2, neg));
+          s8[(2 * c) & 7] += e0;
+          s8[(2 * c + 1) & 7] += e1;
+          pw[c] = pack_bf16(e0, e1);
+        }
+        tmem_st16u(tSP + half * 32 + chunk * 16, pw);
+      }
+      tmem_wait_st();
+      l = l * alpha + (((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])));
       // Stale pool rows past the sequence end are zeroed in this V stage by the first
-      // query tile that uses key tile j: the MMA warp issues tile 0's P V before tile 1's,
-      // so both products read the zeros.
+      // query tile that uses key tile j (the MMA warp issues tile 1's P V of a key tile
+      // after tile 0's), so both products read the zeros. Each warp of a row pair clears
+      // its 64-column d-half of key row r.
+      const int vkey0 = j * kPreKeys;
       const bool zeroer = t == 0 || j >= nk0;
-      if (zeroer && key0 + kPreKeys > end && r < kPreKeys && key0 + r >= end) {
+      if (zeroer && vkey0 + kPreKeys > end && vkey0 + r >= end) {
         // V_j must have landed first, or its TMA write would land over the zeros.
         if (!mbar_wait(&v_full[j % kPreVStages], (j / kPreVStages) & 1, &abort_flag)) { ok = false; break; }
-        uint8_t* vrow = v_s + (j % kPreVStages) * kPreKVBytes;
+        uint8_t* vrow = v_s + (j % kPreVStages) * kPreKVBytes + half * kPreKVHalf;
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          *reinterpret_cast<uint4*>(vrow + sw128(r, c8)) = make_uint4(0, 0, 0, 0);
-          *reinterpret_cast<uint4*>(vrow + kPreKVBytes / 2 + sw128(r, c8)) = make_uint4(0, 0, 0, 0);
-        }
+        for (int c8 = 0; c8 < 8; ++c8) *reinterpret_cast<uint4*>(vrow + sw128(r, c8)) = make_uint4(0, 0, 0, 0);
         fence_proxy_async_smem();  // the zeros are read by the tensor core (async proxy)
       }
       tc_fence_before();
-      mbar_arrive(&p_full[t][j & 1]);
+      mbar_arrive(&p_full[t]);
     }
     // P V completes in issue order: the last one done means all are.
-    if (ok && n > 0 && mbar_wait(&o_done[t][(n - 1) & 1], ((n - 1) >> 1) & 1, &abort_flag)) {
-      tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* o = row_valid ? p.out + (static_cast<int64_t>(q0 + qs + tok) * p.heads + h * GROUP + r % GROUP) * D
-                                   : nullptr;
+    if (ok && n > 0 && mbar_wait(&o_done[t], (n - 1) & 1, &abort_flag)) {
+      xsum[t][half][r] = l;
+      mbar_arrive(&lbar[t][quad]);
+      if (mbar_wait(&lbar[t][quad], 0, &abort_flag)) {
+        const float total = l + xsum[t][half ^ 1][r];
+        tc_fence_after();
+        const float inv = total > 0.f ? 1.f / total : 0.f;
+        __nv_bfloat16* o = row_valid ? p.out + (static_cast<int64_t>(q0 + qs + tok) * p.heads + h * GROUP + r % GROUP) * D + half * 64
+                                     : nullptr;
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          float v[16];
+          tmem_ld16(tO + cc * 16, v);
+          tmem_wait_ld();
+          if (o != nullptr) {
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        float v[32];
-        tmem_ld32(tO + cc * 32, v);
-        tmem_wait_ld();
-        if (o != nullptr) {
-#pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {
-            uint4 w;
-            w.x = pack_bf16(v[c8 * 8 + 0] * inv, v[c8 * 8 + 1] * inv);
-            w.y = pack_bf16(v[c8 * 8 + 2] * inv, v[c8 * 8 + 3] * inv);
-            w.z = pack_bf16(v[c8 * 8 + 4] * inv, v[c8 * 8 + 5] * inv);
-            w.w = pack_bf16(v[c8 * 8 + 6] * inv, v[c8 * 8 + 7] * inv);
-            *reinterpret_cast<uint4*>(o + cc * 32 + c8 * 8) = w;
+            for (int c8 = 0; c8 < 2; ++c8) {
+              uint4 w;
+              w.x = pack_bf16(v[c8 * 8 + 0] * inv, v[c8 * 8 + 1] * inv);
+              w.y = pack_bf16(v[c8 * 8 + 2] * inv, v[c8 * 8 + 3] * inv);
+              w.z = pack_bf16(v[c8 * 8 + 4] * inv, v[c8 * 8 + 5] * inv);
+              w.w = pack_bf16(v[c8 * 8 + 6] * inv, v[c8 * 8 + 7] * inv);
+              *reinterpret_cast<uint4*>(o + cc * 16 + c8 * 8) = w;
+            }
           }
         }
       }

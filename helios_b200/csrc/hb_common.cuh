@@ -33,16 +33,12 @@ __device__ unsigned int g_status;
 
 __device__ __forceinline__ void raise_status(unsigned int bits) { atomicOr(&g_status, bits); }
 
-// Time limit for any spin-wait on an mbarrier (2 s of the GPU's global timer):
-// far above any legitimate wait, short enough that a protocol error ends the
-// kernel with a status bit instead of holding the GPU.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
-
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
+// Time limit for any spin-wait on an mbarrier, in SM clock cycles (2 s at 2 GHz,
+// longer at lower clocks): far above any legitimate wait, short enough that a
+// protocol error ends the kernel with a status bit instead of holding the GPU.
+// The SM's own cycle counter is read in every poll: it costs a few cycles, where a
+// read of the global timer delays the poll loop enough to slow every handoff.
+constexpr long long kWaitLimitCycles = 4000000000ll;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -67,14 +63,17 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 
+// One potentially blocking test: the thread sleeps until the phase completes or about
+// 1 ms passes (suspend-time hint), instead of spinning on the barrier, so hundreds of
+// waiting threads do not flood the shared-memory pipe the tensor core and TMA also use.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
       : "memory");
   return done != 0;
 }
@@ -96,11 +95,11 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 // timeout, or immediately when another thread of the CTA already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = globaltimer_ns();
+  const long long start = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - start > kWaitLimitNs) {
+    if (clock64() - start > kWaitLimitCycles) {
       *abort_flag = 1;
       raise_status(kStatusWaitTimeout);
       return false;
@@ -110,9 +109,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 
 // Drain wait used on the way out of an aborted kernel: never raises, just gives up.
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
-  const uint64_t start = globaltimer_ns();
+  const long long start = clock64();
   while (!mbar_try_wait(bar, parity))
-    if (globaltimer_ns() - start > kWaitLimitNs) return;
+    if (clock64() - start > kWaitLimitCycles) return;
 }
 
 // ---------------------------------------------------------------- TMA (no multicast)
@@ -186,6 +185,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 32 lanes x 16 columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 // 32 lanes x 64 columns: thread t of the warp gets 64 consecutive columns of lane (base + t).
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
   uint32_t* r = reinterpret_cast<uint32_t*>(v);
@@ -213,6 +221,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
       "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
 // 32 lanes x 32 columns of raw 32-bit words (e.g. packed bf16 pairs).
