@@ -33,7 +33,11 @@ struct AttentionParams {
   const int32_t* cu_seq_q;     // [B+1]
   const int32_t* seqused_k;    // [B]
   const int32_t* decode_items;   // [n][4] row, split, partial_base, n_splits
-  const int32_t* prefill_items;  // [n][2] row, query start
+  const int32_t* prefill_items;  // [n][3] row, query start of tile 2i, of tile 2i+1 or -1
+  // Optional device counts {decode items, prefill pairs, partial records} written by the
+  // tick-pack kernel: when set, grids are sized to capacities and CTAs past a count exit
+  // (a launch that stays valid, e.g. in a CUDA graph, while the work list changes).
+  const int32_t* counts;
   float* ws_out;   // [records, H, D]
   float* ws_lse;   // [records, H]
   int32_t width, num_pages, page_size, heads, kv_heads, split_keys, tokens;
@@ -63,6 +67,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_attention_kernel(Attent
   __shared__ int abort_flag;
   __shared__ float merge_ml[kDecConsumerWarps][16][2];
 
+  if (p.counts != nullptr && static_cast<int>(blockIdx.x) >= p.counts[0]) return;  // past this tick's items
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
   const int32_t* item = p.decode_items + 4 * blockIdx.x;
@@ -341,6 +346,7 @@ constexpr int kCombineMaxSplits = 8;
 template <int GROUP>
 __global__ void __launch_bounds__(128) decode_combine_kernel(AttentionParams p) {
   constexpr int D = 128;
+  if (p.counts != nullptr && static_cast<int>(blockIdx.x) >= p.counts[0]) return;
   const int32_t* item = p.decode_items + 4 * blockIdx.x;
   if (item[1] != 0 || item[3] <= 1) return;
   const int row = item[0], pbase = item[2], nsplit = item[3];

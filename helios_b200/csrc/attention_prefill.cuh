@@ -87,10 +87,12 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_flag;
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // KV head fastest, items last to first: the longest query tiles of every head launch first.
+  const int n_items = p.counts != nullptr ? p.counts[1] : p.num_prefill;
+  if (static_cast<int>(blockIdx.y) >= n_items) return;  // past this tick's items (capacity grid)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x;
-  const int32_t* item = p.prefill_items + 3 * (p.num_prefill - 1 - static_cast<int>(blockIdx.y));
+  const int32_t* item = p.prefill_items + 3 * (n_items - 1 - static_cast<int>(blockIdx.y));
   const int row = item[0];
   const int q0 = p.cu_seq_q[row];
   const int count = p.cu_seq_q[row + 1] - q0;

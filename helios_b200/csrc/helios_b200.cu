@@ -147,7 +147,7 @@ int hb_tick_pack(const int32_t* rows, int32_t num_rows, const int32_t* updates, 
                  int32_t* block_table, int32_t* cu_seq_q, int32_t* cu_seq_k, int32_t* seqused_k, int64_t* positions,
                  int64_t* write_slots, int32_t* token_row, int64_t* logit_indices, int32_t logit_capacity,
                  int32_t* decode_items, int32_t decode_capacity, int32_t* prefill_items, int32_t prefill_capacity,
-                 cudaStream_t stream) {
+                 int32_t* counts, cudaStream_t stream) {
   if (num_rows < 1 || num_rows > HB_MAX_TICK_ROWS)
     return fail(HB_ERR_INVALID, "num_rows %d outside [1, %d]", num_rows, HB_MAX_TICK_ROWS);
   if (rows == nullptr || arena == nullptr || block_table == nullptr || cu_seq_q == nullptr || cu_seq_k == nullptr ||
@@ -166,7 +166,7 @@ int hb_tick_pack(const int32_t* rows, int32_t num_rows, const int32_t* updates, 
   hb::TickPackParams p{rows, updates, arena, num_rows, num_updates, arena_width, arena_slots, page_size, width,
                        num_pages, decode_max_tokens, split_keys, prefill_tile_tokens, block_table, cu_seq_q, cu_seq_k,
                        seqused_k, positions, write_slots, token_row, logit_indices, decode_items, prefill_items,
-                       total_tokens, logit_capacity, decode_capacity, prefill_capacity};
+                       total_tokens, logit_capacity, decode_capacity, prefill_capacity, counts};
   const int smem = 6 * (num_rows + 1) * static_cast<int>(sizeof(int32_t));
   if (int rc = ensure_smem(hb::tick_pack_kernel, 6 * (HB_MAX_TICK_ROWS + 1) * 4, g_tick_smem)) return rc;
   hb::tick_pack_kernel<<<1, hb::kTickThreads, smem, stream>>>(p);
@@ -219,9 +219,10 @@ size_t hb_attention_workspace_bytes(int32_t partial_records, int32_t heads, int3
 int hb_paged_attention(const void* q, const void* key_pool, const void* value_pool, int64_t num_pages,
                        int32_t page_size, const int32_t* block_table, int32_t width, const int32_t* cu_seq_q,
                        const int32_t* seqused_k, const int32_t* decode_items, int32_t num_decode_items,
-                       const int32_t* prefill_items, int32_t num_prefill_items, int32_t partial_records,
-                       int32_t split_keys, int32_t total_tokens, int32_t heads, int32_t kv_heads, int32_t head_dim,
-                       float scale, void* workspace, size_t workspace_bytes, void* out, cudaStream_t stream) {
+                       const int32_t* prefill_items, int32_t num_prefill_items, const int32_t* counts,
+                       int32_t partial_records, int32_t split_keys, int32_t total_tokens, int32_t heads,
+                       int32_t kv_heads, int32_t head_dim, float scale, void* workspace, size_t workspace_bytes,
+                       void* out, cudaStream_t stream) {
   if (head_dim != 128) return fail(HB_ERR_UNSUPPORTED, "paged attention supports head_dim 128, got %d", head_dim);
   if (heads < 1 || kv_heads < 1 || heads % kv_heads) return fail(HB_ERR_INVALID, "bad head counts");
   const int group = heads / kv_heads;
@@ -261,6 +262,7 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
   p.split_keys = split_keys;
   p.tokens = total_tokens;
   p.num_prefill = num_prefill_items;
+  p.counts = counts;
   p.scale_log2 = scale * 1.4426950408889634f;
 
   const uint64_t pool_tokens = static_cast<uint64_t>(num_pages) * page_size;
@@ -325,9 +327,9 @@ int hb_paged_attention_static_workspace(const void* q, const void* key_pool, con
                                        int32_t width, const int32_t* cu_seq_q, const int32_t* seqused_k,
                                        const int32_t* decode_items, int32_t num_decode_items,
                                        const int32_t* prefill_items, int32_t num_prefill_items,
-                                       int32_t partial_records, int32_t split_keys, int32_t total_tokens,
-                                       int32_t heads, int32_t kv_heads, int32_t head_dim, float scale, void* out,
-                                       cudaStream_t stream) {
+                                       const int32_t* counts, int32_t partial_records, int32_t split_keys,
+                                       int32_t total_tokens, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                                       float scale, void* out, cudaStream_t stream) {
   const size_t need = hb_attention_workspace_bytes(partial_records, heads, head_dim);
   if (need > HB_STATIC_WORKSPACE_BYTES)
     return fail(HB_ERR_INVALID,
@@ -350,7 +352,7 @@ int hb_paged_attention_static_workspace(const void* q, const void* key_pool, con
     ws = g_static_ws_ptr[dev];
   }
   return hb_paged_attention(q, key_pool, value_pool, num_pages, page_size, block_table, width, cu_seq_q, seqused_k,
-                            decode_items, num_decode_items, prefill_items, num_prefill_items, partial_records,
+                            decode_items, num_decode_items, prefill_items, num_prefill_items, counts, partial_records,
                             split_keys, total_tokens, heads, kv_heads, head_dim, scale, ws, HB_STATIC_WORKSPACE_BYTES,
                             out, stream);
 }

@@ -44,6 +44,7 @@ struct TickPackParams {
   int32_t* decode_items;   // [decode_capacity][4] row, split, partial_base, n_splits
   int32_t* prefill_items;  // [prefill_capacity][3] row, first tile start, second tile start or -1
   int32_t total_tokens, logit_capacity, decode_capacity, prefill_capacity;
+  int32_t* counts;         // optional [3]: decode items, prefill pairs, partial records (capped)
 };
 
 constexpr int kTickThreads = 1024;
@@ -150,6 +151,11 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
     d_off[B] = base[3];
     r_off[B] = base[4];
     f_off[B] = base[5];
+    if (p.counts != nullptr) {  // work-list sizes for launches sized to capacities
+      p.counts[0] = min(base[3], p.decode_capacity);
+      p.counts[1] = min(base[5], p.prefill_capacity);
+      p.counts[2] = base[4];
+    }
   }
   __syncthreads();
 

@@ -149,6 +149,15 @@ class Qwen3Model(nn.Module):
         cos, sin = rope_parameters(config)
         self.register_buffer("cos", cos, persistent=False)
         self.register_buffer("sin", sin, persistent=False)
+        self._graphs = None  # TickGraphs once enable_cuda_graphs() is called
+
+    def enable_cuda_graphs(self, max_graphs: int = 4) -> None:
+        """Replay the device half of packed ticks from CUDA graphs (see helios_b200.graphs).
+        Logits are identical to eager ticks; the returned logits tensor is reused by the
+        next tick of the same shape."""
+        from helios_b200.graphs import TickGraphs
+
+        self._graphs = TickGraphs(self, max_graphs)
 
     def forward(self, input_ids: torch.Tensor, cache: PagedBatchCache | None = None,
                 position_ids: torch.Tensor | None = None,
@@ -169,17 +178,28 @@ class Qwen3Model(nn.Module):
         if max(c.length + tokens for c in cache.caches) > self.config.context_length:
             raise ValueError(f"Qwen3-4B supports at most {self.config.context_length:,} tokens per request.")
         # prepare(tokens) packed one logit row per sequence: its last position.
-        _, normed = self._layers(input_ids.reshape(-1), cache)
+        if self._graphs is not None and input_ids.is_cuda:
+            logits = self._graphs.run(input_ids, cache)
+        else:
+            logits = self._packed_logits(input_ids.reshape(-1), cache)
         cache.advance(tokens, slots=cache_slots)
-        rows = normed.index_select(0, cache.logit_rows)
-        return F.linear(rows, self.output.weight).view(cache.batch_size, 1, -1)
+        return logits.view(cache.batch_size, 1, -1)
 
     def _forward_packed(self, input_ids: torch.Tensor, cache: PackedBatchCache) -> torch.Tensor:
         if input_ids.shape != (1, sum(cache.counts)):
             raise ValueError("Packed input does not match query lengths.")
-        _, normed = self._layers(input_ids.reshape(-1), cache)
+        if self._graphs is not None and input_ids.is_cuda:
+            logits = self._graphs.run(input_ids, cache)
+        else:
+            logits = self._packed_logits(input_ids.reshape(-1), cache)
         cache.advance_packed()
-        rows = normed.index_select(0, cache.logit_indices)
+        return logits
+
+    def _packed_logits(self, ids: torch.Tensor, cache: PagedBatchCache) -> torch.Tensor:
+        """Device half of a prepared tick: logits of the cache's logit rows. It makes no host
+        synchronisation, so it can be captured into a CUDA graph."""
+        _, normed = self._layers(ids, cache)
+        rows = normed.index_select(0, cache.logit_rows)
         return F.linear(rows, self.output.weight)
 
     def _layers(self, ids: torch.Tensor, cache: PagedBatchCache) -> tuple[torch.Tensor, torch.Tensor]:

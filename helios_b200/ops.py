@@ -51,7 +51,8 @@ def tick_pack(rows_dev: torch.Tensor, num_rows: int, updates_dev: torch.Tensor |
         out["seqused_k"].data_ptr(), out["positions"].data_ptr(), out["write_slots"].data_ptr(),
         out["token_row"].data_ptr(), out["logit_store"].data_ptr(), out["logit_store"].numel(),
         out["decode_items"].data_ptr(), out["decode_items"].numel() // 4,
-        out["prefill_items"].data_ptr(), out["prefill_items"].numel() // 3, _stream(rows_dev.device))
+        out["prefill_items"].data_ptr(), out["prefill_items"].numel() // 3, _ptr(out.get("counts")),
+        _stream(rows_dev.device))
     _native.check(rc, "hb_tick_pack")
 
 
@@ -89,7 +90,8 @@ def workspace_bytes(partial_records: int, heads: int, head_dim: int) -> int:
 def paged_attention(q: torch.Tensor, key_pool: torch.Tensor, value_pool: torch.Tensor, meta, out: torch.Tensor,
                     *, scale: float | None = None) -> torch.Tensor:
     """Kernel (c): ``q [T, H, d]`` against the paged pool described by ``meta``
-    (a prepared paged batch cache); writes ``out [T, H, d]``."""
+    (a prepared paged batch cache); writes ``out [T, H, d]``. A cache in capacity mode
+    passes its device work counts and launches grids sized to its capacities."""
     _need(q, BF16, "q")
     _need(out, BF16, "out")
     _need(key_pool, BF16, "key_pool")
@@ -101,8 +103,9 @@ def paged_attention(q: torch.Tensor, key_pool: torch.Tensor, value_pool: torch.T
     rc = lib().hb_paged_attention(
         q.data_ptr(), key_pool.data_ptr(), value_pool.data_ptr(), key_pool.shape[0], key_pool.shape[1],
         meta.block_table.data_ptr(), meta.block_table.shape[1], meta.cu_seq_q.data_ptr(), meta.seqused_k.data_ptr(),
-        meta.decode_items.data_ptr(), meta.num_decode_items, meta.prefill_items.data_ptr(), meta.num_prefill_items,
-        meta.partial_records, meta.split_keys, tokens, heads, kv_heads, dim, float(scale),
+        meta.decode_items.data_ptr(), meta.launch_decode_items, meta.prefill_items.data_ptr(),
+        meta.launch_prefill_items, _ptr(meta.attention_counts), meta.launch_partial_records, meta.split_keys, tokens,
+        heads, kv_heads, dim, float(scale),
         _ptr(ws), ws.numel() if ws is not None else 0, out.data_ptr(), _stream(q.device))
     _native.check(rc, "hb_paged_attention")
     return out

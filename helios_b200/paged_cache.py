@@ -267,6 +267,14 @@ class PagedBatchCache:
         self._i64 = None
         self.workspace: torch.Tensor | None = None
         self.uploaded_bytes = 0
+        # Capacity mode (set by the CUDA-graph runner): metadata buffers and attention
+        # launches are sized to work capacities with headroom and the kernels read the
+        # tick's real work counts from the device, so launch arguments and buffer
+        # addresses stay the same from tick to tick.
+        self.capacity_mode = False
+        self.work_capacity: tuple[int, int] | None = None
+        self.attention_counts: torch.Tensor | None = None
+        self.launch_decode_items = self.launch_prefill_items = self.launch_partial_records = 0
 
     @property
     def length(self) -> int:
@@ -390,6 +398,17 @@ class PagedBatchCache:
         self.num_decode_items = desc["num_decode_items"]
         self.partial_records = desc["partial_records"]
         self.num_prefill_items = desc["num_prefill_items"]
+        if self.capacity_mode:
+            cap = self.work_capacity
+            if cap is None or self.num_decode_items > cap[0] or self.num_prefill_items > cap[1]:
+                # Headroom of one more split and one more tile pair per row.
+                cap = (self.num_decode_items + self.batch_size, self.num_prefill_items + self.batch_size)
+                self.work_capacity = cap
+            self.launch_decode_items, self.launch_prefill_items = cap
+            self.launch_partial_records = cap[0] * desc["decode_max"]  # each item has <= decode_max rows
+        else:
+            self.launch_decode_items, self.launch_prefill_items = self.num_decode_items, self.num_prefill_items
+            self.launch_partial_records = self.partial_records
         rows, updates = desc["rows"], desc["updates"]
         total, width = desc["total_tokens"], desc["width"]
         if self._staging is None:
@@ -400,7 +419,7 @@ class PagedBatchCache:
         ops.tick_pack(dev[: rows.size], self.batch_size, dev[rows.size:], updates.size // 3, pool.arena,
                       pool.page_size, width, pool.num_pages, desc["decode_max"], desc["split_keys"],
                       desc["tile_tokens"], total, out)
-        need = ops.workspace_bytes(self.partial_records, config.n_heads, config.head_dim)
+        need = ops.workspace_bytes(self.launch_partial_records, config.n_heads, config.head_dim)
         if need and (self.workspace is None or self.workspace.numel() < need):
             self.workspace = torch.empty(max(need, 2 * (0 if self.workspace is None else self.workspace.numel())),
                                          dtype=torch.uint8, device=pool.device)
@@ -414,13 +433,14 @@ class PagedBatchCache:
         self.logit_rows = out["logit_indices"]
         self.decode_items = out["decode_items"]
         self.prefill_items = out["prefill_items"]
+        self.attention_counts = out["counts"] if self.capacity_mode else None
         self.total_tokens = total
 
     def _outputs(self, rows: int, width: int, tokens: int, logits: int) -> dict:
         """Views of two reusable device buffers sized for this tick."""
-        n_dec = max(1, self.num_decode_items)
-        n_pre = max(1, self.num_prefill_items)
-        sizes32 = [rows * width, rows + 1, rows + 1, rows, max(tokens, 1), 4 * n_dec, 3 * n_pre]
+        n_dec = max(1, self.launch_decode_items)
+        n_pre = max(1, self.launch_prefill_items)
+        sizes32 = [rows * width, rows + 1, rows + 1, rows, max(tokens, 1), 4 * n_dec, 3 * n_pre, 4]
         sizes64 = [max(tokens, 1), max(tokens, 1), max(logits, 1)]
         dev = self.pool.device
         if self._i32 is None or self._i32.numel() < sum(sizes32):
@@ -433,7 +453,7 @@ class PagedBatchCache:
         v64 = [self._i64[o64[i]:o64[i + 1]] for i in range(len(sizes64))]
         return {
             "block_table": v32[0].view(rows, width), "cu_seq_q": v32[1], "cu_seq_k": v32[2], "seqused_k": v32[3],
-            "token_row": v32[4][:tokens], "decode_items": v32[5], "prefill_items": v32[6],
+            "token_row": v32[4][:tokens], "decode_items": v32[5], "prefill_items": v32[6], "counts": v32[7][:3],
             "positions": v64[0][:tokens], "write_slots": v64[1][:tokens], "logit_store": v64[2],
             "logit_indices": v64[2][:logits],
         }

@@ -70,7 +70,9 @@ HB_API int hb_device_status(uint32_t* status, int clear);
  * partial base, splits) for rows with count <= decode_max_tokens, split every
  * split_keys keys, prefill_items int32 [prefill_capacity][3] (row, start of query
  * tile 2i, start of tile 2i+1 or -1) pairing adjacent tiles of prefill_tile_tokens
- * queries of a row. Entries past a capacity are not written.
+ * queries of a row. Entries past a capacity are not written. counts (device int32[3],
+ * may be null) receives the number of decode items and prefill pairs written (capped at
+ * their capacities) and the partial records the decode items need.
  */
 HB_API int hb_tick_pack(const int32_t* rows, int32_t num_rows, const int32_t* updates, int32_t num_updates,
                         int32_t* arena, int32_t arena_slots, int32_t arena_width, int32_t page_size, int32_t width,
@@ -79,7 +81,7 @@ HB_API int hb_tick_pack(const int32_t* rows, int32_t num_rows, const int32_t* up
                         int32_t* seqused_k, int64_t* positions, int64_t* write_slots, int32_t* token_row,
                         int64_t* logit_indices, int32_t logit_capacity, int32_t* decode_items,
                         int32_t decode_capacity, int32_t* prefill_items, int32_t prefill_capacity,
-                        cudaStream_t stream);
+                        int32_t* counts, cudaStream_t stream);
 
 /*
  * (b) Fused per-head q/k RMSNorm + RoPE + paged KV append. Replaces, in
@@ -110,15 +112,19 @@ HB_API size_t hb_attention_workspace_bytes(int32_t partial_records, int32_t head
  * paged_cache.py:521-546. q and out are [total_tokens][heads][head_dim]; the
  * pools [num_pages][page_size][kv_heads][head_dim]. Work items come from
  * hb_tick_pack: decode items run split-K (partials in `workspace`, merged by a
- * combine launch), prefill items run on tcgen05 tensor cores.
+ * combine launch), prefill items run on tcgen05 tensor cores. With counts null the
+ * launch covers exactly num_decode_items / num_prefill_items. With counts (device, the
+ * array hb_tick_pack filled) those two arguments and partial_records are capacities: the
+ * grids are sized to them and the kernels read the real numbers from counts, so one
+ * launch (for instance inside a CUDA graph) serves every tick within the capacities.
  */
 HB_API int hb_paged_attention(const void* q, const void* key_pool, const void* value_pool, int64_t num_pages,
                               int32_t page_size, const int32_t* block_table, int32_t width, const int32_t* cu_seq_q,
                               const int32_t* seqused_k, const int32_t* decode_items, int32_t num_decode_items,
-                              const int32_t* prefill_items, int32_t num_prefill_items, int32_t partial_records,
-                              int32_t split_keys, int32_t total_tokens, int32_t heads, int32_t kv_heads,
-                              int32_t head_dim, float scale, void* workspace, size_t workspace_bytes, void* out,
-                              cudaStream_t stream);
+                              const int32_t* prefill_items, int32_t num_prefill_items, const int32_t* counts,
+                              int32_t partial_records, int32_t split_keys, int32_t total_tokens, int32_t heads,
+                              int32_t kv_heads, int32_t head_dim, float scale, void* workspace,
+                              size_t workspace_bytes, void* out, cudaStream_t stream);
 
 /*
  * Paged attention with a built-in workspace (no counterpart in the reference).
@@ -141,9 +147,9 @@ HB_API int hb_paged_attention_static_workspace(const void* q, const void* key_po
                                                int32_t width, const int32_t* cu_seq_q, const int32_t* seqused_k,
                                                const int32_t* decode_items, int32_t num_decode_items,
                                                const int32_t* prefill_items, int32_t num_prefill_items,
-                                               int32_t partial_records, int32_t split_keys, int32_t total_tokens,
-                                               int32_t heads, int32_t kv_heads, int32_t head_dim, float scale,
-                                               void* out, cudaStream_t stream);
+                                               const int32_t* counts, int32_t partial_records, int32_t split_keys,
+                                               int32_t total_tokens, int32_t heads, int32_t kv_heads,
+                                               int32_t head_dim, float scale, void* out, cudaStream_t stream);
 
 /*
  * Hidden-size RMSNorm (RMSNorm.forward, src/helios/runtime/qwen3/layers.py:36-40).
