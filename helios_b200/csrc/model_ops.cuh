@@ -193,7 +193,10 @@ __global__ void __launch_bounds__(kSwigluThreads) swiglu_kernel(SwigluParams p) 
         unpack8(u_raw[k], u);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float sl = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(g[e], __fadd_rn(1.f, expf(-g[e])))));
+          // silu(g) = g / (1 + e^-g) in fp32 with the fast exp and divide intrinsics
+          // (fp32 error far below the bf16 rounding that follows; e^-g = inf gives -0,
+          // as the exact quotient does), rounded to bf16, then times up, rounded.
+          const float sl = __bfloat162float(__float2bfloat16_rn(__fdividef(g[e], 1.f + __expf(-g[e]))));
           o[e] = __fmul_rn(sl, u[e]);
         }
         out[c] = pack8(o);

@@ -84,13 +84,17 @@ __global__ void __launch_bounds__(kRopeThreads, 4) norm_rope_append_kernel(NormR
       }
       raw[i] = *reinterpret_cast<const uint4*>(src + 8 * j);
     }
+    // cos and the signed sin of this lane's 8 elements: rot(x) = (-x2, x1), so the
+    // first half multiplies its partner by -sin (negation is exact).
     float cs[8], sn[8];
     if (p.cos != nullptr && pos_ok) {
       const float4* c4 = reinterpret_cast<const float4*>(p.cos + pos * D + 8 * j);
       const float4* s4 = reinterpret_cast<const float4*>(p.sin + pos * D + 8 * j);
       const float4 c0 = c4[0], c1 = c4[1], s0 = s4[0], s1 = s4[1];
+      const float sg = j < kLanes / 2 ? -1.f : 1.f;
       cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w; cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
-      sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+      sn[0] = sg * s0.x; sn[1] = sg * s0.y; sn[2] = sg * s0.z; sn[3] = sg * s0.w;
+      sn[4] = sg * s1.x; sn[5] = sg * s1.y; sn[6] = sg * s1.z; sn[7] = sg * s1.w;
     }
 #pragma unroll
     for (int i = 0; i < kRopeMaxRows; ++i) {
@@ -119,13 +123,19 @@ __global__ void __launch_bounds__(kRopeThreads, 4) norm_rope_append_kernel(NormR
         for (int e = 0; e < 8; ++e) x[e] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[e], inv), g[e])));
       }
       if (p.cos != nullptr) {  // fl(fl(x cos) + fl(rot(x) sin)), rot(x) = (-x2, x1)
-        const bool first_half = j < kLanes / 2;
+        // x holds bf16 values here (the rounded norm, or the raw input), so the partner
+        // lane's 8 values travel as 4 packed bf16 pairs, exactly.
+        const uint4 mine = pack8(x);
+        uint4 other;
+        other.x = __shfl_xor_sync(row_mask, mine.x, kLanes / 2);
+        other.y = __shfl_xor_sync(row_mask, mine.y, kLanes / 2);
+        other.z = __shfl_xor_sync(row_mask, mine.z, kLanes / 2);
+        other.w = __shfl_xor_sync(row_mask, mine.w, kLanes / 2);
+        float partner[8];
+        unpack8(other, partner);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float partner = __shfl_xor_sync(row_mask, x[e], kLanes / 2);
-          const float rot = first_half ? -partner : partner;
-          x[e] = __bfloat162float(__float2bfloat16_rn(__fadd_rn(__fmul_rn(x[e], cs[e]), __fmul_rn(rot, sn[e]))));
-        }
+        for (int e = 0; e < 8; ++e)
+          x[e] = __bfloat162float(__float2bfloat16_rn(__fadd_rn(__fmul_rn(x[e], cs[e]), __fmul_rn(partner[e], sn[e]))));
       }
       __nv_bfloat16* dst = is_q ? p.q_out + (static_cast<int64_t>(t) * p.heads + hr) * D
                                 : p.key_pool + (slot * p.kv_heads + (hr - p.heads)) * D;
