@@ -264,6 +264,17 @@ def time_steps(step, steps: int, device: torch.device) -> float:
     return start.elapsed_time(end) / 1000.0
 
 
+def measured_traffic(kernel: str) -> int | None:
+    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu capture of the
+    same workload (profiles/roofline_traffic.json), or None when there is none."""
+    path = ROOT / "profiles" / "roofline_traffic.json"
+    try:
+        entry = json.loads(path.read_text())[kernel]
+        return int(entry["dram_bytes_read_per_launch"]) + int(entry["dram_bytes_write_per_launch"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
 def decode_attention_roofline(device: torch.device, peak_gbs: float, iters: int = 20) -> dict:
     """BASELINE config 2 through the C ABI: 64 rows x 1 query, contexts U[512, 8192], 4096 pages."""
     from helios_b200 import ops
@@ -303,7 +314,7 @@ def decode_attention_roofline(device: torch.device, peak_gbs: float, iters: int 
     io_bytes = 2 * 64 * 32 * 128 * 2 + 64 * batch.block_table.shape[1] * 4
     achieved = (kv_bytes + io_bytes) / seconds / 1e9
     info = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
-            "frac": round(achieved / peak_gbs, 4), "traffic": None,
+            "frac": round(achieved / peak_gbs, 4), "traffic": measured_traffic("decode_attention_kernel"),
             "kernel": "decode_attention_kernel (+ decode_combine_kernel), hb_paged_attention on decode rows",
             "workload": "BASELINE config 2: 64 rows x 1 query, context U[512,8192], 32/8 heads, d=128, 4096 pages",
             "algorithmic_bytes_per_call": kv_bytes + io_bytes, "us_per_call": round(seconds * 1e6, 2),

@@ -128,13 +128,18 @@ __global__ void __launch_bounds__(kNormWarps * 32) rmsnorm_warp_kernel(RowNormPa
   for (int i = 0; i < MAXV; ++i) {
     const int vi = lane + 32 * i;
     if (vi < nvec) {
-      unpack8(raw[i], v[i]);
-      if (yr) {
-        float w[8];
+      if (yr) {  // residual sum rounded to bf16 (one cvt per pair), stored, then reused as floats
+        float a[8], w[8];
+        unpack8(raw[i], a);
         unpack8(raw_y[i], w);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[i][e] = __bfloat162float(__float2bfloat16_rn(__fadd_rn(v[i][e], w[e])));
-        reinterpret_cast<uint4*>(p.sum_out + static_cast<int64_t>(r) * p.hidden)[vi] = pack8(v[i]);
+        const uint4 sum = make_uint4(pack_bf16(__fadd_rn(a[0], w[0]), __fadd_rn(a[1], w[1])),
+                                     pack_bf16(__fadd_rn(a[2], w[2]), __fadd_rn(a[3], w[3])),
+                                     pack_bf16(__fadd_rn(a[4], w[4]), __fadd_rn(a[5], w[5])),
+                                     pack_bf16(__fadd_rn(a[6], w[6]), __fadd_rn(a[7], w[7])));
+        reinterpret_cast<uint4*>(p.sum_out + static_cast<int64_t>(r) * p.hidden)[vi] = sum;
+        unpack8(sum, v[i]);
+      } else {
+        unpack8(raw[i], v[i]);
       }
 #pragma unroll
       for (int e = 0; e < 8; ++e) ss = __fmaf_rn(v[i][e], v[i][e], ss);

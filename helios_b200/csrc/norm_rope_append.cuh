@@ -106,40 +106,48 @@ __global__ void __launch_bounds__(kRopeThreads, 4) norm_rope_append_kernel(NormR
       }
       const bool is_q = hr < p.heads;
       if (is_q ? (p.q_out == nullptr || !pos_ok) : (!slot_ok || !pos_ok)) continue;
-      float x[8];
-      unpack8(raw[i], x);
+      // Every rounding point yields bf16 values, kept packed (one cvt.bf16x2 per pair) and
+      // unpacked only where fp32 arithmetic follows.
+      uint4 y = raw[i];
       const float* scale = is_q ? p.q_scale : p.k_scale;
-      if (scale != nullptr) {  // RMSNorm over the row (fp32), rounded to bf16
+      if (scale != nullptr) {  // RMSNorm over the row (fp32): bf16(fl(fl(x * inv) * scale))
+        float x[8];
+        unpack8(raw[i], x);
         float ss = 0.f;
 #pragma unroll
         for (int e = 0; e < 8; ++e) ss = __fmaf_rn(x[e], x[e], ss);
 #pragma unroll
         for (int o = kLanes / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(row_mask, ss, o);
-        const float inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), p.eps));
+        // mean = ss / D: D is a power of two, so the product by 1 / D is the exact quotient.
+        const float inv = rsqrtf(__fadd_rn(ss * (1.f / static_cast<float>(D)), p.eps));
         const float4 g0 = reinterpret_cast<const float4*>(scale + 8 * j)[0];
         const float4 g1 = reinterpret_cast<const float4*>(scale + 8 * j)[1];
-        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-#pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(x[e], inv), g[e])));
+        y.x = pack_bf16(__fmul_rn(__fmul_rn(x[0], inv), g0.x), __fmul_rn(__fmul_rn(x[1], inv), g0.y));
+        y.y = pack_bf16(__fmul_rn(__fmul_rn(x[2], inv), g0.z), __fmul_rn(__fmul_rn(x[3], inv), g0.w));
+        y.z = pack_bf16(__fmul_rn(__fmul_rn(x[4], inv), g1.x), __fmul_rn(__fmul_rn(x[5], inv), g1.y));
+        y.w = pack_bf16(__fmul_rn(__fmul_rn(x[6], inv), g1.z), __fmul_rn(__fmul_rn(x[7], inv), g1.w));
       }
-      if (p.cos != nullptr) {  // fl(fl(x cos) + fl(rot(x) sin)), rot(x) = (-x2, x1)
-        // x holds bf16 values here (the rounded norm, or the raw input), so the partner
-        // lane's 8 values travel as 4 packed bf16 pairs, exactly.
-        const uint4 mine = pack8(x);
-        uint4 other;
-        other.x = __shfl_xor_sync(row_mask, mine.x, kLanes / 2);
-        other.y = __shfl_xor_sync(row_mask, mine.y, kLanes / 2);
-        other.z = __shfl_xor_sync(row_mask, mine.z, kLanes / 2);
-        other.w = __shfl_xor_sync(row_mask, mine.w, kLanes / 2);
-        float partner[8];
-        unpack8(other, partner);
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          x[e] = __bfloat162float(__float2bfloat16_rn(__fadd_rn(__fmul_rn(x[e], cs[e]), __fmul_rn(partner[e], sn[e]))));
+      if (p.cos != nullptr) {  // bf16(fl(fl(y cos) + fl(rot(y) sin))), rot(y) = (-y2, y1)
+        uint4 other;  // the partner lane's 8 values, D/2 elements away
+        other.x = __shfl_xor_sync(row_mask, y.x, kLanes / 2);
+        other.y = __shfl_xor_sync(row_mask, y.y, kLanes / 2);
+        other.z = __shfl_xor_sync(row_mask, y.z, kLanes / 2);
+        other.w = __shfl_xor_sync(row_mask, y.w, kLanes / 2);
+        float v[8], w[8];
+        unpack8(y, v);
+        unpack8(other, w);
+        y.x = pack_bf16(__fadd_rn(__fmul_rn(v[0], cs[0]), __fmul_rn(w[0], sn[0])),
+                        __fadd_rn(__fmul_rn(v[1], cs[1]), __fmul_rn(w[1], sn[1])));
+        y.y = pack_bf16(__fadd_rn(__fmul_rn(v[2], cs[2]), __fmul_rn(w[2], sn[2])),
+                        __fadd_rn(__fmul_rn(v[3], cs[3]), __fmul_rn(w[3], sn[3])));
+        y.z = pack_bf16(__fadd_rn(__fmul_rn(v[4], cs[4]), __fmul_rn(w[4], sn[4])),
+                        __fadd_rn(__fmul_rn(v[5], cs[5]), __fmul_rn(w[5], sn[5])));
+        y.w = pack_bf16(__fadd_rn(__fmul_rn(v[6], cs[6]), __fmul_rn(w[6], sn[6])),
+                        __fadd_rn(__fmul_rn(v[7], cs[7]), __fmul_rn(w[7], sn[7])));
       }
       __nv_bfloat16* dst = is_q ? p.q_out + (static_cast<int64_t>(t) * p.heads + hr) * D
                                 : p.key_pool + (slot * p.kv_heads + (hr - p.heads)) * D;
-      *reinterpret_cast<uint4*>(dst + 8 * j) = pack8(x);
+      *reinterpret_cast<uint4*>(dst + 8 * j) = y;
     }
   }
 }
