@@ -1,0 +1,148 @@
+"""Kernel microbenchmarks at the BASELINE config-3 tick shapes, timed from CUDA-graph replays.
+
+    python -m helios_b200.microbench [norm_rope] [swiglu] [add_rmsnorm] [prefill] [decode] [mixed]
+
+Each case captures 24 calls of one entry point into a CUDA graph, cycling over input sets
+whose total exceeds the 126 MB L2 where the kernel is memory-bound, and prints the median
+per-call time of five replays with the algorithmic bytes moved (one read of every input,
+one write of every output). Shapes: 2080 tokens, hidden 2560, 32 query / 8 KV heads,
+d = 128, inter 9728; attention cases are the config-3 halves (one 2048-token prefill row;
+32 decode rows with contexts U[1024, 4096]) on 256-token pages.
+"""
+
+from __future__ import annotations
+
+import math
+import sys
+
+import torch
+
+from helios_b200 import _native, ops
+from helios_b200.config import Qwen3Config
+from helios_b200.paged_cache import KVPagePool, PackedBatchCache, PagedKVCache
+
+T, H, HKV, D, HIDDEN, INTER = 2080, 32, 8, 128, 2560, 9728
+
+
+def graph_time(calls, reps: int = 24, replays: int = 5) -> float:
+    """Median microseconds per call over `replays` replays of a graph of `reps` calls."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for call in calls:
+            call()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(reps):
+            calls[i % len(calls)]()
+    graph.replay()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(replays):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        graph.replay()
+        end.record()
+        torch.cuda.synchronize()
+        times.append(start.elapsed_time(end) * 1e3 / reps)
+    return sorted(times)[len(times) // 2]
+
+
+def _norm_rope(dev, g):
+    cos, sin = torch.randn(40960, D, device=dev), torch.randn(40960, D, device=dev)
+    qs, ks = torch.rand(D, device=dev) + 0.5, torch.rand(D, device=dev) + 0.5
+    pages = 600
+
+    def make():
+        qkv = torch.randn(T, (H + 2 * HKV) * D, device=dev, generator=g).to(torch.bfloat16)
+        q = qkv[:, :H * D].view(T, H, D)
+        k = qkv[:, H * D:(H + HKV) * D].view(T, HKV, D)
+        v = qkv[:, (H + HKV) * D:].view(T, HKV, D)
+        kp = torch.zeros(pages, 256, HKV, D, dtype=torch.bfloat16, device=dev)
+        vp = torch.zeros_like(kp)
+        slots = torch.randperm(pages * 256, device=dev, generator=g)[:T].long()
+        pos = torch.randint(0, 4096, (T,), device=dev, generator=g).long()
+        qo = torch.empty(T, H, D, dtype=torch.bfloat16, device=dev)
+        return lambda: ops.qk_norm_rope_append(q, k, v, q_scale=qs, k_scale=ks, eps=1e-6, cos=cos, sin=sin,
+                                               positions=pos, write_slots=slots, q_out=qo, key_pool=kp,
+                                               value_pool=vp)
+
+    return [make() for _ in range(4)], T * (H + 2 * HKV) * D * 2 * 2
+
+
+def _swiglu(dev, g):
+    def make():
+        gu = torch.randn(T, 2 * INTER, device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty(T, INTER, dtype=torch.bfloat16, device=dev)
+        return lambda: ops.swiglu(gu, out)
+
+    return [make() for _ in range(4)], T * INTER * 3 * 2
+
+
+def _add_rmsnorm(dev, g):
+    scale = torch.rand(HIDDEN, device=dev) + 0.5
+
+    def make():
+        x = torch.randn(T, HIDDEN, device=dev, generator=g).to(torch.bfloat16)
+        y = torch.randn_like(x)
+        s, n = torch.empty_like(x), torch.empty_like(x)
+        return lambda: ops.add_rmsnorm(x, y, scale, 1e-6, s, n)
+
+    return [make() for _ in range(8)], T * HIDDEN * 2 * 4
+
+
+def _attention(dev, lengths, counts, sets):
+    cfg = Qwen3Config(n_layers=1, context_length=8192)
+    calls, kv_bytes = [], sum(l + c for l, c in zip(lengths, counts)) * HKV * D * 2 * 2
+    for seed in range(sets):
+        g = torch.Generator().manual_seed(seed)
+        pages = sum(math.ceil((l + c) / 256) for l, c in zip(lengths, counts)) + 4
+        pool = KVPagePool(cfg, pages, device=dev)
+        pool.storage.normal_(0.0, 0.3)
+        pool._free = list(reversed(torch.randperm(pages, generator=g).tolist()))  # pages in random order
+        caches = []
+        for length, count in zip(lengths, counts):
+            cache = PagedKVCache(pool, length + count + 8)
+            cache.pages.extend(pool.acquire(math.ceil(length / 256)))
+            cache.length = length
+            caches.append(cache)
+        batch = PackedBatchCache(caches)
+        batch.prepare_packed(counts)
+        q = torch.randn(sum(counts), H, D, device=dev).to(torch.bfloat16)
+        out = torch.empty_like(q)
+        calls.append((lambda q=q, pool=pool, batch=batch, out=out, caches=caches:
+                      ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out)))
+    return calls, kv_bytes
+
+
+def main(argv: list[str]) -> None:
+    if not torch.cuda.is_available():
+        raise SystemExit("the microbenchmarks need a CUDA device")
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    rng = torch.Generator().manual_seed(3)
+    decode_lengths = torch.randint(1024, 4097, (32,), generator=rng).tolist()
+    cases = {
+        "norm_rope": lambda: _norm_rope(dev, g),
+        "swiglu": lambda: _swiglu(dev, g),
+        "add_rmsnorm": lambda: _add_rmsnorm(dev, g),
+        "prefill": lambda: _attention(dev, [0], [2048], 1),
+        "decode": lambda: _attention(dev, decode_lengths, [1] * 32, 2),
+        "mixed": lambda: _attention(dev, decode_lengths + [0], [1] * 32 + [2048], 2),
+    }
+    for name in argv or list(cases):
+        calls, nbytes = cases[name]()
+        with torch.inference_mode():
+            us = graph_time(calls)
+        print(f"{name:12s} {us:8.2f} us/call   {nbytes / 1e6:8.1f} MB   {nbytes / us / 1e3:8.1f} GB/s", flush=True)
+        del calls
+        torch.cuda.empty_cache()
+    status = _native.device_status()
+    if status:
+        raise SystemExit(f"device status: {_native.describe_status(status)}")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1:])
