@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_kernel(RowNormParams p) {
 
 // Warp-per-row variant for hidden <= 32 * 8 * MAXV: every lane issues all of its
 // 16-byte loads before reducing, and the reduction stays inside the warp.
-constexpr int kNormWarps = 8;
+constexpr int kNormWarps = 4;  // rows (warps) per CTA: small CTAs spread 2080 rows evenly over the SMs
 
 template <int MAXV>
 __global__ void __launch_bounds__(kNormWarps * 32) rmsnorm_warp_kernel(RowNormParams p) {
