@@ -55,6 +55,7 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "hb_embedding": (c_int, [P, P, I64, P, I64, I32, P]),
     "hb_page_copy": (c_int, [P, I64, I32, I64, I64, P, P, I32, P]),
     "hb_sample": (c_int, [P, I64, I32, I32, P, P, P, P, P]),
+    "hb_verify_drafts": (c_int, [P, P, P, P, I32, P, P, P]),
 }
 
 

@@ -442,4 +442,18 @@ int hb_sample(const void* logits, int64_t row_stride, int32_t rows, int32_t voca
   return check_launch("sample_kernel");
 }
 
+int hb_verify_drafts(const int64_t* tokens, const int32_t* cu_seq_q, const int32_t* logit_offsets,
+                     const int64_t* predictions, int32_t rows, int32_t* accepted, int64_t* emitted,
+                     cudaStream_t stream) {
+  if (rows < 0 || rows > HB_MAX_TICK_ROWS) return fail(HB_ERR_INVALID, "rows %d outside [0, %d]", rows, HB_MAX_TICK_ROWS);
+  if (rows == 0) return HB_OK;
+  if (tokens == nullptr || cu_seq_q == nullptr || logit_offsets == nullptr || predictions == nullptr ||
+      accepted == nullptr || emitted == nullptr)
+    return fail(HB_ERR_INVALID, "null verification pointer");
+  hb::VerifyParams p{tokens, cu_seq_q, logit_offsets, predictions, rows, accepted, emitted};
+  const unsigned blocks = static_cast<unsigned>((rows + hb::kVerifyThreads - 1) / hb::kVerifyThreads);
+  hb::verify_drafts_kernel<<<blocks, hb::kVerifyThreads, 0, stream>>>(p);
+  return check_launch("verify_drafts_kernel");
+}
+
 }  // extern "C"

@@ -242,3 +242,41 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) 
 }
 
 }  // namespace hb
+
+namespace hb {
+
+// Speculative verification of drafted rows (the acceptance loop of Engine._execute_batch,
+// src/helios/runtime/engine.py:507-520). A row whose logit rows are its trailing lc
+// tokens has prediction i (the greedy id after token count - lc + i) compared with the
+// row's next token; the drafts accepted are the longest matching prefix, and the row
+// emits predictions 0 .. accepted. A row with one logit row emits its prediction.
+struct VerifyParams {
+  const int64_t* tokens;         // [T] the tick's token ids, rows packed by cu_seq_q
+  const int32_t* cu_seq_q;       // [B+1]
+  const int32_t* logit_offsets;  // [B+1] first logit row of each row
+  const int64_t* predictions;    // [logit rows] one id per logit row
+  int32_t rows;
+  int32_t* accepted;             // [B]
+  int64_t* emitted;              // [logit rows]: row r writes logit_offsets[r] .. + accepted[r]
+};
+
+constexpr int kVerifyThreads = 128;
+
+__global__ void __launch_bounds__(kVerifyThreads) verify_drafts_kernel(VerifyParams p) {
+  const int r = blockIdx.x * kVerifyThreads + threadIdx.x;
+  if (r >= p.rows) return;
+  const int q0 = p.cu_seq_q[r], count = p.cu_seq_q[r + 1] - q0;
+  const int l0 = p.logit_offsets[r], lc = p.logit_offsets[r + 1] - l0;
+  if (lc < 1 || lc > count) {  // logit rows must be trailing tokens of the row
+    raise_status(kStatusBadRow);
+    p.accepted[r] = 0;
+    return;
+  }
+  const int first = q0 + count - lc;  // token whose prediction is logit row l0
+  int accepted = 0;
+  while (accepted < lc - 1 && p.tokens[first + accepted + 1] == p.predictions[l0 + accepted]) ++accepted;
+  for (int i = 0; i <= accepted; ++i) p.emitted[l0 + i] = p.predictions[l0 + i];
+  p.accepted[r] = accepted;
+}
+
+}  // namespace hb

@@ -9,12 +9,14 @@ uniform per row is drawn on the device (no host synchronisation).
 
 ``sample_rows`` is the batched sampling of ``Engine._execute_batch``
 (src/helios/runtime/engine.py:470-492): per-row temperature and top-p in one
-launch instead of grouping rows by equal settings.
+launch instead of grouping rows by equal settings. ``sample_and_verify`` adds the
+speculative verification of drafted rows (engine.py:488-520) on the device.
 """
 
 from __future__ import annotations
 
 from collections.abc import Sequence
+from itertools import accumulate
 
 import torch
 
@@ -99,3 +101,52 @@ def sample_rows(logits: torch.Tensor, samplings: Sequence[Sampling], *, uniforms
     if logits.dtype != torch.bfloat16:
         logits = logits.to(torch.bfloat16)
     return ops.sample(logits, settings[:, 0].contiguous(), settings[:, 1].contiguous(), uniforms.contiguous())
+
+
+_GREEDY = Sampling(max_new_tokens=1, temperature=0.0, top_p=1.0)
+
+
+def sample_and_verify(logits: torch.Tensor, chunks: Sequence[Sequence[int]], logit_counts: Sequence[int],
+                      samplings: Sequence[Sampling], *, caches: Sequence[PagedKVCache] | None = None,
+                      cache_lengths: Sequence[int] | None = None,
+                      uniforms: torch.Tensor | None = None) -> list[list[int]]:
+    """Tokens each row of a packed tick emits, with speculative drafts verified on the device.
+
+    ``logits [sum(logit_counts), V]`` come from ``Decoder.packed_caches(..., logit_counts=...)``.
+    As in Engine._execute_batch (src/helios/runtime/engine.py:466-520): every row's head
+    (its first logit row) is drawn with the row's sampling; the other logit rows of a
+    drafted row get their greedy ids (drafts are only proposed for temperature-0 requests,
+    engine.py:380); a drafted row accepts the longest prefix of its drafts (its chunk after
+    the pending token) matching those ids and emits ids 0 .. accepted. Sampling,
+    verification and the emitted tokens stay on the device; one transfer brings back the
+    accepted counts and tokens. With ``caches`` and their ``cache_lengths`` from before the
+    tick, each drafted row's cache is truncated to ``length + 1 + accepted`` (engine.py:515).
+    """
+    rows = len(chunks)
+    if len(logit_counts) != rows or len(samplings) != rows:
+        raise ValueError("Each chunk needs its logit count and sampling settings.")
+    if any(not 1 <= lc <= len(chunk) for chunk, lc in zip(chunks, logit_counts, strict=True)):
+        raise ValueError("Logit rows must be 1 through each chunk length.")
+    starts = list(accumulate(logit_counts, initial=0))
+    if logits.shape[0] != starts[-1]:
+        raise ValueError("Logits must hold one row per logit count.")
+    per_row = []
+    for sampling, lc in zip(samplings, logit_counts, strict=True):
+        per_row.append(sampling)
+        per_row.extend([_GREEDY] * (lc - 1))
+    device = logits.device
+    predictions = sample_rows(logits, per_row, uniforms=uniforms)
+    tokens = torch.tensor([t for chunk in chunks for t in chunk], dtype=torch.long).to(device)
+    cu = torch.tensor(list(accumulate((len(c) for c in chunks), initial=0)), dtype=torch.int32).to(device)
+    offsets = torch.tensor(starts, dtype=torch.int32).to(device)
+    accepted, emitted = ops.verify_drafts(tokens, cu, offsets, predictions)
+    host = torch.cat([accepted.long(), emitted]).cpu().tolist()  # the tick's one device->host transfer
+    counts, flat = host[:rows], host[rows:]
+    out = []
+    for row in range(rows):
+        out.append(flat[starts[row]: starts[row] + counts[row] + 1])
+        if caches is not None and logit_counts[row] > 1:
+            if cache_lengths is None:
+                raise ValueError("Truncating drafted rows needs their cache lengths before the tick.")
+            caches[row].truncate(cache_lengths[row] + 1 + counts[row])
+    return out

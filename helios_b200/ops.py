@@ -186,3 +186,24 @@ def sample(logits: torch.Tensor, temperature: torch.Tensor, top_p: torch.Tensor,
                          uniforms.data_ptr(), out.data_ptr(), _stream(logits.device))
     _native.check(rc, "hb_sample")
     return out
+
+
+def verify_drafts(tokens: torch.Tensor, cu_seq_q: torch.Tensor, logit_offsets: torch.Tensor,
+                  predictions: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Speculative verification on the device: ``(accepted [B] int32, emitted [logit rows]
+    int64)``; row r's emitted tokens are ``emitted[logit_offsets[r] : logit_offsets[r] +
+    accepted[r] + 1]`` (engine.py:507-520)."""
+    _need(tokens, torch.long, "tokens")
+    _need(cu_seq_q, torch.int32, "cu_seq_q")
+    _need(logit_offsets, torch.int32, "logit_offsets")
+    _need(predictions, torch.long, "predictions")
+    rows = cu_seq_q.numel() - 1
+    if logit_offsets.numel() != rows + 1:
+        raise ValueError("logit_offsets needs one entry per row plus one")
+    accepted = torch.empty(rows, dtype=torch.int32, device=tokens.device)
+    emitted = torch.zeros(predictions.numel(), dtype=torch.long, device=tokens.device)
+    rc = lib().hb_verify_drafts(tokens.data_ptr(), cu_seq_q.data_ptr(), logit_offsets.data_ptr(),
+                                predictions.data_ptr(), rows, accepted.data_ptr(), emitted.data_ptr(),
+                                _stream(tokens.device))
+    _native.check(rc, "hb_verify_drafts")
+    return accepted, emitted

@@ -192,6 +192,21 @@ HB_API int hb_page_copy(void* pool_base, int64_t tensor_stride_bytes, int32_t te
 HB_API int hb_sample(const void* logits, int64_t row_stride, int32_t rows, int32_t vocab, const float* temperature,
                      const float* top_p, const float* uniforms, int64_t* out_ids, cudaStream_t stream);
 
+/*
+ * Speculative verification of drafted rows. Replaces the acceptance loop of
+ * Engine._execute_batch (src/helios/runtime/engine.py:507-520), which copies every logit
+ * row's argmax to the host and compares there. Row r of the tick holds tokens
+ * tokens[cu_seq_q[r] .. cu_seq_q[r+1]) and logit rows logit_offsets[r] .. logit_offsets[r+1]
+ * (its trailing tokens); predictions holds one id per logit row (the greedy id, e.g. from
+ * hb_sample with temperature 0). accepted[r] = the longest prefix of the row's drafted
+ * tokens (its tokens after the first logit row) equal to its predictions; emitted receives
+ * predictions logit_offsets[r] .. + accepted[r] (the tokens the row produces). A row with
+ * one logit row accepts 0 and emits its prediction. All pointers are device memory.
+ */
+HB_API int hb_verify_drafts(const int64_t* tokens, const int32_t* cu_seq_q, const int32_t* logit_offsets,
+                            const int64_t* predictions, int32_t rows, int32_t* accepted, int64_t* emitted,
+                            cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
