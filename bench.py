@@ -275,6 +275,42 @@ def measured_traffic(kernel: str) -> int | None:
         return None
 
 
+def prefill_attention_roofline(device: torch.device, peak_tflops: float, iters: int = 20) -> dict:
+    """The prefill half of BASELINE config 3 through the C ABI: one 2048-token row at offset 0,
+    32/8 heads, d=128 (tensor-bound). Algorithmic FLOPs per call: 4 * H * d * causal keys."""
+    from helios_b200 import ops
+    from helios_b200.config import Qwen3Config
+    from helios_b200.paged_cache import KVPagePool, PackedBatchCache, PagedKVCache
+
+    cfg = Qwen3Config(n_layers=1, context_length=PREFILL + 64)
+    pool = KVPagePool(cfg, math.ceil(PREFILL / 256) + 1, device=device)
+    gen = torch.Generator(device=device).manual_seed(2)
+    pool.storage.normal_(0.0, 0.3, generator=gen)
+    batch = PackedBatchCache([PagedKVCache(pool, PREFILL)])
+    with torch.inference_mode():
+        batch.prepare_packed([PREFILL])
+        q = torch.randn(PREFILL, cfg.n_heads, cfg.head_dim, device=device, generator=gen).to(torch.bfloat16)
+        out = torch.empty_like(q)
+        for _ in range(3):
+            ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out)
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(iters):
+            ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out)
+        end.record()
+        torch.cuda.synchronize(device)
+    seconds = start.elapsed_time(end) / 1000.0 / iters
+    flops = 4 * cfg.n_heads * cfg.head_dim * (PREFILL * (PREFILL + 1) // 2)
+    achieved = flops / seconds / 1e12
+    del pool, batch
+    torch.cuda.empty_cache()
+    return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_tflops, "unit": "TFLOP/s",
+            "frac": round(achieved / peak_tflops, 4), "kernel": "prefill_attention_kernel (tcgen05/TMEM)",
+            "workload": "BASELINE config 3 prefill half: one 2048-token row at offset 0, 32/8 heads, d=128",
+            "flops_per_call": flops, "us_per_call": round(seconds * 1e6, 2)}
+
+
 def decode_attention_roofline(device: torch.device, peak_gbs: float, iters: int = 20) -> dict:
     """BASELINE config 2 through the C ABI: 64 rows x 1 query, contexts U[512, 8192], 4096 pages."""
     from helios_b200 import ops
@@ -449,8 +485,9 @@ def run_b200(args) -> None:
     del runner, model, decoder, pool, caches
     torch.cuda.empty_cache()
     roof = decode_attention_roofline(device, pk["hbm_gbs"]) if rank == 0 else None
+    prefill_roof = prefill_attention_roofline(device, pk["bf16_tflops"]) if rank == 0 else None
     if roof is not None:
-        roof["peak_kind"] = pk_kind
+        roof["peak_kind"] = prefill_roof["peak_kind"] = pk_kind
     cpu = cpu_baseline() if (rank == 0 and size == 1 and not args.no_cpu) else None
     if rank == 0:
         step_s = seconds / args.steps
@@ -460,6 +497,7 @@ def run_b200(args) -> None:
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": DATA,
             "config": workload_config(size),
             "roofline": roof,
+            "prefill_roofline": prefill_roof,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(1000 * e2e_seconds / args.steps, 3)},
@@ -477,7 +515,7 @@ def run_b200(args) -> None:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--steps", type=int, default=32)  # BASELINE config 3 times 32 consecutive ticks
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")

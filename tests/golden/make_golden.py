@@ -234,7 +234,7 @@ def bf16_tick() -> dict:
     chunks = [rand_ids(g, 1, cfg.vocab_size), rand_ids(g, 1, cfg.vocab_size), rand_ids(g, 3, cfg.vocab_size),
               rand_ids(g, 150, cfg.vocab_size), rand_ids(g, 300, cfg.vocab_size)]
     logit_counts = [1, 1, 3, 1, 1]
-    steps = 16
+    steps = 64
     pool = KVPagePool(cfg, 24, device=torch.device("cpu"))
     decoder = Decoder(model)
     decoder.page_pool = pool
@@ -247,16 +247,20 @@ def bf16_tick() -> dict:
         caches.append(PagedKVCache(pool, 300 + steps))
         logits = decoder.packed_caches(caches, chunks, logit_counts=logit_counts)
         last_rows = np.cumsum(logit_counts) - 1
-        tokens = [logits[torch.as_tensor(last_rows)].float().argmax(-1).tolist()]
+        heads = logits[torch.as_tensor(last_rows)].float()
+        tokens = [heads.argmax(-1).tolist()]
+        maxima = [heads.max(-1).values.tolist()]
         for _ in range(steps - 1):
-            out = decoder.packed_caches(caches, [[t] for t in tokens[-1]])
-            tokens.append(out.float().argmax(-1).tolist())
+            out = decoder.packed_caches(caches, [[t] for t in tokens[-1]]).float()
+            tokens.append(out.argmax(-1).tolist())
+            maxima.append(out.max(-1).values.tolist())
     return {
         "prompt_lengths": np.array(contexts), "prompts": np.concatenate([np.array(p) for p in prompts]),
         "chunk_lengths": np.array([len(c) for c in chunks]),
         "chunks": np.concatenate([np.array(c) for c in chunks]),
         "logit_counts": np.array(logit_counts),
         "logits": logits.float().numpy(), "greedy": np.array(tokens).T,
+        "greedy_max": np.array(maxima, dtype=np.float32).T,
         "page_tables": np.array([p.index for c in caches for p in c.pages]),
         "page_counts": np.array([len(c.pages) for c in caches]),
     }

@@ -2,7 +2,7 @@
 
 ``tests/golden/bf16_tick.npz`` holds the reference's packed-path logits for a
 mixed tick (decode rows, a drafted row, a continued chunk and a fresh prefill)
-at the Qwen3-4B head shape, and its greedy continuation for 16 steps. The B200
+at the Qwen3-4B head shape, and its greedy continuation for 64 steps. The B200
 model loads the reference's seed-0 random-init weights (rebuilt by the oracle,
 whose weight construction the CPU suite pins against the reference), replays
 the same prompts through paged prefill ticks, and must give logits within
@@ -57,22 +57,28 @@ def test_mixed_tick_logits_and_greedy_match_reference(golden_dir):
     prompts = _split(g["prompts"].tolist(), g["prompt_lengths"].tolist())
     chunks = _split(g["chunks"].tolist(), g["chunk_lengths"].tolist())
     logit_counts = g["logit_counts"].tolist()
+    steps = g["greedy"].shape[1]
     caches = []
     for prompt in prompts:
-        cache = PagedKVCache(pool, len(prompt) + 320 + 16)
+        cache = PagedKVCache(pool, len(prompt) + 320 + steps)
         decoder.packed_caches([cache], [prompt])
         caches.append(cache)
-    caches.append(PagedKVCache(pool, 316))
+    caches.append(PagedKVCache(pool, 300 + steps))
     logits = decoder.packed_caches(caches, chunks, logit_counts=logit_counts).float().cpu()
     ref = torch.from_numpy(g["logits"])
     diff = (logits - ref).abs().max(-1).values
     assert (diff <= 2e-2 * ref.abs().max(-1).values).all(), diff
     last = np.cumsum(logit_counts) - 1
-    greedy = [logits[torch.as_tensor(last)].argmax(-1).tolist()]
-    for _ in range(15):
-        out = decoder.packed_caches(caches, [[t] for t in greedy[-1]])
-        greedy.append(out.float().argmax(-1).tolist())
+    heads = logits[torch.as_tensor(last)]
+    greedy, maxima = [heads.argmax(-1).tolist()], [heads.max(-1).values.tolist()]
+    for _ in range(steps - 1):
+        out = decoder.packed_caches(caches, [[t] for t in greedy[-1]]).float()
+        greedy.append(out.argmax(-1).tolist())
+        maxima.append(out.max(-1).values.tolist())
     assert (np.array(greedy).T == g["greedy"]).all()
+    # The winning logit of every row at every step tracks the reference's.
+    want = g["greedy_max"]
+    assert (np.abs(np.array(maxima).T - want) <= 2e-2 * np.abs(want).clip(min=1.0)).all()
     assert [p.index for c in caches for p in c.pages] == g["page_tables"].tolist()
     assert _native.device_status() == 0
 

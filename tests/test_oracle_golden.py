@@ -81,12 +81,15 @@ def _run_tick_and_greedy(config, sd, prompts, chunks, capacities, logit_counts, 
         logits = model.forward_packed([t for c in chunks for t in c], kp, vp, meta)
         req.advance(rows, counts)
         last = np.cumsum(logit_counts) - 1
-        tokens = [logits[torch.as_tensor(last)].float().argmax(-1).tolist()]
+        heads = logits[torch.as_tensor(last)].float()
+        tokens, maxima = [heads.argmax(-1).tolist()], [heads.max(-1).values.tolist()]
         for _ in range(steps - 1):
             meta = req.tick(rows, [1] * len(rows))
-            out = model.forward_packed(tokens[-1], kp, vp, meta)
+            out = model.forward_packed(tokens[-1], kp, vp, meta).float()
             req.advance(rows, [1] * len(rows))
-            tokens.append(out.float().argmax(-1).tolist())
+            tokens.append(out.argmax(-1).tolist())
+            maxima.append(out.max(-1).values.tolist())
+    _run_tick_and_greedy.maxima = np.array(maxima).T  # winning logit per row and step
     return logits, np.array(tokens).T, req, rows
 
 
@@ -111,7 +114,8 @@ def test_config1_logits_and_greedy_match_reference_dense_path(golden_dir):
 
 
 def test_bf16_mixed_tick_matches_reference_packed_path(golden_dir):
-    """bf16 mixed tick at the Qwen3-4B head shape; logits within 2e-2, greedy ids identical."""
+    """bf16 mixed tick at the Qwen3-4B head shape; logits within 2e-2, greedy ids identical
+    over the fixture's 64 steps."""
     g = np.load(golden_dir / "bf16_tick.npz")
     sd = build_state_dict(BF16, 0)
     flat = g["prompts"].tolist()
@@ -122,9 +126,10 @@ def test_bf16_mixed_tick_matches_reference_packed_path(golden_dir):
     chunks, at = [], 0
     for n in g["chunk_lengths"].tolist():
         chunks.append(flat[at:at + n]); at += n
-    caps = [n + 320 + 16 for n in g["prompt_lengths"].tolist()] + [316]
+    steps = g["greedy"].shape[1]
+    caps = [n + 320 + steps for n in g["prompt_lengths"].tolist()] + [300 + steps]
     logits, greedy, req, rows = _run_tick_and_greedy(BF16, sd, prompts, chunks, caps,
-                                                     g["logit_counts"].tolist(), 16, 24)
+                                                     g["logit_counts"].tolist(), steps, 24)
     ref = torch.from_numpy(g["logits"])
     # bf16 logits of a random-init model reach |logit| ~ 500, where one bf16 ulp is 2-4;
     # the 2e-2 bound is therefore taken relative to each row's logit scale.
@@ -132,6 +137,8 @@ def test_bf16_mixed_tick_matches_reference_packed_path(golden_dir):
     scale = ref.abs().max(-1).values
     assert (diff <= 2e-2 * scale).all(), (diff, scale)
     assert (greedy == g["greedy"]).all()
+    want = g["greedy_max"]
+    assert (np.abs(_run_tick_and_greedy.maxima - want) <= 2e-2 * np.abs(want).clip(min=1.0)).all()
     tables = [p for r in rows for p in req.tables[r]]
     assert tables == g["page_tables"].tolist()
 
