@@ -38,6 +38,11 @@ struct AttentionParams {
   // tick-pack kernel: when set, grids are sized to capacities and CTAs past a count exit
   // (a launch that stays valid, e.g. in a CUDA graph, while the work list changes).
   const int32_t* counts;
+  // Set when the prefill kernel is launched right behind the decode kernel (programmatic
+  // dependent launch): it then reads q, K and V without waiting (the decode kernel waited
+  // for them before triggering), and one of its CTAs waits for the decode grid before
+  // exiting, so the prefill grid completes after the decode grid.
+  int32_t prefill_after_decode;
   float* ws_out;   // [records, H, D]
   float* ws_lse;   // [records, H]
   int32_t width, num_pages, page_size, heads, kv_heads, split_keys, tokens;
@@ -67,6 +72,8 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_attention_kernel(Attent
   __shared__ int abort_flag;
   __shared__ float merge_ml[kDecConsumerWarps][16][2];
 
+  pdl_wait();     // q, K and V from the norm/RoPE/append kernel ahead of this one
+  pdl_trigger();  // the prefill kernel (or the split combine) may launch behind this grid
   if (p.counts != nullptr && static_cast<int>(blockIdx.x) >= p.counts[0]) return;  // past this tick's items
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
@@ -346,6 +353,7 @@ constexpr int kCombineMaxSplits = 8;
 template <int GROUP>
 __global__ void __launch_bounds__(128) decode_combine_kernel(AttentionParams p) {
   constexpr int D = 128;
+  pdl_wait();  // the kernel ahead (decode, or prefill, which completes after decode) has finished
   if (p.counts != nullptr && static_cast<int>(blockIdx.x) >= p.counts[0]) return;
   const int32_t* item = p.decode_items + 4 * blockIdx.x;
   if (item[1] != 0 || item[3] <= 1) return;

@@ -87,9 +87,20 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_flag;
 
+  // Programmatic dependent launch. Right behind the decode kernel, this grid starts while
+  // decode CTAs still run: q, K and V are complete (the decode kernel waited for them before
+  // triggering) and this kernel does not read decode output; one CTA (the last launched)
+  // waits for the decode grid before it exits, so this grid completes after it. Behind the
+  // norm/RoPE/append kernel instead, every CTA waits first.
+  if (!p.prefill_after_decode) pdl_wait();
+  pdl_trigger();
+  const bool joins_decode = blockIdx.x == 0 && blockIdx.y == gridDim.y - 1;
   // KV head fastest, items last to first: the longest query tiles of every head launch first.
   const int n_items = p.counts != nullptr ? p.counts[1] : p.num_prefill;
-  if (static_cast<int>(blockIdx.y) >= n_items) return;  // past this tick's items (capacity grid)
+  if (static_cast<int>(blockIdx.y) >= n_items) {  // past this tick's items (capacity grid)
+    if (joins_decode) pdl_wait();
+    return;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x;
   const int32_t* item = p.prefill_items + 3 * (n_items - 1 - static_cast<int>(blockIdx.y));
@@ -421,6 +432,7 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
     tc_fence_after();
     tmem_dealloc(tmem, kPreTmemCols);
   }
+  if (joins_decode) pdl_wait();
 }
 
 }  // namespace hb

@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "../../include/helios_b200.h"
 #include "attention_decode.cuh"
@@ -101,6 +102,26 @@ std::mutex g_static_ws_mutex;
 void* g_static_ws_ptr[64];
 
 int group_slot(int group) { return group == 1 ? 0 : group == 2 ? 1 : group == 4 ? 2 : 3; }
+
+// Launch with programmatic stream serialization: the kernel may start before the kernel
+// ahead of it in the stream has finished, once that one's CTAs have all triggered (the
+// kernels of this library wait with griddepcontrol.wait before reading what the kernel
+// ahead of them wrote).
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // RMSNorm launch: warp per row up to hidden 4096, CTA per row beyond.
 int launch_rmsnorm(const hb::RowNormParams& p, cudaStream_t stream, const char* what) {
@@ -203,11 +224,11 @@ int hb_qk_norm_rope_append(const void* q, int64_t q_token_stride, int64_t q_head
                        positions, write_slots, static_cast<__nv_bfloat16*>(q_out),
                        static_cast<__nv_bfloat16*>(key_pool), static_cast<__nv_bfloat16*>(value_pool), pool_slots,
                        tokens, heads, kv_heads};
-  const unsigned blocks = static_cast<unsigned>(tokens);  // one CTA per token
-  if (head_dim == 128)
-    hb::norm_rope_append_kernel<128><<<blocks, hb::kRopeThreads, 0, stream>>>(p);
-  else
-    hb::norm_rope_append_kernel<64><<<blocks, hb::kRopeThreads, 0, stream>>>(p);
+  const dim3 blocks(static_cast<unsigned>(tokens));  // one CTA per token
+  const cudaError_t e = head_dim == 128
+                            ? launch_pdl(hb::norm_rope_append_kernel<128>, blocks, dim3(hb::kRopeThreads), 0, stream, p)
+                            : launch_pdl(hb::norm_rope_append_kernel<64>, blocks, dim3(hb::kRopeThreads), 0, stream, p);
+  if (e != cudaSuccess) return fail(HB_ERR_CUDA, "norm_rope_append_kernel: %s", cudaGetErrorString(e));
   return check_launch("norm_rope_append_kernel");
 }
 
@@ -278,8 +299,30 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
   if (num_decode_items > 0 && decode_items == nullptr) return fail(HB_ERR_INVALID, "null decode items");
   if (num_prefill_items > 0 && prefill_items == nullptr) return fail(HB_ERR_INVALID, "null prefill items");
 
+  // Launch order decode -> prefill -> split combine, each behind the previous one with
+  // programmatic dependent launch: the prefill tiles start on the SMs the decode splits free
+  // (they read none of the decode output), and every completion is ordered through the
+  // kernels' grid-dependency waits (see prefill_after_decode).
+  if (num_prefill_items > 65535) return fail(HB_ERR_UNSUPPORTED, "more than 65535 prefill tile pairs in one call");
+  p.prefill_after_decode = num_decode_items > 0 ? 1 : 0;
+  if (num_decode_items > 0) {
+    const dim3 grid(num_decode_items, kv_heads);
+#define HB_DECODE(G)                                                                                           \
+  do {                                                                                                         \
+    if (int rc = ensure_smem(hb::decode_attention_kernel<G>, hb::kDecSmemBytes, g_dec_smem[gs])) return rc;    \
+    const cudaError_t e = launch_pdl(hb::decode_attention_kernel<G>, grid, dim3(hb::kDecThreads),              \
+                                     hb::kDecSmemBytes, stream, p, kmap, vmap);                               \
+    if (e != cudaSuccess) return fail(HB_ERR_CUDA, "decode_attention_kernel: %s", cudaGetErrorString(e));      \
+  } while (0)
+    switch (group) {
+      case 1: HB_DECODE(1); break;
+      case 2: HB_DECODE(2); break;
+      case 4: HB_DECODE(4); break;
+      default: HB_DECODE(8); break;
+    }
+#undef HB_DECODE
+  }
   if (num_prefill_items > 0) {
-    if (num_prefill_items > 65535) return fail(HB_ERR_UNSUPPORTED, "more than 65535 prefill tile pairs in one call");
     CUtensorMap qmap;
     const dim3 grid(kv_heads, num_prefill_items);
 #define HB_PREFILL(G)                                                                                           \
@@ -288,8 +331,9 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
                            static_cast<uint64_t>(heads) * head_dim * 2, 64, G, hb::kPreRows / G))               \
       return rc;                                                                                                \
     if (int rc = ensure_smem(hb::prefill_attention_kernel<G>, hb::kPreSmemBytes, g_pre_smem[gs])) return rc;     \
-    hb::prefill_attention_kernel<G><<<grid, hb::kPreThreads, hb::kPreSmemBytes, stream>>>(p, qmap, kmap, vmap);  \
-    if (int rc = check_launch("prefill_attention_kernel")) return rc;                                           \
+    const cudaError_t e = launch_pdl(hb::prefill_attention_kernel<G>, grid, dim3(hb::kPreThreads),              \
+                                     hb::kPreSmemBytes, stream, p, qmap, kmap, vmap);                           \
+    if (e != cudaSuccess) return fail(HB_ERR_CUDA, "prefill_attention_kernel: %s", cudaGetErrorString(e));      \
   } while (0)
     switch (group) {
       case 1: HB_PREFILL(1); break;
@@ -299,25 +343,20 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
     }
 #undef HB_PREFILL
   }
-  if (num_decode_items > 0) {
+  if (num_decode_items > 0 && partial_records > 0) {
     const dim3 grid(num_decode_items, kv_heads);
-#define HB_DECODE(G)                                                                                          \
-  do {                                                                                                        \
-    if (int rc = ensure_smem(hb::decode_attention_kernel<G>, hb::kDecSmemBytes, g_dec_smem[gs])) return rc;   \
-    hb::decode_attention_kernel<G><<<grid, hb::kDecThreads, hb::kDecSmemBytes, stream>>>(p, kmap, vmap);      \
-    if (int rc = check_launch("decode_attention_kernel")) return rc;                                          \
-    if (partial_records > 0) {                                                                                \
-      hb::decode_combine_kernel<G><<<grid, 128, 0, stream>>>(p);                                              \
-      if (int rc = check_launch("decode_combine_kernel")) return rc;                                          \
-    }                                                                                                         \
+#define HB_COMBINE(G)                                                                                          \
+  do {                                                                                                         \
+    const cudaError_t e = launch_pdl(hb::decode_combine_kernel<G>, grid, dim3(128), 0, stream, p);             \
+    if (e != cudaSuccess) return fail(HB_ERR_CUDA, "decode_combine_kernel: %s", cudaGetErrorString(e));        \
   } while (0)
     switch (group) {
-      case 1: HB_DECODE(1); break;
-      case 2: HB_DECODE(2); break;
-      case 4: HB_DECODE(4); break;
-      default: HB_DECODE(8); break;
+      case 1: HB_COMBINE(1); break;
+      case 2: HB_COMBINE(2); break;
+      case 4: HB_COMBINE(4); break;
+      default: HB_COMBINE(8); break;
     }
-#undef HB_DECODE
+#undef HB_COMBINE
   }
   return HB_OK;
 }

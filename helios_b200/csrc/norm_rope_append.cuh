@@ -61,6 +61,8 @@ __global__ void __launch_bounds__(kRopeThreads, 4) norm_rope_append_kernel(NormR
   constexpr int kLanes = D / 8;                    // lanes per head row
   constexpr int kSlots = kRopeThreads / kLanes;    // head rows handled side by side
   constexpr int kHalf = D / 2;
+  pdl_wait();     // the q|k|v projection ahead of this kernel has finished
+  pdl_trigger();  // every CTA is resident once all have passed here: the attention may launch
   const int t = blockIdx.x;
   const int j = threadIdx.x % kLanes;              // elements 4j..4j+3 and D/2+4j..D/2+4j+3
   const int slot0 = threadIdx.x / kLanes;
