@@ -52,6 +52,7 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "hb_rmsnorm": (c_int, [P, I64, P, P, F32, P, I32, I32, P]),
     "hb_add_rmsnorm": (c_int, [P, P, P, F32, P, P, I32, I32, P]),
     "hb_swiglu": (c_int, [P, P, I64, I64, P]),
+    "hb_gemm_swiglu": (c_int, [P, I32, I32, P, I32, P, P]),
     "hb_embedding": (c_int, [P, P, I64, P, I64, I32, P]),
     "hb_page_copy": (c_int, [P, I64, I32, I64, I64, P, P, I32, P]),
     "hb_sample": (c_int, [P, I64, I32, I32, P, P, P, P, P]),

@@ -14,6 +14,7 @@
 #include "../../include/helios_b200.h"
 #include "attention_decode.cuh"
 #include "attention_prefill.cuh"
+#include "gemm_swiglu.cuh"
 #include "hb_common.cuh"
 #include "model_ops.cuh"
 #include "norm_rope_append.cuh"
@@ -75,6 +76,31 @@ int encode_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint
   return HB_OK;
 }
 
+// 2-D bf16 tensor map over a row-major [rows][cols] matrix (cols contiguous, row stride
+// in bytes), 128-byte swizzle, box (box0 columns, box1 rows); rows past the end read as zeros.
+int encode_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t row_bytes, uint32_t b0,
+              uint32_t b1) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(HB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {b0, b1};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(HB_ERR_CUDA, "cuTensorMapEncodeTiled (2-D) failed (%d)", static_cast<int>(r));
+  return HB_OK;
+}
+
+int sm_count() {
+  static int count[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (count[dev] == 0) cudaDeviceGetAttribute(&count[dev], cudaDevAttrMultiProcessorCount, dev);
+  return count[dev];
+}
+
 // Per-device one-time opt-in to large dynamic shared memory.
 template <typename K>
 int ensure_smem(K kernel, int bytes, bool (&done)[64]) {
@@ -91,7 +117,7 @@ int ensure_smem(K kernel, int bytes, bool (&done)[64]) {
   return HB_OK;
 }
 
-bool g_dec_smem[4][64], g_pre_smem[4][64], g_tick_smem[64];
+bool g_dec_smem[4][64], g_pre_smem[4][64], g_tick_smem[64], g_gemm_smem[64];
 
 // Split-K workspace of hb_paged_attention_static_workspace: one fixed array per GPU,
 // for callers that cannot allocate device memory. In host code the name stands for a
@@ -479,6 +505,32 @@ int hb_sample(const void* logits, int64_t row_stride, int32_t rows, int32_t voca
                      out_ids};
   hb::sample_kernel<<<rows, hb::kSampleThreads, 0, stream>>>(p);
   return check_launch("sample_kernel");
+}
+
+int hb_gemm_swiglu(const void* x, int32_t m, int32_t k, const void* w_gate_up, int32_t inter, void* out,
+                   cudaStream_t stream) {
+  if (m < 0 || k < 1 || inter < 1) return fail(HB_ERR_INVALID, "bad GEMM sizes");
+  if (k % hb::kGemmTileK != 0 || inter % hb::kGemmTileN != 0)
+    return fail(HB_ERR_UNSUPPORTED, "gate|up GEMM needs K %% %d == 0 and intermediate %% %d == 0 (got %d, %d)",
+                hb::kGemmTileK, hb::kGemmTileN, k, inter);
+  if (m == 0) return HB_OK;
+  if (x == nullptr || w_gate_up == nullptr || out == nullptr || !aligned(x, 16) || !aligned(w_gate_up, 16) ||
+      !aligned(out, 16))
+    return fail(HB_ERR_INVALID, "gate|up GEMM pointers must be non-null and 16-byte aligned");
+  CUtensorMap amap, bmap;
+  const uint64_t row_bytes = static_cast<uint64_t>(k) * 2;
+  if (int rc = encode_2d(&amap, x, k, m, row_bytes, hb::kGemmTileK, hb::kGemmTileM)) return rc;
+  if (int rc = encode_2d(&bmap, w_gate_up, k, 2 * static_cast<uint64_t>(inter), row_bytes, hb::kGemmTileK,
+                         hb::kGemmTileN))
+    return rc;
+  hb::GemmSwigluParams p{static_cast<__nv_bfloat16*>(out), m, inter, k, (m + hb::kGemmTileM - 1) / hb::kGemmTileM,
+                         inter / hb::kGemmTileN};
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int sms = sm_count();
+  if (sms <= 0) return fail(HB_ERR_CUDA, "cannot read the SM count");
+  if (int rc = ensure_smem(hb::gemm_swiglu_kernel, hb::kGemmSmemBytes, g_gemm_smem)) return rc;
+  hb::gemm_swiglu_kernel<<<std::min(tiles, sms), hb::kGemmThreads, hb::kGemmSmemBytes, stream>>>(p, amap, bmap);
+  return check_launch("gemm_swiglu_kernel");
 }
 
 int hb_verify_drafts(const int64_t* tokens, const int32_t* cu_seq_q, const int32_t* logit_offsets,

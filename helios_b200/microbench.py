@@ -1,6 +1,7 @@
 """Kernel microbenchmarks at the BASELINE config-3 tick shapes, timed from CUDA-graph replays.
 
     python -m helios_b200.microbench [norm_rope] [swiglu] [add_rmsnorm] [prefill] [decode] [mixed]
+                                     [gate_up_fused] [gate_up_cublas]
 
 Each case captures 24 calls of one entry point into a CUDA graph, cycling over input sets
 whose total exceeds the 126 MB L2 where the kernel is memory-bound, and prints the median
@@ -93,6 +94,23 @@ def _add_rmsnorm(dev, g):
     return [make() for _ in range(8)], T * HIDDEN * 2 * 4
 
 
+def _gate_up(dev, g, fused: bool):
+    """The MLP input side: gate|up projection + SwiGLU, fused (tcgen05) or cuBLAS + swiglu kernel."""
+    import torch.nn.functional as F
+
+    w = (torch.randn(2 * INTER, HIDDEN, device=dev, generator=g) / HIDDEN ** 0.5).to(torch.bfloat16)
+
+    def make():
+        x = torch.randn(T, HIDDEN, device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty(T, INTER, dtype=torch.bfloat16, device=dev)
+        if fused:
+            return lambda: ops.gemm_swiglu(x, w, out)
+        return lambda: ops.swiglu(F.linear(x, w), out)
+
+    flops = 2 * T * HIDDEN * 2 * INTER
+    return [make() for _ in range(2)], flops
+
+
 def _attention(dev, lengths, counts, sets):
     cfg = Qwen3Config(n_layers=1, context_length=8192)
     calls, kv_bytes = [], sum(l + c for l, c in zip(lengths, counts)) * HKV * D * 2 * 2
@@ -131,12 +149,17 @@ def main(argv: list[str]) -> None:
         "prefill": lambda: _attention(dev, [0], [2048], 1),
         "decode": lambda: _attention(dev, decode_lengths, [1] * 32, 2),
         "mixed": lambda: _attention(dev, decode_lengths + [0], [1] * 32 + [2048], 2),
+        "gate_up_fused": lambda: _gate_up(dev, g, True),
+        "gate_up_cublas": lambda: _gate_up(dev, g, False),
     }
     for name in argv or list(cases):
         calls, nbytes = cases[name]()
         with torch.inference_mode():
             us = graph_time(calls)
-        print(f"{name:12s} {us:8.2f} us/call   {nbytes / 1e6:8.1f} MB   {nbytes / us / 1e3:8.1f} GB/s", flush=True)
+        if name.startswith("gate_up"):  # compute-bound: report TFLOP/s
+            print(f"{name:14s} {us:8.2f} us/call   {nbytes / us / 1e6:8.1f} TFLOP/s", flush=True)
+        else:
+            print(f"{name:12s} {us:8.2f} us/call   {nbytes / 1e6:8.1f} MB   {nbytes / us / 1e3:8.1f} GB/s", flush=True)
         del calls
         torch.cuda.empty_cache()
     status = _native.device_status()

@@ -17,7 +17,7 @@ The forward is the packed mixed-batch path of ``Qwen3Model._forward_packed``
       qkv = n @ [Wq; Wk; Wv]^T                           cuBLAS GEMM (one, fused weights)
       q = attend(norm+rope(q), append(norm+rope(k), v))  kernels b + c
       h, n2 = x + q @ Wo^T, rmsnorm(.)                   GEMM + kernel: add_rmsnorm
-      m = silu(n2 @ Wg^T) * (n2 @ Wu^T) @ Wd^T           GEMM (fused gate|up) + kernel: swiglu + GEMM
+      m = silu(n2 @ Wg^T) * (n2 @ Wu^T) @ Wd^T           tcgen05 gate|up GEMM with SwiGLU epilogue + GEMM
       x, n = h + m, rmsnorm(., next norm)                kernel: add_rmsnorm
     logits = n[logit rows] @ E^T                         GEMM
 
@@ -59,6 +59,9 @@ def rope_parameters(config: Qwen3Config) -> tuple[torch.Tensor, torch.Tensor]:
     return torch.cos(angles), torch.sin(angles)
 
 
+FUSED_GATE_UP_MIN_ROWS = 256  # token rows from which the fused tcgen05 gate|up + SwiGLU kernel is used
+
+
 class _Fused:
     """Concatenation of several Linear weights along the output dimension, rebuilt
     when any of them is replaced or modified in place (e.g. by load_state_dict)."""
@@ -96,10 +99,17 @@ class FeedForward(nn.Module):
         self._gate_up = _Fused(self.gate, self.up)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        """``x [T, hidden]`` -> ``[T, hidden]``: one gate|up GEMM, fused SwiGLU, down GEMM."""
-        gate_up = F.linear(x, self._gate_up.get())
-        act = torch.empty((x.shape[0], self.gate.out_features), dtype=x.dtype, device=x.device)
-        ops.swiglu(gate_up, act)
+        """``x [T, hidden]`` -> ``[T, hidden]``: gate|up projection + SwiGLU, then the down GEMM.
+        From FUSED_GATE_UP_MIN_ROWS rows the gate|up GEMM runs on this library's tcgen05 kernel
+        with SwiGLU in its epilogue; fewer rows (mostly padding in its 128-row tiles) take
+        cuBLAS and the SwiGLU kernel. Both keep the reference's rounding points."""
+        inter = self.gate.out_features
+        if x.shape[0] >= FUSED_GATE_UP_MIN_ROWS and x.shape[1] % 64 == 0 and inter % 128 == 0:
+            act = ops.gemm_swiglu(x.contiguous(), self._gate_up.get())
+        else:
+            gate_up = F.linear(x, self._gate_up.get())
+            act = torch.empty((x.shape[0], inter), dtype=x.dtype, device=x.device)
+            ops.swiglu(gate_up, act)
         return F.linear(act, self.down.weight)
 
 

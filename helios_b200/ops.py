@@ -148,6 +148,22 @@ def swiglu(gate_up: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def gemm_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``silu(x Wg^T) * (x Wu^T)`` with the reference's bf16 rounding points, for ``x [m, k]``
+    and the fused ``w_gate_up [2 * inter, k]`` (gate rows then up rows), on tcgen05."""
+    _need(x, BF16, "x")
+    _need(w_gate_up, BF16, "w_gate_up")
+    m, k = x.shape
+    inter = w_gate_up.shape[0] // 2
+    if w_gate_up.shape[1] != k or w_gate_up.shape[0] != 2 * inter:
+        raise ValueError("w_gate_up must be [2 * intermediate, hidden] matching x")
+    if out is None:
+        out = torch.empty((m, inter), dtype=BF16, device=x.device)
+    rc = lib().hb_gemm_swiglu(x.data_ptr(), m, k, w_gate_up.data_ptr(), inter, out.data_ptr(), _stream(x.device))
+    _native.check(rc, "hb_gemm_swiglu")
+    return out
+
+
 def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     if ids.dtype != torch.long or not ids.is_cuda or not ids.is_contiguous():
         raise ValueError("token ids must be a contiguous CUDA int64 tensor")

@@ -166,6 +166,16 @@ HB_API int hb_add_rmsnorm(const void* x, const void* y, const float* scale, floa
 /* silu(gate) * up from a [rows][2*inter] gate|up GEMM output (FeedForward.forward, layers.py:26-27). */
 HB_API int hb_swiglu(const void* gate_up, void* out, int64_t rows, int64_t inter, cudaStream_t stream);
 
+/*
+ * Gate|up projection fused with SwiGLU on tcgen05 tensor cores. Replaces, in FeedForward.forward
+ * (src/helios/runtime/qwen3/layers.py:26-27), gate(x), up(x) and silu(gate) * up for
+ * x bf16 [m][k] (rows contiguous) and the fused weight w_gate_up bf16 [2*inter][k] (the gate
+ * rows, then the up rows): out bf16 [m][inter] = bf16(bf16(silu(bf16(x Wg^T))) * bf16(x Wu^T)).
+ * Needs k % 64 == 0 and inter % 128 == 0.
+ */
+HB_API int hb_gemm_swiglu(const void* x, int32_t m, int32_t k, const void* w_gate_up, int32_t inter, void* out,
+                          cudaStream_t stream);
+
 /* Token-embedding gather (Qwen3Model._forward_packed, src/helios/runtime/qwen3/model.py:97). */
 HB_API int hb_embedding(const int64_t* ids, const void* table, int64_t vocab, void* out, int64_t tokens,
                         int32_t hidden, cudaStream_t stream);
