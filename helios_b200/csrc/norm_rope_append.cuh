@@ -56,6 +56,57 @@ __device__ __forceinline__ void unpack4(const uint2& v, float (&f)[4]) {
   f[3] = __high2float(h[1]);
 }
 
+// One lane's share of a head row's RMSNorm: the row's D values are spread over kLanes lanes
+// (named by row_mask), this lane holding elements [4j, 4j+4) in ylo and [D/2 + 4j, D/2 + 4j
+// + 4) in yhi as packed bf16, and ga / gb the norm scales at those elements. fp32 norm
+// bf16(fl(fl(x * inv) * scale)) with inv = rsqrt(mean(x^2) + eps); the sum of squares is
+// this lane's eight products in order, then a butterfly over the row's lanes.
+template <int kLanes, int D>
+__device__ __forceinline__ void norm_lane(uint2& ylo, uint2& yhi, const float4& ga, const float4& gb, float eps,
+                                          unsigned row_mask) {
+  float a[4], b[4];
+  unpack4(ylo, a);
+  unpack4(yhi, b);
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) ss = __fmaf_rn(a[e], a[e], ss);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) ss = __fmaf_rn(b[e], b[e], ss);
+#pragma unroll
+  for (int o = kLanes / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(row_mask, ss, o);
+  // mean = ss / D: D is a power of two, so the product by 1 / D is the exact quotient.
+  const float inv = rsqrtf(__fadd_rn(ss * (1.f / static_cast<float>(D)), eps));
+  ylo.x = pack_bf16(__fmul_rn(__fmul_rn(a[0], inv), ga.x), __fmul_rn(__fmul_rn(a[1], inv), ga.y));
+  ylo.y = pack_bf16(__fmul_rn(__fmul_rn(a[2], inv), ga.z), __fmul_rn(__fmul_rn(a[3], inv), ga.w));
+  yhi.x = pack_bf16(__fmul_rn(__fmul_rn(b[0], inv), gb.x), __fmul_rn(__fmul_rn(b[1], inv), gb.y));
+  yhi.y = pack_bf16(__fmul_rn(__fmul_rn(b[2], inv), gb.z), __fmul_rn(__fmul_rn(b[3], inv), gb.w));
+}
+
+// One lane's share of RoPE, y * cos + rot(y) * sin with rot(y) = (-y_hi, y_lo):
+// lo = fl(fl(y_lo c) - fl(y_hi s)), hi = fl(fl(y_hi c) + fl(y_lo s)), each rounded to bf16
+// (negation is exact); c_lo/s_lo are the tables at this lane's first-half elements.
+__device__ __forceinline__ void rope_lane(uint2& ylo, uint2& yhi, const float (&c_lo)[4], const float (&c_hi)[4],
+                                          const float (&s_lo)[4], const float (&s_hi)[4]) {
+  float a[4], b[4], o[8];
+  unpack4(ylo, a);
+  unpack4(yhi, b);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    o[e] = __fsub_rn(__fmul_rn(a[e], c_lo[e]), __fmul_rn(b[e], s_lo[e]));
+    o[4 + e] = __fadd_rn(__fmul_rn(b[e], c_hi[e]), __fmul_rn(a[e], s_hi[e]));
+  }
+  ylo = make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
+  yhi = make_uint2(pack_bf16(o[4], o[5]), pack_bf16(o[6], o[7]));
+}
+
+// rope_lane with the table values as float4 (the same arithmetic).
+__device__ __forceinline__ void rope_lane(uint2& ylo, uint2& yhi, const float4& cl, const float4& ch,
+                                          const float4& sl, const float4& sh) {
+  const float c_lo[4] = {cl.x, cl.y, cl.z, cl.w}, c_hi[4] = {ch.x, ch.y, ch.z, ch.w};
+  const float s_lo[4] = {sl.x, sl.y, sl.z, sl.w}, s_hi[4] = {sh.x, sh.y, sh.z, sh.w};
+  rope_lane(ylo, yhi, c_lo, c_hi, s_lo, s_hi);
+}
+
 template <int D>
 __global__ void __launch_bounds__(kRopeThreads, 4) norm_rope_append_kernel(NormRopeParams p) {
   constexpr int kLanes = D / 8;                    // lanes per head row
@@ -130,40 +181,12 @@ __global__ void __launch_bounds__(kRopeThreads, 4) norm_rope_append_kernel(NormR
       // unpacked only where fp32 arithmetic follows.
       uint2 ylo = lo[i], yhi = hi[i];
       const float* scale = is_q ? p.q_scale : p.k_scale;
-      if (scale != nullptr) {  // RMSNorm over the row (fp32): bf16(fl(fl(x * inv) * scale))
-        float a[4], b[4];
-        unpack4(ylo, a);
-        unpack4(yhi, b);
-        float ss = 0.f;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) ss = __fmaf_rn(a[e], a[e], ss);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) ss = __fmaf_rn(b[e], b[e], ss);
-#pragma unroll
-        for (int o = kLanes / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(row_mask, ss, o);
-        // mean = ss / D: D is a power of two, so the product by 1 / D is the exact quotient.
-        const float inv = rsqrtf(__fadd_rn(ss * (1.f / static_cast<float>(D)), p.eps));
+      if (scale != nullptr) {
         const float4 ga = *reinterpret_cast<const float4*>(scale + 4 * j);
         const float4 gb = *reinterpret_cast<const float4*>(scale + kHalf + 4 * j);
-        ylo.x = pack_bf16(__fmul_rn(__fmul_rn(a[0], inv), ga.x), __fmul_rn(__fmul_rn(a[1], inv), ga.y));
-        ylo.y = pack_bf16(__fmul_rn(__fmul_rn(a[2], inv), ga.z), __fmul_rn(__fmul_rn(a[3], inv), ga.w));
-        yhi.x = pack_bf16(__fmul_rn(__fmul_rn(b[0], inv), gb.x), __fmul_rn(__fmul_rn(b[1], inv), gb.y));
-        yhi.y = pack_bf16(__fmul_rn(__fmul_rn(b[2], inv), gb.z), __fmul_rn(__fmul_rn(b[3], inv), gb.w));
+        norm_lane<kLanes, D>(ylo, yhi, ga, gb, p.eps, row_mask);
       }
-      if (p.cos != nullptr) {
-        // y * cos + rot(y) * sin with rot(y) = (-y_hi, y_lo): lo = fl(fl(y_lo c) - fl(y_hi s)),
-        // hi = fl(fl(y_hi c) + fl(y_lo s)), each rounded to bf16 (negation is exact).
-        float a[4], b[4], o[8];
-        unpack4(ylo, a);
-        unpack4(yhi, b);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          o[e] = __fsub_rn(__fmul_rn(a[e], c_lo[e]), __fmul_rn(b[e], s_lo[e]));
-          o[4 + e] = __fadd_rn(__fmul_rn(b[e], c_hi[e]), __fmul_rn(a[e], s_hi[e]));
-        }
-        ylo = make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
-        yhi = make_uint2(pack_bf16(o[4], o[5]), pack_bf16(o[6], o[7]));
-      }
+      if (p.cos != nullptr) rope_lane(ylo, yhi, c_lo, c_hi, s_lo, s_hi);
       __nv_bfloat16* dst = is_q ? p.q_out + (static_cast<int64_t>(t) * p.heads + hr) * D
                                 : p.key_pool + (slot * p.kv_heads + (hr - p.heads)) * D;
       *reinterpret_cast<uint2*>(dst + 4 * j) = ylo;

@@ -1,7 +1,7 @@
 """Kernel microbenchmarks at the BASELINE config-3 tick shapes, timed from CUDA-graph replays.
 
     python -m helios_b200.microbench [norm_rope] [swiglu] [add_rmsnorm] [prefill] [decode] [mixed]
-                                     [gate_up_fused] [gate_up_cublas]
+                                     [gate_up_fused] [gate_up_cublas] [qkv_fused] [qkv_fused_full_tables] [qkv_cublas]
 
 Each case captures 24 calls of one entry point into a CUDA graph, cycling over input sets
 whose total exceeds the 126 MB L2 where the kernel is memory-bound, and prints the median
@@ -111,6 +111,44 @@ def _gate_up(dev, g, fused: bool):
     return [make() for _ in range(2)], flops
 
 
+def _qkv(dev, g, fused: bool, half_tables: bool = True):
+    """The attention input side: q|k|v projection + per-head norm, RoPE and KV append, fused
+    (tcgen05, epilogue) or cuBLAS + the norm/RoPE/append kernel. Rope tables repeat their
+    first half in the second (as the model's do) unless half_tables is False."""
+    import torch.nn.functional as F
+
+    w = (torch.randn((H + 2 * HKV) * D, HIDDEN, device=dev, generator=g) / HIDDEN ** 0.5).to(torch.bfloat16)
+    cos, sin = torch.randn(40960, D, device=dev), torch.randn(40960, D, device=dev)
+    if half_tables:
+        cos[:, D // 2:], sin[:, D // 2:] = cos[:, :D // 2], sin[:, :D // 2]
+    qs, ks = torch.rand(D, device=dev) + 0.5, torch.rand(D, device=dev) + 0.5
+    pages = 600
+
+    def make():
+        x = torch.randn(T, HIDDEN, device=dev, generator=g).to(torch.bfloat16)
+        kp = torch.zeros(pages, 256, HKV, D, dtype=torch.bfloat16, device=dev)
+        vp = torch.zeros_like(kp)
+        slots = torch.randperm(pages * 256, device=dev, generator=g)[:T].long()
+        pos = torch.randint(0, 4096, (T,), device=dev, generator=g).long()
+        qo = torch.empty(T, H, D, dtype=torch.bfloat16, device=dev)
+        if fused:
+            return lambda: ops.gemm_qkv_norm_rope_append(x, w, heads=H, kv_heads=HKV, q_scale=qs, k_scale=ks,
+                                                         eps=1e-6, cos=cos, sin=sin, positions=pos, write_slots=slots,
+                                                         q_out=qo, key_pool=kp, value_pool=vp,
+                                                         rope_half_tables=half_tables)
+
+        def unfused():
+            qkv = F.linear(x, w)
+            ops.qk_norm_rope_append(qkv[:, :H * D].view(T, H, D), qkv[:, H * D:(H + HKV) * D].view(T, HKV, D),
+                                    qkv[:, (H + HKV) * D:].view(T, HKV, D), q_scale=qs, k_scale=ks, eps=1e-6,
+                                    cos=cos, sin=sin, positions=pos, write_slots=slots, q_out=qo, key_pool=kp,
+                                    value_pool=vp)
+        return unfused
+
+    flops = 2 * T * HIDDEN * (H + 2 * HKV) * D
+    return [make() for _ in range(2)], flops
+
+
 def _attention(dev, lengths, counts, sets):
     cfg = Qwen3Config(n_layers=1, context_length=8192)
     calls, kv_bytes = [], sum(l + c for l, c in zip(lengths, counts)) * HKV * D * 2 * 2
@@ -151,12 +189,15 @@ def main(argv: list[str]) -> None:
         "mixed": lambda: _attention(dev, decode_lengths + [0], [1] * 32 + [2048], 2),
         "gate_up_fused": lambda: _gate_up(dev, g, True),
         "gate_up_cublas": lambda: _gate_up(dev, g, False),
+        "qkv_fused": lambda: _qkv(dev, g, True),
+        "qkv_fused_full_tables": lambda: _qkv(dev, g, True, half_tables=False),
+        "qkv_cublas": lambda: _qkv(dev, g, False),
     }
     for name in argv or list(cases):
         calls, nbytes = cases[name]()
         with torch.inference_mode():
             us = graph_time(calls)
-        if name.startswith("gate_up"):  # compute-bound: report TFLOP/s
+        if name.startswith(("gate_up", "qkv")):  # compute-bound: report TFLOP/s
             print(f"{name:14s} {us:8.2f} us/call   {nbytes / us / 1e6:8.1f} TFLOP/s", flush=True)
         else:
             print(f"{name:12s} {us:8.2f} us/call   {nbytes / 1e6:8.1f} MB   {nbytes / us / 1e3:8.1f} GB/s", flush=True)

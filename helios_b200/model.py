@@ -60,6 +60,11 @@ def rope_parameters(config: Qwen3Config) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 FUSED_GATE_UP_MIN_ROWS = 256  # token rows from which the fused tcgen05 gate|up + SwiGLU kernel is used
+# Token rows from which the fused tcgen05 q|k|v + norm/RoPE/append kernel would be used. None:
+# not used. At the Qwen3-4B tick shape (2080 rows) it measured 58-62 us against 56 us for cuBLAS
+# plus the norm/RoPE/append kernel: its one-SM main loop is TMA-latency-bound (~24k cycles per
+# 128 x 256 tile) and the last tile's epilogue (norm, RoPE, scattered row writes) stays exposed.
+FUSED_QKV_MIN_ROWS: int | None = None
 
 
 class _Fused:
@@ -131,10 +136,19 @@ class GroupedQueryAttention(nn.Module):
         self._qkv = _Fused(self.query, self.key, self.value)
 
     def forward(self, x: torch.Tensor, cache: PagedBatchCache, layer_index: int, cos: torch.Tensor,
-                sin: torch.Tensor) -> torch.Tensor:
-        """``x [T, hidden]`` (already input-normed) -> attention block output ``[T, hidden]``."""
-        qkv = F.linear(x, self._qkv.get())
-        context = cache.attend_fused(layer_index, qkv, self.q_norm.scale, self.k_norm.scale, self.q_norm.eps, cos, sin)
+                sin: torch.Tensor, rope_half_tables: bool = False) -> torch.Tensor:
+        """``x [T, hidden]`` (already input-normed) -> attention block output ``[T, hidden]``.
+        ``rope_half_tables``: every cos/sin row's second half repeats its first."""
+        if (FUSED_QKV_MIN_ROWS is not None and x.shape[0] >= FUSED_QKV_MIN_ROWS and self.head_dim == 128
+                and x.shape[1] % 64 == 0
+                and (self.n_heads + 2 * self.n_kv_heads) % 2 == 0):
+            # One tcgen05 GEMM whose epilogue does the q/k norm, RoPE and KV append.
+            context = cache.attend_projected(layer_index, x.contiguous(), self._qkv.get(), self.q_norm.scale,
+                                             self.k_norm.scale, self.q_norm.eps, cos, sin, rope_half_tables)
+        else:
+            qkv = F.linear(x, self._qkv.get())
+            context = cache.attend_fused(layer_index, qkv, self.q_norm.scale, self.k_norm.scale, self.q_norm.eps,
+                                         cos, sin)
         return F.linear(context.view(x.shape[0], -1), self.output.weight)
 
 
@@ -159,6 +173,10 @@ class Qwen3Model(nn.Module):
         cos, sin = rope_parameters(config)
         self.register_buffer("cos", cos, persistent=False)
         self.register_buffer("sin", sin, persistent=False)
+        # Each row's second half repeats its first (duplicated angles): the fused q|k|v
+        # kernel may then read half of every row. Checked on the host tables once.
+        half = config.head_dim // 2
+        self.rope_half_tables = bool(torch.equal(cos[:, :half], cos[:, half:]) and torch.equal(sin[:, :half], sin[:, half:]))
         self._graphs = None  # TickGraphs once enable_cuda_graphs() is called
 
     def enable_cuda_graphs(self, max_graphs: int = 4) -> None:
@@ -225,7 +243,7 @@ class Qwen3Model(nn.Module):
         h = torch.empty_like(x)
         normed2 = torch.empty_like(x)
         for index, block in enumerate(self.blocks):
-            attn = block.attention(normed, cache, index, self.cos, self.sin)
+            attn = block.attention(normed, cache, index, self.cos, self.sin, rope_half_tables=self.rope_half_tables)
             ops.add_rmsnorm(x, attn, block.post_attention_norm.scale, eps, h, normed2)
             mlp = block.feed_forward(normed2)
             nxt = self.blocks[index + 1].input_norm.scale if index + 1 < len(self.blocks) else self.final_norm.scale
