@@ -519,9 +519,15 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    parser.add_argument("--decode-sms", type=int, default=None,
+                        help="SMs the decode attention grid keeps beside prefill work (0: all; default: the library's)")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("at least 3 warm-up steps")
+    if args.decode_sms is not None and args.impl == "b200":
+        from helios_b200 import _native
+
+        _native.check(_native.load().hb_attention_set_overlap(args.decode_sms), "hb_attention_set_overlap")
     if args.impl == "reference":
         run_reference(args)
     else:

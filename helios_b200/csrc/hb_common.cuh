@@ -133,6 +133,11 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
 // completed and its writes are visible (a no-op for an ordinary launch), and
 // pdl_trigger() lets the kernel behind this one start once every CTA of this grid has
 // triggered or exited.
+// Barrier over `threads` threads (a multiple of 32) of the CTA, id 1..15 (0 is __syncthreads).
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

@@ -5,6 +5,7 @@
 // 0 on success or a negative code (HB_ERR_*) with a message in hb_last_error().
 // Declarations and the reference interface each one replaces: include/helios_b200.h.
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -118,7 +119,15 @@ int ensure_smem(K kernel, int bytes, bool (&done)[64]) {
   return HB_OK;
 }
 
-bool g_dec_smem[4][64], g_pre_smem[4][64], g_tick_smem[64], g_gemm_smem[64], g_qkv_smem[64];
+bool g_dec_smem[4][64], g_decp_smem[4][64], g_pre_smem[4][64], g_tick_smem[64], g_gemm_smem[64], g_qkv_smem[64];
+
+constexpr int kDefaultOverlapDecodeSms = 100;
+
+// SMs the decode grid keeps when a call also has prefill work (its other CTAs exit at once and
+// leave their SMs to the prefill grid, which runs beside it); 0: the decode grid keeps all.
+std::atomic<int> g_overlap_decode_sms{kDefaultOverlapDecodeSms};
+
+
 
 // Split-K workspace of hb_paged_attention_static_workspace: one fixed array per GPU,
 // for callers that cannot allocate device memory. In host code the name stands for a
@@ -274,9 +283,14 @@ int hb_qk_norm_rope_append(const void* q, int64_t q_token_stride, int64_t q_head
   return check_launch("norm_rope_append_kernel");
 }
 
+// Workspace: kWorkspaceHeader bytes of decode work counters, then the split-K partials
+// ([records][heads][head_dim] outputs, then [records][heads] log2-sum-exps).
+constexpr size_t kWorkspaceHeader = 256;
+
 size_t hb_attention_workspace_bytes(int32_t partial_records, int32_t heads, int32_t head_dim) {
-  if (partial_records <= 0 || heads <= 0 || head_dim <= 0) return 0;
-  return static_cast<size_t>(partial_records) * heads * (head_dim + 1) * sizeof(float);
+  if (heads <= 0 || head_dim <= 0) return 0;
+  const size_t records = partial_records > 0 ? static_cast<size_t>(partial_records) : 0;
+  return kWorkspaceHeader + records * heads * (head_dim + 1) * sizeof(float);
 }
 
 int hb_paged_attention(const void* q, const void* key_pool, const void* value_pool, int64_t num_pages,
@@ -303,8 +317,8 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
   if (!aligned(key_pool, 16) || !aligned(value_pool, 16) || !aligned(q, 16) || !aligned(out, 16))
     return fail(HB_ERR_INVALID, "q, out and pools must be 16-byte aligned");
   const size_t need = hb_attention_workspace_bytes(partial_records, heads, head_dim);
-  if (workspace_bytes < need || (need > 0 && workspace == nullptr))
-    return fail(HB_ERR_INVALID, "workspace holds %zu bytes, needs %zu", workspace_bytes, need);
+  if (workspace_bytes < need || workspace == nullptr || !aligned(workspace, 16))
+    return fail(HB_ERR_INVALID, "workspace holds %zu bytes, needs %zu (16-byte aligned)", workspace_bytes, need);
   if (total_tokens == 0) return HB_OK;
 
   hb::AttentionParams p{};
@@ -315,8 +329,9 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
   p.seqused_k = seqused_k;
   p.decode_items = decode_items;
   p.prefill_items = prefill_items;
-  p.ws_out = static_cast<float*>(workspace);
-  p.ws_lse = p.ws_out ? p.ws_out + static_cast<size_t>(partial_records) * heads * head_dim : nullptr;
+  p.work_counter = static_cast<int32_t*>(workspace);
+  p.ws_out = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWorkspaceHeader);
+  p.ws_lse = p.ws_out + static_cast<size_t>(partial_records > 0 ? partial_records : 0) * heads * head_dim;
   p.width = width;
   p.num_pages = static_cast<int32_t>(num_pages);
   p.page_size = page_size;
@@ -341,20 +356,40 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
   if (num_decode_items > 0 && decode_items == nullptr) return fail(HB_ERR_INVALID, "null decode items");
   if (num_prefill_items > 0 && prefill_items == nullptr) return fail(HB_ERR_INVALID, "null prefill items");
 
-  // Launch order decode -> prefill -> split combine, each behind the previous one with
-  // programmatic dependent launch: the prefill tiles start on the SMs the decode splits free
-  // (they read none of the decode output), and every completion is ordered through the
-  // kernels' grid-dependency waits (see prefill_after_decode).
+  // Launch order decode -> prefill -> split combine on the caller's stream, each behind the
+  // previous one with programmatic dependent launch; completions are ordered through
+  // grid-dependency waits (the prefill grid completes after the decode grid, see
+  // prefill_after_decode, and the combine after both). Decode alone: one CTA per unit, two
+  // per SM. Decode with prefill work: the persistent decode grid, whose CTAs past
+  // decode_ctas exit at once so that the prefill tiles start on those SMs while the decode
+  // CTAs stream K/V (decode is HBM-bound, prefill tensor-bound).
   if (num_prefill_items > 65535) return fail(HB_ERR_UNSUPPORTED, "more than 65535 prefill tile pairs in one call");
+  const int overlap_sms = g_overlap_decode_sms.load();
+  const bool beside = num_decode_items > 0 && num_prefill_items > 0 && overlap_sms > 0;
+  int decode_grid = 0;
+  if (beside) {
+    const int sms = sm_count();
+    if (sms <= 0) return fail(HB_ERR_CUDA, "cannot read the SM count");
+    decode_grid = std::min(sms, (num_decode_items * kv_heads + hb::kDecSubs - 1) / hb::kDecSubs);
+  }
+  p.num_decode = num_decode_items;
+  p.decode_ctas = std::max(1, std::min(overlap_sms, decode_grid));
   p.prefill_after_decode = num_decode_items > 0 ? 1 : 0;
   if (num_decode_items > 0) {
-    const dim3 grid(num_decode_items, kv_heads);
-#define HB_DECODE(G)                                                                                           \
-  do {                                                                                                         \
-    if (int rc = ensure_smem(hb::decode_attention_kernel<G>, hb::kDecSmemBytes, g_dec_smem[gs])) return rc;    \
-    const cudaError_t e = launch_pdl(hb::decode_attention_kernel<G>, grid, dim3(hb::kDecThreads),              \
-                                     hb::kDecSmemBytes, stream, p, kmap, vmap);                               \
-    if (e != cudaSuccess) return fail(HB_ERR_CUDA, "decode_attention_kernel: %s", cudaGetErrorString(e));      \
+#define HB_DECODE(G)                                                                                            \
+  do {                                                                                                          \
+    cudaError_t e;                                                                                              \
+    if (beside) {                                                                                               \
+      if (int rc = ensure_smem(hb::decode_persistent_kernel<G>, hb::kDecPersistentSmemBytes, g_decp_smem[gs]))  \
+        return rc;                                                                                              \
+      e = launch_pdl(hb::decode_persistent_kernel<G>, dim3(decode_grid), dim3(hb::kDecPersistentThreads),       \
+                     hb::kDecPersistentSmemBytes, stream, p, kmap, vmap);                                       \
+    } else {                                                                                                    \
+      if (int rc = ensure_smem(hb::decode_attention_kernel<G>, hb::kDecSmemBytes, g_dec_smem[gs])) return rc;   \
+      e = launch_pdl(hb::decode_attention_kernel<G>, dim3(num_decode_items, kv_heads), dim3(hb::kDecSubThreads), \
+                     hb::kDecSmemBytes, stream, p, kmap, vmap);                                                 \
+    }                                                                                                           \
+    if (e != cudaSuccess) return fail(HB_ERR_CUDA, "decode attention: %s", cudaGetErrorString(e));              \
   } while (0)
     switch (group) {
       case 1: HB_DECODE(1); break;
@@ -385,7 +420,7 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
     }
 #undef HB_PREFILL
   }
-  if (num_decode_items > 0 && partial_records > 0) {
+  if (num_decode_items > 0 && (partial_records > 0 || beside)) {  // also resets the decode work ticket
     const dim3 grid(num_decode_items, kv_heads);
 #define HB_COMBINE(G)                                                                                          \
   do {                                                                                                         \
@@ -400,6 +435,12 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
     }
 #undef HB_COMBINE
   }
+  return HB_OK;
+}
+
+int hb_attention_set_overlap(int32_t decode_sms) {
+  if (decode_sms < 0) return fail(HB_ERR_INVALID, "decode_sms must be >= 0");
+  g_overlap_decode_sms.store(decode_sms);
   return HB_OK;
 }
 

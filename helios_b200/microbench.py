@@ -1,6 +1,6 @@
 """Kernel microbenchmarks at the BASELINE config-3 tick shapes, timed from CUDA-graph replays.
 
-    python -m helios_b200.microbench [norm_rope] [swiglu] [add_rmsnorm] [prefill] [decode] [mixed]
+    python -m helios_b200.microbench [norm_rope] [swiglu] [add_rmsnorm] [prefill] [decode] [mixed[:N]]
                                      [gate_up_fused] [gate_up_cublas] [qkv_fused] [qkv_fused_full_tables] [qkv_cublas]
 
 Each case captures 24 calls of one entry point into a CUDA graph, cycling over input sets
@@ -193,14 +193,23 @@ def main(argv: list[str]) -> None:
         "qkv_fused_full_tables": lambda: _qkv(dev, g, True, half_tables=False),
         "qkv_cublas": lambda: _qkv(dev, g, False),
     }
-    for name in argv or list(cases):
+    for arg in argv or list(cases):
+        # "mixed:48" times a case with the decode grid keeping 48 SMs beside the prefill grid
+        # (hb_attention_set_overlap; 0 runs them one after the other).
+        name, _, overlap = arg.partition(":")
+        if overlap:
+            _native.check(_native.load().hb_attention_set_overlap(int(overlap)), "hb_attention_set_overlap")
+            name_shown = arg
+        else:
+            name_shown = name
         calls, nbytes = cases[name]()
         with torch.inference_mode():
             us = graph_time(calls)
         if name.startswith(("gate_up", "qkv")):  # compute-bound: report TFLOP/s
-            print(f"{name:14s} {us:8.2f} us/call   {nbytes / us / 1e6:8.1f} TFLOP/s", flush=True)
+            print(f"{name_shown:14s} {us:8.2f} us/call   {nbytes / us / 1e6:8.1f} TFLOP/s", flush=True)
         else:
-            print(f"{name:12s} {us:8.2f} us/call   {nbytes / 1e6:8.1f} MB   {nbytes / us / 1e3:8.1f} GB/s", flush=True)
+            print(f"{name_shown:12s} {us:8.2f} us/call   {nbytes / 1e6:8.1f} MB   {nbytes / us / 1e3:8.1f} GB/s",
+                  flush=True)
         del calls
         torch.cuda.empty_cache()
     status = _native.device_status()

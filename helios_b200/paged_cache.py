@@ -401,8 +401,10 @@ class PagedBatchCache:
         if self.capacity_mode:
             cap = self.work_capacity
             if cap is None or self.num_decode_items > cap[0] or self.num_prefill_items > cap[1]:
-                # Headroom of one more split and one more tile pair per row.
-                cap = (self.num_decode_items + self.batch_size, self.num_prefill_items + self.batch_size)
+                # Headroom of one more split and one more tile pair per row; no prefill capacity for a
+                # decode-only tick, so its attention runs the decode grid alone (all SMs).
+                cap = (self.num_decode_items + self.batch_size,
+                       self.num_prefill_items + self.batch_size if self.num_prefill_items else 0)
                 self.work_capacity = cap
             self.launch_decode_items, self.launch_prefill_items = cap
             self.launch_partial_records = cap[0] * desc["decode_max"]  # each item has <= decode_max rows
@@ -421,7 +423,8 @@ class PagedBatchCache:
                       desc["tile_tokens"], total, out)
         need = ops.workspace_bytes(self.launch_partial_records, config.n_heads, config.head_dim)
         if need and (self.workspace is None or self.workspace.numel() < need):
-            self.workspace = torch.empty(max(need, 2 * (0 if self.workspace is None else self.workspace.numel())),
+            # Zeroed: its header holds the decode work ticket, which every call leaves at zero.
+            self.workspace = torch.zeros(max(need, 2 * (0 if self.workspace is None else self.workspace.numel())),
                                          dtype=torch.uint8, device=pool.device)
         self.block_table = out["block_table"]
         self.cu_seq_q = out["cu_seq_q"]

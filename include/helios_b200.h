@@ -101,7 +101,9 @@ HB_API int hb_qk_norm_rope_append(const void* q, int64_t q_token_stride, int64_t
                                   void* q_out, void* key_pool, void* value_pool, int64_t pool_slots, int32_t tokens,
                                   int32_t heads, int32_t kv_heads, int32_t head_dim, cudaStream_t stream);
 
-/* Bytes of float workspace hb_paged_attention needs for `partial_records` split records. */
+/* Bytes of workspace hb_paged_attention needs: 256 bytes of decode work counters (zero before
+ * the first call, left zero by every call) plus the float partials of `partial_records` split
+ * records (16-byte aligned; required on every call). */
 HB_API size_t hb_attention_workspace_bytes(int32_t partial_records, int32_t heads, int32_t head_dim);
 
 /*
@@ -117,6 +119,10 @@ HB_API size_t hb_attention_workspace_bytes(int32_t partial_records, int32_t head
  * array hb_tick_pack filled) those two arguments and partial_records are capacities: the
  * grids are sized to them and the kernels read the real numbers from counts, so one
  * launch (for instance inside a CUDA graph) serves every tick within the capacities.
+ * The decode grid is persistent (at most one CTA per SM); with prefill items in the same call the
+ * prefill grid runs beside it on the SMs it leaves (hb_attention_set_overlap), all on `stream`.
+ * The workspace's first 256 bytes hold a work ticket: they must be zero before the first call
+ * with a workspace, and every call leaves them zero.
  */
 HB_API int hb_paged_attention(const void* q, const void* key_pool, const void* value_pool, int64_t num_pages,
                               int32_t page_size, const int32_t* block_table, int32_t width, const int32_t* cu_seq_q,
@@ -125,6 +131,14 @@ HB_API int hb_paged_attention(const void* q, const void* key_pool, const void* v
                               int32_t partial_records, int32_t split_keys, int32_t total_tokens, int32_t heads,
                               int32_t kv_heads, int32_t head_dim, float scale, void* workspace,
                               size_t workspace_bytes, void* out, cudaStream_t stream);
+
+/*
+ * Overlap of decode and prefill attention in one hb_paged_attention call: the decode grid
+ * keeps decode_sms SMs (one persistent CTA each) and the prefill grid, launched behind it,
+ * starts on the others at once. 0: the decode grid keeps every SM and the prefill tiles start
+ * as decode CTAs finish. Process-wide; applies to later calls.
+ */
+HB_API int hb_attention_set_overlap(int32_t decode_sms);
 
 /*
  * Paged attention with a built-in workspace (no counterpart in the reference).

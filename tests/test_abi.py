@@ -32,8 +32,8 @@ def test_every_declared_symbol_is_exported(lib):
 
 def test_version_and_workspace_arithmetic(lib):
     assert lib.hb_version() == 1
-    assert lib.hb_attention_workspace_bytes(0, 32, 128) == 0
-    assert lib.hb_attention_workspace_bytes(10, 32, 128) == 10 * 32 * 129 * 4
+    assert lib.hb_attention_workspace_bytes(0, 32, 128) == 256
+    assert lib.hb_attention_workspace_bytes(10, 32, 128) == 256 + 10 * 32 * 129 * 4
 
 
 def test_invalid_arguments_are_rejected_before_any_launch(lib):

@@ -166,3 +166,39 @@ def test_other_group_sizes(heads, kv_heads):
 
 def test_stale_nan_slots_never_reach_the_output():
     _run([5, 300, 0, 600], [1, 2, 70, 1], nan_fill=True)
+
+
+@pytest.mark.parametrize("budget", [1, 7, 100])
+def test_persistent_decode_beside_prefill_matches_per_unit_decode(budget):
+    """With prefill work in the call the decode rows run on the persistent grid, which keeps
+    `budget` SMs (hb_attention_set_overlap). Decode rows of 1, 4, 8 and 16 tokens (16, 32 and
+    64 query rows per KV head: every key-split mode), single- and multi-split, give the same
+    bits as the one-CTA-per-unit grid (budget 0), call after call (the work ticket is reset
+    between calls), and the oracle's values."""
+    g = torch.Generator().manual_seed(5)
+    lengths = torch.randint(1, 6000, (24,), generator=g).tolist() + [0, 700]
+    counts = [1] * 12 + [4] * 4 + [8] * 4 + [16] * 4 + [300, 200]
+    lib = _native.load()
+    try:
+        _native.check(lib.hb_attention_set_overlap(0), "hb_attention_set_overlap")
+        base = _run(lengths, counts, seed=5)
+        want = base.attend(0, *_qkv(base, 5))
+        _native.check(lib.hb_attention_set_overlap(budget), "hb_attention_set_overlap")
+        batch = _run(lengths, counts, seed=5)
+        for _ in range(2):
+            got = batch.attend(0, *_qkv(batch, 5))
+            assert torch.equal(got, want)
+        assert _native.device_status() == 0
+    finally:
+        _native.check(lib.hb_attention_set_overlap(100), "hb_attention_set_overlap")
+    assert batch.num_prefill_items > 0 and batch.num_decode_items > 24
+
+
+def _qkv(batch, seed):
+    """Fresh q/k/v for another attend on the same prepared batch (same values for a seed)."""
+    g = torch.Generator().manual_seed(seed + 1000)
+    T = batch.total_tokens
+    q = torch.randn(1, 32, T, 128, generator=g).to(torch.bfloat16).to(DEV)
+    k = (torch.randn(1, 8, T, 128, generator=g) / 3).to(torch.bfloat16).to(DEV)
+    v = torch.randn(1, 8, T, 128, generator=g).to(torch.bfloat16).to(DEV)
+    return q, k, v
