@@ -11,7 +11,12 @@
 //     then by rank within the tied key;
 //   * the draw: kept tokens in ascending index order, the first whose running
 //     mass exceeds u * kept_mass for the caller's uniform u in [0, 1).
-// Six passes over the row, all L2-resident after the first.
+// Layout: each of the 32 warps owns one contiguous segment of the row and reads it in
+// 256-element steps, lane l taking elements 8l .. 8l + 7 of a step as one 16-byte load,
+// so every pass is coalesced and index order is (warp, step, lane, element). The mass
+// histograms are per warp (no cross-warp atomics on the few bins a peaked distribution
+// fills), index-ordered counts and sums are warp scans plus one block scan over the warps,
+// and the last pass walks only the warp whose segment holds the draw.
 #pragma once
 
 #include <climits>
@@ -21,6 +26,13 @@
 namespace hb {
 
 constexpr int kSampleThreads = 1024;
+constexpr int kSampleWarps = kSampleThreads / 32;
+constexpr int kSampleUnroll = 4;  // groups a lane loads before using any (loads in flight)
+// Weights below 2^-40 of the row's largest (which is exactly 1) are left out of the mass
+// histograms that locate the top-p cut: even all 2^17+ of them together stay below
+// 2^-23 of the partition function, the rounding of its own fp32 sum, so the cut is the
+// one the full sums give; the kept mass and the draw still sum every kept token.
+constexpr float kNegligibleWeight = 9.094947e-13f;  // 2^-40
 
 struct SampleParams {
   const __nv_bfloat16* logits;  // [rows, row_stride]
@@ -33,10 +45,8 @@ struct SampleParams {
 };
 
 // Order-preserving 16-bit key of a bf16 value (larger value -> larger key).
-__device__ __forceinline__ uint32_t bf16_key(__nv_bfloat16 v) {
-  const uint16_t b = __bfloat16_as_ushort(v);
-  return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
-}
+__device__ __forceinline__ uint32_t bf16_key_bits(uint32_t b) { return (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u); }
+__device__ __forceinline__ uint32_t bf16_key(__nv_bfloat16 v) { return bf16_key_bits(__bfloat16_as_ushort(v)); }
 
 template <typename T, typename Op>
 __device__ __forceinline__ T block_reduce(T v, Op op, T* red) {
@@ -52,53 +62,135 @@ __device__ __forceinline__ T block_reduce(T v, Op op, T* red) {
   return v;
 }
 
-// Exclusive block scan of one double per thread; returns this thread's prefix.
-__device__ __forceinline__ double block_exclusive_scan(double v, double* red, double* total) {
+// Exclusive scan of one value per warp (read from lane 0's argument) over the 32 warps in
+// order; every thread gets its warp's prefix and the total.
+template <typename T>
+__device__ __forceinline__ T warps_exclusive_scan(T v, T* red, T* total) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  double x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const double n = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += n;
-  }
-  if (lane == 31) red[warp] = x;
+  if (lane == 0) red[warp] = v;
   __syncthreads();
   if (warp == 0) {
-    double w = red[lane];
+    T w = red[lane];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const double n = __shfl_up_sync(0xffffffffu, w, o);
+      const T n = __shfl_up_sync(0xffffffffu, w, o);
       if (lane >= o) w += n;
     }
-    red[lane] = w;
+    red[lane] = w;  // inclusive
   }
   __syncthreads();
-  const double before = (warp ? red[warp - 1] : 0.0) + x - v;
+  const T before = warp ? red[warp - 1] : T(0);
   *total = red[31];
   __syncthreads();
   return before;
 }
 
+// Inclusive scan over the lanes of a warp.
+template <typename T>
+__device__ __forceinline__ T warp_inclusive_scan(T v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const T n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += n;
+  }
+  return v;
+}
+
+// The 8 logits of group g (elements 8g .. 8g + 7, n of them inside the row) as bf16 bits.
+__device__ __forceinline__ int load_group(const __nv_bfloat16* lg, int g, int V, bool vec_ok, uint32_t (&b)[8]) {
+  const int i0 = 8 * g;
+  const int n = min(8, V - i0);
+  if (vec_ok && n == 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(lg + i0);
+    b[0] = v.x & 0xFFFFu; b[1] = v.x >> 16; b[2] = v.y & 0xFFFFu; b[3] = v.y >> 16;
+    b[4] = v.z & 0xFFFFu; b[5] = v.z >> 16; b[6] = v.w & 0xFFFFu; b[7] = v.w >> 16;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) b[e] = e < n ? __bfloat16_as_ushort(lg[i0 + e]) : 0u;
+  }
+  return n;
+}
+
+__device__ __forceinline__ float bits_to_float(uint32_t b) { return __uint_as_float(b << 16); }
+
+// Groups base + 32u + lane (u < kSampleUnroll) of a warp segment ending at g_end, all loads
+// issued before any is used; n[u] = 0 past the segment.
+__device__ __forceinline__ void load_groups(const __nv_bfloat16* lg, int base, int g_end, int V, bool vec_ok,
+                                            uint32_t (&b)[kSampleUnroll][8], int (&n)[kSampleUnroll]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int u = 0; u < kSampleUnroll; ++u) {
+    const int g = base + 32 * u + lane;
+    n[u] = g < g_end ? load_group(lg, g, V, vec_ok, b[u]) : 0;
+  }
+}
+
+// The 256 bins of `hist` in descending key order (bin 255 first), by one warp: the first bin
+// k with cum <= target < cum + hist[k] (and hist[k] > 0 when `nonempty`), where cum is `base`
+// plus the mass of the bins above k. Returns the bin (or -1) and its cum; also the total mass.
+__device__ __forceinline__ int warp_find_cut(const double* hist, double base, double target, bool nonempty,
+                                             double* cum_out, double* total_out) {
+  const int lane = threadIdx.x & 31;
+  double h[8], sum = 0.0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    h[i] = hist[255 - (8 * lane + i)];
+    sum += h[i];
+  }
+  const double incl = warp_inclusive_scan(sum);
+  double c = base + incl - sum;
+  int found = -1;
+  double found_cum = 0.0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (found < 0 && (!nonempty || h[i] > 0.0) && c <= target && target < c + h[i]) {
+      found = 255 - (8 * lane + i);
+      found_cum = c;
+    }
+    c += h[i];
+  }
+  *total_out = __shfl_sync(0xffffffffu, incl, 31);
+  const unsigned hit = __ballot_sync(0xffffffffu, found >= 0);
+  if (hit == 0u) return -1;
+  const int src = __ffs(hit) - 1;  // the lane with the highest bins
+  *cum_out = __shfl_sync(0xffffffffu, found_cum, src);
+  return __shfl_sync(0xffffffffu, found, src);
+}
+
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) {
+  __shared__ float whist[kSampleWarps][256];  // per-warp mass histograms
+  __shared__ double hist[256];                // their sum over the warps
   __shared__ float fred[32];
   __shared__ int ired[32];
   __shared__ double dred[32];
-  __shared__ float hist[256];
   __shared__ uint32_t cut_key;
-  __shared__ float cut_mass_above;
+  __shared__ double cut_mass_above, cut_target;
   __shared__ int cut_found;
   __shared__ int chosen;
 
-  const int row = blockIdx.x, tid = threadIdx.x;
+  const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const __nv_bfloat16* lg = p.logits + static_cast<int64_t>(row) * p.row_stride;
   const int V = p.vocab;
+  const bool vec_ok = (reinterpret_cast<uintptr_t>(lg) & 15) == 0;
+  const int groups = (V + 7) / 8;
+  const int gpw = (groups + kSampleWarps - 1) / kSampleWarps;  // groups per warp segment
+  const int g_begin = min(groups, warp * gpw), g_end = min(groups, g_begin + gpw);
 
   // Pass 1: max and its first index.
   float mx = -INFINITY;
   int arg = INT_MAX;
-  for (int i = tid; i < V; i += kSampleThreads) {
-    const float v = __bfloat162float(lg[i]);
-    if (v > mx) { mx = v; arg = i; }  // strided order: first hit per thread is its smallest index
+  for (int base = g_begin; base < g_end; base += 32 * kSampleUnroll) {
+    uint32_t b[kSampleUnroll][8];
+    int n[kSampleUnroll];
+    load_groups(lg, base, g_end, V, vec_ok, b, n);
+#pragma unroll
+    for (int u = 0; u < kSampleUnroll; ++u)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float v = bits_to_float(b[u][e]);
+        if (e < n[u] && v > mx) { mx = v; arg = 8 * (base + 32 * u + lane) + e; }  // indices visited in order
+      }
   }
   const float gmax = block_reduce(mx, [](float a, float b) { return fmaxf(a, b); }, fred);
   if (mx != gmax) arg = INT_MAX;
@@ -110,66 +202,91 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) 
   }
   const float m = __fdiv_rn(gmax, T);
   const float top_p = p.top_p[row];
+  auto weight = [&](uint32_t bits) { return expf(__fdiv_rn(bits_to_float(bits), T) - m); };
+  // Logits below x_floor have weight < e^-28 < kNegligibleWeight (x / T - m < -28 up to the
+  // rounding of the division), so the histogram passes skip them without computing it.
+  const float x_floor = T * (m - 28.f);
 
-  // Pass 2: partition function Z.
-  float z = 0.f;
-  for (int i = tid; i < V; i += kSampleThreads) z += expf(__fdiv_rn(__bfloat162float(lg[i]), T) - m);
-  const float Z = block_reduce(z, [](float a, float b) { return a + b; }, fred);
-
-  uint32_t key_star = 0;        // tokens with key > key_star are kept
-  int n_tie_keep = 0;           // how many tokens with key == key_star are kept (lowest indices)
+  uint32_t key_star = 0;  // tokens with key > key_star are kept
+  int n_tie_keep = 0;     // how many tokens with key == key_star are kept (lowest indices)
   bool keep_all = !(top_p < 1.f);
   if (!keep_all) {
-    const float target = top_p * Z;
-    // Level 1: mass per high byte of the key.
-    for (int b = tid; b < 256; b += kSampleThreads) hist[b] = 0.f;
-    __syncthreads();
-    for (int i = tid; i < V; i += kSampleThreads) {
-      const __nv_bfloat16 v = lg[i];
-      atomicAdd(&hist[bf16_key(v) >> 8], expf(__fdiv_rn(__bfloat162float(v), T) - m));
+    // Pass 2: mass per high byte of the key (its total is the partition function Z).
+    for (int k = lane; k < 256; k += 32) whist[warp][k] = 0.f;
+    __syncwarp();
+    for (int base = g_begin; base < g_end; base += 32 * kSampleUnroll) {
+      uint32_t b[kSampleUnroll][8];
+      int n[kSampleUnroll];
+      load_groups(lg, base, g_end, V, vec_ok, b, n);
+#pragma unroll
+      for (int u = 0; u < kSampleUnroll; ++u)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (e >= n[u] || !(bits_to_float(b[u][e]) >= x_floor)) continue;
+          const float w = weight(b[u][e]);
+          if (w > kNegligibleWeight) atomicAdd(&whist[warp][bf16_key_bits(b[u][e]) >> 8], w);
+        }
     }
     __syncthreads();
-    if (tid == 0) {
-      float cum = 0.f;
-      cut_found = 0;
-      for (int b = 255; b >= 0; --b) {
-        if (cum <= target && target < cum + hist[b]) {
-          cut_key = static_cast<uint32_t>(b);
-          cut_mass_above = cum;
-          cut_found = 1;
-          break;
-        }
-        cum += hist[b];
+    if (tid < 256) {
+      double t = 0.0;
+      for (int w = 0; w < kSampleWarps; ++w) t += whist[w][tid];
+      hist[tid] = t;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // Z first (the total of the bins), then the cut against top_p * Z.
+      double cum = 0.0, Z = 0.0;
+      warp_find_cut(hist, 0.0, -1.0, false, &cum, &Z);
+      const double t = static_cast<double>(top_p) * Z;
+      const int k = warp_find_cut(hist, 0.0, t, false, &cum, &Z);
+      if (lane == 0) {
+        cut_found = k >= 0;
+        cut_key = static_cast<uint32_t>(k);
+        cut_mass_above = cum;
+        cut_target = t;
       }
     }
     __syncthreads();
+    const double target = cut_target;
     if (!cut_found) {
       keep_all = true;
     } else {
+      // Pass 3: mass per low byte within the selected high byte.
       const uint32_t hi = cut_key;
-      // Level 2: mass per low byte within the selected high byte.
       __syncthreads();
-      for (int b = tid; b < 256; b += kSampleThreads) hist[b] = 0.f;
-      __syncthreads();
-      for (int i = tid; i < V; i += kSampleThreads) {
-        const __nv_bfloat16 v = lg[i];
-        const uint32_t k = bf16_key(v);
-        if ((k >> 8) == hi) atomicAdd(&hist[k & 255u], expf(__fdiv_rn(__bfloat162float(v), T) - m));
+      for (int k = lane; k < 256; k += 32) whist[warp][k] = 0.f;
+      __syncwarp();
+      for (int base = g_begin; base < g_end; base += 32 * kSampleUnroll) {
+        uint32_t b[kSampleUnroll][8];
+        int n[kSampleUnroll];
+        load_groups(lg, base, g_end, V, vec_ok, b, n);
+#pragma unroll
+        for (int u = 0; u < kSampleUnroll; ++u)
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint32_t k = bf16_key_bits(b[u][e]);
+            if (e < n[u] && (k >> 8) == hi && bits_to_float(b[u][e]) >= x_floor) {
+              const float w = weight(b[u][e]);
+              if (w > kNegligibleWeight) atomicAdd(&whist[warp][k & 255u], w);
+            }
+          }
       }
       __syncthreads();
-      if (tid == 0) {
-        float cum = cut_mass_above;
-        int found = 0;
-        for (int b = 255; b >= 0; --b) {
-          if (hist[b] > 0.f && cum <= target && target < cum + hist[b]) {
-            cut_key = (hi << 8) | static_cast<uint32_t>(b);
-            cut_mass_above = cum;
-            found = 1;
-            break;
-          }
-          cum += hist[b];
+      if (tid < 256) {
+        double t = 0.0;
+        for (int w = 0; w < kSampleWarps; ++w) t += whist[w][tid];
+        hist[tid] = t;
+      }
+      __syncthreads();
+      if (warp == 0) {
+        double cum = 0.0, total = 0.0;
+        const int k = warp_find_cut(hist, cut_mass_above, target, true, &cum, &total);
+        if (lane == 0) {
+          cut_found = k >= 0;
+          cut_key = (hi << 8) | static_cast<uint32_t>(k);
+          cut_mass_above = cum;
         }
-        cut_found = found;
       }
       __syncthreads();
       if (!cut_found) {
@@ -177,64 +294,130 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) 
       } else {
         key_star = cut_key;
         // All tokens sharing key_star share one probability e_star.
-        const uint16_t bits = (key_star & 0x8000u) ? static_cast<uint16_t>(key_star & 0x7FFFu)
-                                                   : static_cast<uint16_t>(~key_star & 0xFFFFu);
-        const float e_star = expf(__fdiv_rn(__bfloat162float(__ushort_as_bfloat16(bits)), T) - m);
-        const float room = target - cut_mass_above;
-        n_tie_keep = static_cast<int>(floorf(room / e_star)) + 1;
+        const uint32_t bits = (key_star & 0x8000u) ? (key_star & 0x7FFFu) : (~key_star & 0xFFFFu);
+        const double e_star = weight(bits);
+        const double room = target - cut_mass_above;
+        n_tie_keep = static_cast<int>(floor(room / e_star)) + 1;
       }
     }
   }
 
-  // Passes 5 + 6: contiguous chunks in index order; kept mass per chunk, scan, locate u * M.
-  const int chunk = (V + kSampleThreads - 1) / kSampleThreads;
-  const int c0 = min(V, tid * chunk), c1 = min(V, c0 + chunk);
-  // Rank of this chunk's first tie among all ties (index order).
-  int ties = 0;
-  if (!keep_all)
-    for (int i = c0; i < c1; ++i) ties += bf16_key(lg[i]) == key_star;
-  double unused;
-  const int tie_before = static_cast<int>(block_exclusive_scan(static_cast<double>(ties), dred, &unused));
-  double kept_sum = 0.0;
-  int last_kept = -1;
-  {
-    int rank = tie_before;
-    for (int i = c0; i < c1; ++i) {
-      const __nv_bfloat16 v = lg[i];
+  // Pass 4: tokens tied at key_star before each warp's segment (index order).
+  int tie_base = 0;
+  if (!keep_all) {
+    int ties = 0;
+    for (int base = g_begin; base < g_end; base += 32 * kSampleUnroll) {
+      uint32_t b[kSampleUnroll][8];
+      int n[kSampleUnroll];
+      load_groups(lg, base, g_end, V, vec_ok, b, n);
+#pragma unroll
+      for (int u = 0; u < kSampleUnroll; ++u)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ties += (e < n[u] && bf16_key_bits(b[u][e]) == key_star);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ties += __shfl_xor_sync(0xffffffffu, ties, o);
+    int total_ties;
+    tie_base = warps_exclusive_scan(ties, ired, &total_ties);
+  }
+  // Kept mass of this lane's group, in index order; `rank` is the lane's first tie rank.
+  auto group_mass = [&](const uint32_t (&b)[8], int n, int g, int rank, double& mass, int& last) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (e >= n) continue;
       bool kept = keep_all;
       if (!kept) {
-        const uint32_t k = bf16_key(v);
+        const uint32_t k = bf16_key_bits(b[e]);
         kept = k > key_star || (k == key_star && rank++ < n_tie_keep);
       }
       if (kept) {
-        kept_sum += expf(__fdiv_rn(__bfloat162float(v), T) - m);
-        last_kept = i;
+        mass += static_cast<double>(weight(b[e]));
+        last = 8 * g + e;
+      }
+    }
+  };
+  auto group_ties = [&](const uint32_t (&b)[8], int n) {
+    int t = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) t += (!keep_all && e < n && bf16_key_bits(b[e]) == key_star);
+    return t;
+  };
+
+  // Pass 5: kept mass per warp segment, then their scan.
+  double seg_mass = 0.0;
+  int last_kept = -1;
+  {
+    int rank_base = tie_base;
+    for (int base = g_begin; base < g_end; base += 32 * kSampleUnroll) {
+      uint32_t b[kSampleUnroll][8];
+      int n[kSampleUnroll];
+      load_groups(lg, base, g_end, V, vec_ok, b, n);
+#pragma unroll
+      for (int u = 0; u < kSampleUnroll; ++u) {
+        const int g = base + 32 * u + lane;
+        const int t = n[u] ? group_ties(b[u], n[u]) : 0;
+        const int t_incl = warp_inclusive_scan(t);
+        double mass = 0.0;
+        if (n[u]) group_mass(b[u], n[u], g, rank_base + t_incl - t, mass, last_kept);
+        seg_mass += mass;
+        rank_base += __shfl_sync(0xffffffffu, t_incl, 31);
       }
     }
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) seg_mass += __shfl_xor_sync(0xffffffffu, seg_mass, o);
   double total;
-  const double before = block_exclusive_scan(kept_sum, dred, &total);
+  const double before = warps_exclusive_scan(seg_mass, dred, &total);
   const int glast = block_reduce(last_kept, [](int a, int b) { return max(a, b); }, ired);
   const double target = static_cast<double>(p.uniforms[row]) * total;
   if (tid == 0) chosen = glast;
   __syncthreads();
-  if (kept_sum > 0.0 && before <= target && target < before + kept_sum) {
+
+  // Pass 6: the warp whose segment holds the target walks it in index order.
+  if (seg_mass > 0.0 && before <= target && target < before + seg_mass) {
     double run = before;
-    int rank = tie_before;
-    for (int i = c0; i < c1; ++i) {
-      const __nv_bfloat16 v = lg[i];
-      bool kept = keep_all;
-      if (!kept) {
-        const uint32_t k = bf16_key(v);
-        kept = k > key_star || (k == key_star && rank++ < n_tie_keep);
-      }
-      if (kept) {
-        run += expf(__fdiv_rn(__bfloat162float(v), T) - m);
-        if (run > target) {
-          atomicMin(&chosen, i);
-          break;
+    int rank_base = tie_base;
+    for (int base = g_begin; base < g_end; base += 32) {
+      const int g = base + lane;
+      uint32_t b[8];
+      const int n = g < g_end ? load_group(lg, g, V, vec_ok, b) : 0;
+      const int t = n ? group_ties(b, n) : 0;
+      const int t_incl = warp_inclusive_scan(t);
+      double mass = 0.0;
+      int unused = -1;
+      if (n) group_mass(b, n, g, rank_base + t_incl - t, mass, unused);
+      const double m_incl = warp_inclusive_scan(mass);
+      const double step_total = __shfl_sync(0xffffffffu, m_incl, 31);
+      if (run + step_total > target) {
+        // The first lane whose running mass passes the target holds the draw (when rounding
+        // leaves none, the last lane with kept mass in this step).
+        const unsigned has = __ballot_sync(0xffffffffu, mass > 0.0);
+        const unsigned passed = __ballot_sync(0xffffffffu, mass > 0.0 && run + m_incl > target);
+        const int owner = passed ? __ffs(passed) - 1 : 31 - __clz(has);
+        if (has != 0u && lane == owner) {
+          double r = run + m_incl - mass;
+          int rank = rank_base + t_incl - t;
+          int pick = -1, lane_last = -1;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            if (e >= n) continue;
+            bool kept = keep_all;
+            if (!kept) {
+              const uint32_t k = bf16_key_bits(b[e]);
+              kept = k > key_star || (k == key_star && rank++ < n_tie_keep);
+            }
+            if (kept && pick < 0) {
+              r += static_cast<double>(weight(b[e]));
+              lane_last = 8 * g + e;
+              if (r > target) pick = lane_last;
+            }
+          }
+          atomicMin(&chosen, pick >= 0 ? pick : lane_last);
         }
+        break;  // uniform: every lane saw the same step total
       }
+      run += step_total;
+      rank_base += __shfl_sync(0xffffffffu, t_incl, 31);
     }
   }
   __syncthreads();

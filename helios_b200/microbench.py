@@ -1,6 +1,6 @@
 """Kernel microbenchmarks at the BASELINE config-3 tick shapes, timed from CUDA-graph replays.
 
-    python -m helios_b200.microbench [norm_rope] [swiglu] [add_rmsnorm] [prefill] [decode] [mixed[:N]]
+    python -m helios_b200.microbench [norm_rope] [swiglu] [add_rmsnorm] [prefill] [decode] [mixed[:N]] [prefix_decode] [sample]
                                      [gate_up_fused] [gate_up_cublas] [qkv_fused] [qkv_fused_full_tables] [qkv_cublas]
 
 Each case captures 24 calls of one entry point into a CUDA graph, cycling over input sets
@@ -173,6 +173,56 @@ def _attention(dev, lengths, counts, sets):
     return calls, kv_bytes
 
 
+def _prefix_decode(dev, sets):
+    """BASELINE config 4's decode attention: 128 rows share a 4096-token prefix (16 pages restored
+    by page aliasing), each with its own tail of U[256, 1024] tokens, one query token per row.
+    Reported bytes are the K/V the rows read (the shared pages once per row)."""
+    cfg = Qwen3Config(n_layers=1, context_length=8192)
+    rng = torch.Generator().manual_seed(3)
+    tails = torch.randint(256, 1025, (128,), generator=rng).tolist()
+    calls, kv_bytes = [], sum(4096 + t + 1 for t in tails) * HKV * D * 2 * 2
+    for seed in range(sets):
+        g = torch.Generator().manual_seed(seed)
+        pages = 16 + sum(math.ceil((4096 + t + 1) / 256) - 16 for t in tails) + 4
+        pool = KVPagePool(cfg, pages, device=dev)
+        pool.storage.normal_(0.0, 0.3)
+        pool._free = list(reversed(torch.randperm(pages, generator=g).tolist()))  # pages in random order
+        prefix = PagedKVCache(pool, 4096)
+        prefix.pages.extend(pool.acquire(16))
+        prefix.length = 4096
+        block = prefix.snapshot_block(0, 4096)
+        caches = []
+        for tail in tails:
+            cache = PagedKVCache(pool, 4096 + tail + 8)
+            cache.restore_blocks([block])  # the shared pages, aliased
+            cache.pages.extend(pool.acquire(math.ceil((4096 + tail) / 256) - 16))
+            cache.length = 4096 + tail
+            caches.append(cache)
+        batch = PackedBatchCache(caches)
+        batch.prepare_packed([1] * len(caches))
+        q = torch.randn(len(caches), H, D, device=dev).to(torch.bfloat16)
+        out = torch.empty_like(q)
+        calls.append((lambda q=q, pool=pool, batch=batch, out=out, caches=caches, prefix=prefix:
+                      ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out)))
+    return calls, kv_bytes
+
+
+def _sample(dev, g):
+    """BASELINE config 4's sampling: 128 rows over the Qwen3 vocabulary (151936), temperature 0.2,
+    top-p 0.95. Bytes: one read of the bf16 logits."""
+    vocab, rows = 151936, 128
+
+    def make():
+        logits = (torch.randn(rows, vocab, device=dev, generator=g) * 3).to(torch.bfloat16)
+        temperature = torch.full((rows,), 0.2, device=dev)
+        top_p = torch.full((rows,), 0.95, device=dev)
+        uniforms = torch.rand(rows, device=dev, generator=g)
+        out = torch.empty(rows, dtype=torch.long, device=dev)
+        return lambda: ops.sample(logits, temperature, top_p, uniforms, out)
+
+    return [make() for _ in range(4)], rows * vocab * 2
+
+
 def main(argv: list[str]) -> None:
     if not torch.cuda.is_available():
         raise SystemExit("the microbenchmarks need a CUDA device")
@@ -187,6 +237,8 @@ def main(argv: list[str]) -> None:
         "prefill": lambda: _attention(dev, [0], [2048], 1),
         "decode": lambda: _attention(dev, decode_lengths, [1] * 32, 2),
         "mixed": lambda: _attention(dev, decode_lengths + [0], [1] * 32 + [2048], 2),
+        "prefix_decode": lambda: _prefix_decode(dev, 2),
+        "sample": lambda: _sample(dev, g),
         "gate_up_fused": lambda: _gate_up(dev, g, True),
         "gate_up_cublas": lambda: _gate_up(dev, g, False),
         "qkv_fused": lambda: _qkv(dev, g, True),
