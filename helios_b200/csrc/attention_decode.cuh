@@ -5,7 +5,8 @@
 // window_size=(-1, 0), num_splits=1), src/helios/runtime/qwen3/paged_cache.py:501-520;
 // PagedBatchCache.attend, :301-333). The reference runs with num_splits=1, which
 // leaves most SMs idle when a tick holds few long decode rows; here the work unit is
-// (row, split of split_keys keys, KV head).
+// (row, split of split_keys keys, KV head), or (group of rows sharing a prefix, split of the
+// prefix keys, KV head): see the decode item layout in tick_pack.cuh.
 //
 // Semantics (bottom-right causal, as the reference's window_size=(-1, 0)): query
 // i of a row with `count` queries and `end = seqused_k` keys sits at key position
@@ -33,6 +34,8 @@
 //                             tensor-bound).
 #pragma once
 
+#include <climits>
+
 #include "hb_common.cuh"
 
 namespace hb {
@@ -43,7 +46,10 @@ struct AttentionParams {
   const int32_t* block_table;  // [B, W]
   const int32_t* cu_seq_q;     // [B+1]
   const int32_t* seqused_k;    // [B]
-  const int32_t* decode_items;   // [n][4] row, split, partial_base, n_splits
+  const int32_t* decode_items;   // [n][6] row, first key, end key, record or prefix split, splits, group rows
+  const int32_t* row_records;    // [rows+1] first partial record of each row
+  int32_t num_rows;
+  int32_t record_capacity;       // partial records the workspace holds
   const int32_t* prefill_items;  // [n][3] row, query start of tile 2i, of tile 2i+1 or -1
   // Optional device counts {decode items, prefill pairs, partial records} written by the
   // tick-pack kernel: when set, grids are sized to capacities and CTAs past a count exit
@@ -82,24 +88,32 @@ constexpr int kMergeStride = 132;  // floats per row of the split merge scratch 
 // The key-split merge writes the accumulators of at most 3 warps into one stage.
 static_assert((kDecConsumerWarps - 1) * 16 * kMergeStride * 4 <= kDecStageBytes, "merge scratch fits a stage");
 
-// What a consumer warp needs to know about its unit.
+// What a consumer warp needs to know about its unit. A group unit (group > 0) holds the
+// single query token of rows row .. row + group - 1 against their shared prefix keys: no
+// causal mask inside the prefix, and query row j writes record row_records[row + j / GROUP]
+// + split (the prefix split index).
 struct DecodeUnit {
-  int h, pbase, nsplit, q0, count, end, kb, ke, n_tiles;
+  int h, row, q0, count, end, kb, ke, n_tiles, rec, nsplit, group;
   int qrows, key_split, kpw, mt, kpart;
 };
 
+constexpr int kDecodeItemInts = 6;
+
+// From decode item `it` (the tick-pack layout), q0 / count / end of its row or group.
 template <int GROUP>
-__device__ __forceinline__ DecodeUnit decode_unit(const AttentionParams& p, int h, int split, int pbase, int nsplit,
+__device__ __forceinline__ DecodeUnit decode_unit(const AttentionParams& p, int h, const int4& ia, const int2& ib,
                                                   int q0, int count, int end, int consumer_warp) {
   DecodeUnit u;
   u.h = h;
-  u.pbase = pbase;
-  u.nsplit = nsplit;
+  u.row = ia.x;
+  u.kb = ia.y;
+  u.ke = ia.z;
+  u.rec = ia.w;
+  u.nsplit = ib.x;
+  u.group = ib.y;
   u.q0 = q0;
   u.count = count;
   u.end = end;
-  u.kb = split * p.split_keys;
-  u.ke = min(end, u.kb + p.split_keys);
   u.n_tiles = (u.ke - u.kb + kDecTileKeys - 1) / kDecTileKeys;
   u.qrows = count * GROUP;
   const int m_tiles = u.qrows <= 16 ? 1 : (u.qrows <= 32 ? 2 : 4);
@@ -108,6 +122,32 @@ __device__ __forceinline__ DecodeUnit decode_unit(const AttentionParams& p, int 
   u.mt = consumer_warp / u.key_split;
   u.kpart = consumer_warp % u.key_split;
   return u;
+}
+
+// The decode item as two vectors plus its row's (or group's) query range and key end.
+__device__ __forceinline__ void decode_item(const AttentionParams& p, int index, int4& ia, int2& ib, int& q0,
+                                            int& count, int& end) {
+  const int32_t* it = p.decode_items + kDecodeItemInts * index;
+  ia = make_int4(it[0], it[1], it[2], it[3]);
+  ib = make_int2(it[4], it[5]);
+  q0 = p.cu_seq_q[ia.x];
+  count = ib.y > 0 ? ib.y : p.cu_seq_q[ia.x + 1] - q0;
+  end = ib.y > 0 ? ia.z : p.seqused_k[ia.x];
+  if (ib.y > 0) {  // a group's rows and their single tokens must exist
+    const int limit = max(0, min(p.num_rows - ia.x, p.tokens - q0));
+    if (count > limit) {
+      raise_status(kStatusBadRow);
+      count = limit;
+      ib.y = limit;
+    }
+  }
+}
+
+// Key position limit of query row j (bottom-right causal); group units see every key.
+template <int GROUP>
+__device__ __forceinline__ int decode_qpos(const DecodeUnit& u, int j) {
+  if (j >= u.qrows) return -1;
+  return u.group > 0 ? INT_MAX : u.end - u.count + j / GROUP;
 }
 
 // Query A-fragments for rows mt*16 + g4 and +8 of the unit: 8 k-steps of 16 dims.
@@ -304,7 +344,21 @@ __device__ __forceinline__ void decode_store(const AttentionParams& p, const Dec
     const float m = half ? m_b : m_a, l = half ? l_b : l_a;
     const float inv = l > 0.f ? 1.f / l : 0.f;
     const int tq = j / GROUP, head = u.h * GROUP + j % GROUP;
-    if (u.nsplit == 1) {
+    if (u.group > 0) {  // member row u.row + tq, prefix split u.rec
+      const int r = p.row_records[u.row + tq] + u.rec;
+      if (r < 0 || r >= p.record_capacity) {
+        raise_status(kStatusBadRow);
+        continue;
+      }
+      const int64_t rec = static_cast<int64_t>(r) * p.heads + head;
+      float* o = p.ws_out + rec * D;
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        const int col = n * 8 + 2 * c4;
+        *reinterpret_cast<float2*>(o + col) = make_float2(acc[n][2 * half] * inv, acc[n][2 * half + 1] * inv);
+      }
+      if (c4 == 0) p.ws_lse[rec] = l > 0.f ? m + log2f(l) : -INFINITY;
+    } else if (u.nsplit == 1) {
       __nv_bfloat16* o = p.out + (static_cast<int64_t>(u.q0 + tq) * p.heads + head) * D;
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
@@ -312,7 +366,11 @@ __device__ __forceinline__ void decode_store(const AttentionParams& p, const Dec
         *reinterpret_cast<uint32_t*>(o + col) = pack_bf16(acc[n][2 * half] * inv, acc[n][2 * half + 1] * inv);
       }
     } else {
-      const int64_t rec = static_cast<int64_t>(u.pbase + tq) * p.heads + head;
+      if (u.rec + tq < 0 || u.rec + tq >= p.record_capacity) {
+        raise_status(kStatusBadRow);
+        continue;
+      }
+      const int64_t rec = static_cast<int64_t>(u.rec + tq) * p.heads + head;
       float* o = p.ws_out + rec * D;
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
@@ -361,11 +419,12 @@ __global__ void __launch_bounds__(kDecSubThreads, 2) decode_attention_kernel(Att
   pdl_trigger();  // the prefill kernel (or the split combine) may launch behind this grid
   if (p.counts != nullptr && static_cast<int>(blockIdx.x) >= p.counts[0]) return;  // past this tick's items
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int32_t* item = p.decode_items + 4 * blockIdx.x;
-  const int row = item[0];
-  const int q0 = p.cu_seq_q[row];
-  const DecodeUnit u = decode_unit<GROUP>(p, blockIdx.y, item[1], item[2], item[3], q0, p.cu_seq_q[row + 1] - q0,
-                                          p.seqused_k[row], warp);
+  int4 ia;
+  int2 ib;
+  int q0, count, end;
+  decode_item(p, blockIdx.x, ia, ib, q0, count, end);
+  const int row = ia.x;
+  const DecodeUnit u = decode_unit<GROUP>(p, blockIdx.y, ia, ib, q0, count, end, warp);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kDecStages; ++s) {
@@ -407,8 +466,7 @@ __global__ void __launch_bounds__(kDecSubThreads, 2) decode_attention_kernel(Att
   decode_load_q<GROUP>(p, u, lane, qa);
   // Key position limit per query row (bottom-right causal) for rows g4, g4+8.
   const int ja = u.mt * 16 + g4, jb = ja + 8;
-  const int qpos_a = ja < u.qrows ? u.end - u.count + ja / GROUP : -1;
-  const int qpos_b = jb < u.qrows ? u.end - u.count + jb / GROUP : -1;
+  const int qpos_a = decode_qpos<GROUP>(u, ja), qpos_b = decode_qpos<GROUP>(u, jb);
   float acc[16][4];
 #pragma unroll
   for (int n = 0; n < 16; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
@@ -445,9 +503,9 @@ __global__ void __launch_bounds__(kDecPersistentThreads, 1) decode_persistent_ke
   __shared__ uint64_t full_bars[kDecSubs][kDecStages], empty_bars[kDecSubs][kDecStages];
   __shared__ int abort_flag;
   __shared__ float merge_ml[kDecSubs][kDecConsumerWarps][16][2];
-  // The unit whose first tile a stage holds, with its metadata: {unit, row, split, partial
-  // base}, {splits, first query, queries, keys}; unit -1: no more units for this half.
-  __shared__ int4 unit_meta[kDecSubs][kDecStages][2];
+  // The unit whose first tile a stage holds, with its metadata: {unit, row, first key, end
+  // key}, {record, splits, group rows, first query}, {queries, keys}; unit -1: no more units.
+  __shared__ int4 unit_meta[kDecSubs][kDecStages][3];
 
   pdl_wait();     // q, K and V from the norm/RoPE/append kernel ahead of this one
   pdl_trigger();  // the prefill kernel (or the split combine) may launch behind this grid
@@ -483,27 +541,28 @@ __global__ void __launch_bounds__(kDecPersistentThreads, 1) decode_persistent_ke
       bool ok = true;
       // Units are claimed two ahead and the next unit's metadata is loaded while this one's
       // tiles stream, so the ring keeps filling across unit boundaries.
+      auto load_meta = [&](int unit, int4& a, int4& b, int4& c) {
+        int4 ia;
+        int2 ib;
+        int q0, count, end;
+        decode_item(p, unit / p.kv_heads, ia, ib, q0, count, end);
+        a = make_int4(unit, ia.x, ia.y, ia.z);
+        b = make_int4(ia.w, ib.x, ib.y, q0);
+        c = make_int4(count, end, 0, 0);
+      };
       int u = atomicAdd(p.work_counter, 1);
       int u_next = atomicAdd(p.work_counter, 1);
-      int4 a = make_int4(0, 0, 0, 0), b = a;  // this unit: {u, row, split, pbase}, {nsplit, q0, count, end}
-      if (u < units) {
-        const int32_t* item = p.decode_items + 4 * (u / p.kv_heads);
-        a = make_int4(u, item[0], item[1], item[2]);
-        const int q0 = p.cu_seq_q[a.y];
-        b = make_int4(item[3], q0, p.cu_seq_q[a.y + 1] - q0, p.seqused_k[a.y]);
-      }
+      int4 a = make_int4(0, 0, 0, 0), b = a, c = a;
+      if (u < units) load_meta(u, a, b, c);
       while (ok && u < units) {
-        int4 na = make_int4(0, 0, 0, 0), nb = na;
+        int4 na = make_int4(0, 0, 0, 0), nb = na, nc = na;
         int u_after = units;
         if (u_next < units) {  // issued now, used after this unit's tiles
-          const int32_t* item = p.decode_items + 4 * (u_next / p.kv_heads);
-          na = make_int4(u_next, item[0], item[1], item[2]);
-          nb.x = item[3];
+          load_meta(u_next, na, nb, nc);
           u_after = atomicAdd(p.work_counter, 1);
         }
         const int h = u % p.kv_heads, row = a.y;
-        const int kb = a.z * p.split_keys;
-        const int ke = min(b.w, kb + p.split_keys);
+        const int kb = a.z, ke = a.w;
         const int n_tiles = (ke - kb + kDecTileKeys - 1) / kDecTileKeys;
         int cached_pidx = -1, cached_page = -1;
         for (int t = 0; t < n_tiles; ++t) {
@@ -513,8 +572,9 @@ __global__ void __launch_bounds__(kDecPersistentThreads, 1) decode_persistent_ke
             break;
           }
           if (t == 0) {  // published by the expect_tx arrive of the tile's issue
-            metas[2 * stage] = a;
-            metas[2 * stage + 1] = b;
+            metas[3 * stage] = a;
+            metas[3 * stage + 1] = b;
+            metas[3 * stage + 2] = c;
           }
           if (!decode_issue_tile(p, &kmap, &vmap, smem + stage * kDecStageBytes, &full_bar[stage], row, h,
                                  kb + t * kDecTileKeys, cached_pidx, cached_page)) {
@@ -523,23 +583,18 @@ __global__ void __launch_bounds__(kDecPersistentThreads, 1) decode_persistent_ke
             break;
           }
           ++it;
-          if (t == 0 && u_next < units) {  // the next unit's row-dependent metadata
-            const int q0 = p.cu_seq_q[na.y];
-            nb.y = q0;
-            nb.z = p.cu_seq_q[na.y + 1] - q0;
-            nb.w = p.seqused_k[na.y];
-          }
         }
         u = u_next;
         u_next = u_after;
         a = na;
         b = nb;
+        c = nc;
       }
       // End of work: a stage tagged -1, completed by a plain arrive (no bytes).
       if (ok) {
         const int stage = it % kDecStages;
         if (it < kDecStages || mbar_wait(&empty_bar[stage], ((it / kDecStages) - 1) & 1, &abort_flag)) {
-          metas[2 * stage] = make_int4(-1, 0, 0, 0);
+          metas[3 * stage] = make_int4(-1, 0, 0, 0);
           mbar_arrive(&full_bar[stage]);
         } else {
           ok = false;
@@ -563,15 +618,16 @@ __global__ void __launch_bounds__(kDecPersistentThreads, 1) decode_persistent_ke
     const bool got = mbar_wait(&full_bar[it % kDecStages], (it / kDecStages) & 1, &abort_flag);
     sync();
     if (!got || abort_flag) break;
-    const int4 ma = metas[2 * (it % kDecStages)];
+    const int4 ma = metas[3 * (it % kDecStages)];
     if (ma.x < 0) break;
-    const int4 mb = metas[2 * (it % kDecStages) + 1];
-    const DecodeUnit u = decode_unit<GROUP>(p, ma.x % p.kv_heads, ma.z, ma.w, mb.x, mb.y, mb.z, mb.w, cw);
+    const int4 mb = metas[3 * (it % kDecStages) + 1];
+    const int4 mc = metas[3 * (it % kDecStages) + 2];
+    const DecodeUnit u = decode_unit<GROUP>(p, ma.x % p.kv_heads, make_int4(ma.y, ma.z, ma.w, mb.x),
+                                            make_int2(mb.y, mb.z), mb.w, mc.x, mc.y, cw);
     uint32_t qa[8][4];
     decode_load_q<GROUP>(p, u, lane, qa);
     const int ja = u.mt * 16 + g4, jb = ja + 8;
-    const int qpos_a = ja < u.qrows ? u.end - u.count + ja / GROUP : -1;
-    const int qpos_b = jb < u.qrows ? u.end - u.count + jb / GROUP : -1;
+    const int qpos_a = decode_qpos<GROUP>(u, ja), qpos_b = decode_qpos<GROUP>(u, jb);
     float acc[16][4];
 #pragma unroll
     for (int n = 0; n < 16; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
@@ -610,8 +666,10 @@ __global__ void __launch_bounds__(kDecPersistentThreads, 1) decode_persistent_ke
 }
 
 // Merge the splits of every multi-split decode row: out = sum_s w_s o_s / sum_s w_s
-// with w_s = 2^(lse_s - max lse). One CTA per (split-0 item, KV head); each warp merges
-// one query row, lane l owning dims 4l..4l+3, so every split's loads are in flight at once.
+// with w_s = 2^(lse_s - max lse). One CTA per (row, KV head): the row's records are
+// row_records[r] .. row_records[r + 1], split s of query token tq at + s * count + tq (rows
+// with one split wrote their output directly; prefill rows have none). Each warp merges one
+// query row, lane l owning dims 4l..4l+3, so every split's loads are in flight at once.
 constexpr int kCombineMaxSplits = 8;
 
 template <int GROUP>
@@ -619,13 +677,17 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(AttentionParams p) 
   constexpr int D = 128;
   pdl_wait();  // the kernel ahead (decode, or prefill, which completes after decode) has finished
   if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *p.work_counter = 0;  // for the next call
-  if (p.counts != nullptr && static_cast<int>(blockIdx.x) >= p.counts[0]) return;
-  const int32_t* item = p.decode_items + 4 * blockIdx.x;
-  if (item[1] != 0 || item[3] <= 1) return;
-  const int row = item[0], pbase = item[2], nsplit = item[3];
-  const int h = blockIdx.y;
+  const int row = blockIdx.x, h = blockIdx.y;
   const int q0 = p.cu_seq_q[row];
   const int count = p.cu_seq_q[row + 1] - q0;
+  const int pbase = p.row_records[row];
+  const int records = p.row_records[row + 1] - pbase;
+  if (count <= 0 || records <= count) return;  // one split (written directly) or a prefill row
+  if (pbase < 0 || pbase + records > p.record_capacity) {
+    if (threadIdx.x == 0) raise_status(kStatusBadRow);
+    return;
+  }
+  const int nsplit = records / count;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int j = warp; j < count * GROUP; j += 4) {
     const int tq = j / GROUP, head = h * GROUP + j % GROUP;

@@ -219,7 +219,7 @@ int hb_tick_pack(const int32_t* rows, int32_t num_rows, const int32_t* updates, 
                  int32_t* block_table, int32_t* cu_seq_q, int32_t* cu_seq_k, int32_t* seqused_k, int64_t* positions,
                  int64_t* write_slots, int32_t* token_row, int64_t* logit_indices, int32_t logit_capacity,
                  int32_t* decode_items, int32_t decode_capacity, int32_t* prefill_items, int32_t prefill_capacity,
-                 int32_t* counts, cudaStream_t stream) {
+                 int32_t* counts, int32_t* row_records, cudaStream_t stream) {
   if (num_rows < 1 || num_rows > HB_MAX_TICK_ROWS)
     return fail(HB_ERR_INVALID, "num_rows %d outside [1, %d]", num_rows, HB_MAX_TICK_ROWS);
   if (rows == nullptr || arena == nullptr || block_table == nullptr || cu_seq_q == nullptr || cu_seq_k == nullptr ||
@@ -238,7 +238,7 @@ int hb_tick_pack(const int32_t* rows, int32_t num_rows, const int32_t* updates, 
   hb::TickPackParams p{rows, updates, arena, num_rows, num_updates, arena_width, arena_slots, page_size, width,
                        num_pages, decode_max_tokens, split_keys, prefill_tile_tokens, block_table, cu_seq_q, cu_seq_k,
                        seqused_k, positions, write_slots, token_row, logit_indices, decode_items, prefill_items,
-                       total_tokens, logit_capacity, decode_capacity, prefill_capacity, counts};
+                       total_tokens, logit_capacity, decode_capacity, prefill_capacity, counts, row_records};
   const int smem = 6 * (num_rows + 1) * static_cast<int>(sizeof(int32_t));
   if (int rc = ensure_smem(hb::tick_pack_kernel, 6 * (HB_MAX_TICK_ROWS + 1) * 4, g_tick_smem)) return rc;
   hb::tick_pack_kernel<<<1, hb::kTickThreads, smem, stream>>>(p);
@@ -295,7 +295,8 @@ size_t hb_attention_workspace_bytes(int32_t partial_records, int32_t heads, int3
 
 int hb_paged_attention(const void* q, const void* key_pool, const void* value_pool, int64_t num_pages,
                        int32_t page_size, const int32_t* block_table, int32_t width, const int32_t* cu_seq_q,
-                       const int32_t* seqused_k, const int32_t* decode_items, int32_t num_decode_items,
+                       const int32_t* seqused_k, int32_t num_rows, const int32_t* row_records,
+                       const int32_t* decode_items, int32_t num_decode_items,
                        const int32_t* prefill_items, int32_t num_prefill_items, const int32_t* counts,
                        int32_t partial_records, int32_t split_keys, int32_t total_tokens, int32_t heads,
                        int32_t kv_heads, int32_t head_dim, float scale, void* workspace, size_t workspace_bytes,
@@ -308,8 +309,9 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
   if (page_size % hb::kDecTileKeys != 0 || split_keys % page_size != 0 || split_keys < page_size)
     return fail(HB_ERR_INVALID, "page_size must be a multiple of 64 and split_keys of page_size");
   if (num_decode_items < 0 || num_prefill_items < 0 || total_tokens < 0 || num_pages < 1 || width < 1 ||
-      partial_records < 0)
+      partial_records < 0 || num_rows < 1 || num_rows > HB_MAX_TICK_ROWS)
     return fail(HB_ERR_INVALID, "bad work sizes");
+  if (num_decode_items > 0 && row_records == nullptr) return fail(HB_ERR_INVALID, "null row records");
   if (num_pages * page_size > (int64_t(1) << 31)) return fail(HB_ERR_UNSUPPORTED, "pool exceeds 2^31 tokens");
   if (q == nullptr || key_pool == nullptr || value_pool == nullptr || out == nullptr || block_table == nullptr ||
       cu_seq_q == nullptr || seqused_k == nullptr)
@@ -328,6 +330,9 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
   p.cu_seq_q = cu_seq_q;
   p.seqused_k = seqused_k;
   p.decode_items = decode_items;
+  p.row_records = row_records;
+  p.num_rows = num_rows;
+  p.record_capacity = partial_records;
   p.prefill_items = prefill_items;
   p.work_counter = static_cast<int32_t*>(workspace);
   p.ws_out = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWorkspaceHeader);
@@ -421,7 +426,7 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
 #undef HB_PREFILL
   }
   if (num_decode_items > 0 && (partial_records > 0 || beside)) {  // also resets the decode work ticket
-    const dim3 grid(num_decode_items, kv_heads);
+    const dim3 grid(num_rows, kv_heads);
 #define HB_COMBINE(G)                                                                                          \
   do {                                                                                                         \
     const cudaError_t e = launch_pdl(hb::decode_combine_kernel<G>, grid, dim3(128), 0, stream, p);             \
@@ -447,6 +452,7 @@ int hb_attention_set_overlap(int32_t decode_sms) {
 int hb_paged_attention_static_workspace(const void* q, const void* key_pool, const void* value_pool,
                                        int64_t num_pages, int32_t page_size, const int32_t* block_table,
                                        int32_t width, const int32_t* cu_seq_q, const int32_t* seqused_k,
+                                       int32_t num_rows, const int32_t* row_records,
                                        const int32_t* decode_items, int32_t num_decode_items,
                                        const int32_t* prefill_items, int32_t num_prefill_items,
                                        const int32_t* counts, int32_t partial_records, int32_t split_keys,
@@ -474,7 +480,8 @@ int hb_paged_attention_static_workspace(const void* q, const void* key_pool, con
     ws = g_static_ws_ptr[dev];
   }
   return hb_paged_attention(q, key_pool, value_pool, num_pages, page_size, block_table, width, cu_seq_q, seqused_k,
-                            decode_items, num_decode_items, prefill_items, num_prefill_items, counts, partial_records,
+                            num_rows, row_records, decode_items, num_decode_items, prefill_items, num_prefill_items,
+                            counts, partial_records,
                             split_keys, total_tokens, heads, kv_heads, head_dim, scale, ws, HB_STATIC_WORKSPACE_BYTES,
                             out, stream);
 }

@@ -18,17 +18,31 @@
 //     (count <= decode_max_tokens) and, for prefill-class rows, pairs of adjacent
 //     query tiles (2i, 2i+1) of a row with m tiles. Tiles of at most 32 tokens
 //     (GROUP >= 4) read the same 64-key tiles, so the two stay busy together; larger
-//     tiles differ by at most two key tiles.
+//     tiles differ by at most two key tiles;
+//   * shared-prefix groups: consecutive single-token decode rows whose block tables
+//     start with the same shared_len keys (pages restored by aliasing) form a group. The
+//     group's first row carries group_rows = n. Its keys [0, shared_len) are split once
+//     for all n rows (items with group_rows = n, every query of the group against the
+//     same pages); each row's own items cover only [shared_len, end). The row's partial
+//     records are the prefix splits, then its tail splits, merged by the split combine.
+//
+// Decode item (6 int32): row, first key, end key, then
+//   group_rows == 0: record base of the item (row record base + split * count), splits of the row
+//   group_rows  > 0: the prefix split index s (member i's record: row_records[row + i] + s), unused
+// then group_rows.
 // Every output write is bounded by the capacity the host sized it for; an entry
 // that would fall outside is skipped and reported in the status word.
 #pragma once
 
+#include "attention_decode.cuh"  // kDecodeItemInts: the decode item layout
 #include "hb_common.cuh"
 
 namespace hb {
 
+constexpr int kTickRowFields = 7;  // slot, length, count, logit_count, n_pages, shared_len, group_rows
+
 struct TickPackParams {
-  const int32_t* rows;     // [B][5] slot, length, count, logit_count, n_pages
+  const int32_t* rows;     // [B][kTickRowFields]
   const int32_t* updates;  // [U][3] slot, page position, page index
   int32_t* arena;          // [slots][arena_width]
   int32_t num_rows, num_updates, arena_width, arena_slots, page_size, width, num_pages;
@@ -41,15 +55,38 @@ struct TickPackParams {
   int64_t* write_slots;    // [T]
   int32_t* token_row;      // [T]
   int64_t* logit_indices;  // [logit_capacity]
-  int32_t* decode_items;   // [decode_capacity][4] row, split, partial_base, n_splits
+  int32_t* decode_items;   // [decode_capacity][kDecodeItemInts] (above)
   int32_t* prefill_items;  // [prefill_capacity][3] row, first tile start, second tile start or -1
   int32_t total_tokens, logit_capacity, decode_capacity, prefill_capacity;
   int32_t* counts;         // optional [3]: decode items, prefill pairs, partial records (capped)
+  int32_t* row_records;    // [B+1] first partial record of each row (exclusive prefix)
 };
 
 constexpr int kTickThreads = 1024;
 
 __device__ __forceinline__ int row_splits(int end, int split_keys) { return (end + split_keys - 1) / split_keys; }
+
+// Decode items and partial records of row r (see the header).
+struct RowWork {
+  int items, records, prefix_splits, tail_splits;
+};
+__device__ __forceinline__ RowWork row_work(const TickPackParams& p, int r) {
+  const int32_t* row = p.rows + kTickRowFields * r;
+  const int32_t end = row[1] + row[2], cnt = row[2], shared = row[5], group = row[6];
+  RowWork w{0, 0, 0, 0};
+  if (cnt > p.decode_max_tokens) return w;
+  if (shared > 0) {
+    w.prefix_splits = row_splits(shared, p.split_keys);
+    w.tail_splits = row_splits(end - shared, p.split_keys);
+    w.items = w.tail_splits + (group > 0 ? w.prefix_splits : 0);
+    w.records = (w.prefix_splits + w.tail_splits) * cnt;
+  } else {
+    w.tail_splits = row_splits(end, p.split_keys);
+    w.items = w.tail_splits;
+    w.records = w.tail_splits * cnt;
+  }
+  return w;
+}
 __device__ __forceinline__ int row_prefill_items(int count, int tile_tokens) {
   return ((count + tile_tokens - 1) / tile_tokens + 1) / 2;  // tiles, paired
 }
@@ -82,15 +119,16 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
   const int r0 = min(B, tid * per), r1 = min(B, r0 + per);
   int32_t s[6] = {0, 0, 0, 0, 0, 0};
   for (int r = r0; r < r1; ++r) {
-    const int32_t len = p.rows[5 * r + 1], cnt = p.rows[5 * r + 2], lc = p.rows[5 * r + 3];
+    const int32_t len = p.rows[kTickRowFields * r + 1], cnt = p.rows[kTickRowFields * r + 2];
+    const int32_t lc = p.rows[kTickRowFields * r + 3];
     const int32_t end = len + cnt;
     s[0] += cnt;
     s[1] += end;
     s[2] += lc;
     if (cnt <= p.decode_max_tokens) {
-      const int sp = row_splits(end, p.split_keys);
-      s[3] += sp;
-      s[4] += sp * cnt;
+      const RowWork w = row_work(p, r);
+      s[3] += w.items;
+      s[4] += w.records;
     } else {
       s[5] += row_prefill_items(cnt, p.prefill_tile_tokens);
     }
@@ -125,7 +163,8 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
 #pragma unroll
   for (int f = 0; f < 6; ++f) base[f] = (warp ? warp_tot[warp - 1][f] : 0) + incl[f] - s[f];
   for (int r = r0; r < r1; ++r) {
-    const int32_t len = p.rows[5 * r + 1], cnt = p.rows[5 * r + 2], lc = p.rows[5 * r + 3];
+    const int32_t len = p.rows[kTickRowFields * r + 1], cnt = p.rows[kTickRowFields * r + 2];
+    const int32_t lc = p.rows[kTickRowFields * r + 3];
     const int32_t end = len + cnt;
     q_off[r] = base[0];
     k_off[r] = base[1];
@@ -137,9 +176,9 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
     base[1] += end;
     base[2] += lc;
     if (cnt <= p.decode_max_tokens) {
-      const int sp = row_splits(end, p.split_keys);
-      base[3] += sp;
-      base[4] += sp * cnt;
+      const RowWork w = row_work(p, r);
+      base[3] += w.items;
+      base[4] += w.records;
     } else {
       base[5] += row_prefill_items(cnt, p.prefill_tile_tokens);
     }
@@ -163,9 +202,11 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
   for (int r = tid; r <= B; r += kTickThreads) {
     p.cu_seq_q[r] = q_off[r];
     p.cu_seq_k[r] = k_off[r];
+    if (p.row_records != nullptr) p.row_records[r] = r_off[r];
   }
   for (int r = tid; r < B; r += kTickThreads) {
-    const int32_t len = p.rows[5 * r + 1], cnt = p.rows[5 * r + 2], lc = p.rows[5 * r + 3];
+    const int32_t len = p.rows[kTickRowFields * r + 1], cnt = p.rows[kTickRowFields * r + 2];
+    const int32_t lc = p.rows[kTickRowFields * r + 3];
     const int32_t end = len + cnt;
     p.seqused_k[r] = end;
     for (int i = 0; i < lc; ++i) {
@@ -173,14 +214,32 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
       p.logit_indices[l_off[r] + i] = static_cast<int64_t>(q_off[r + 1] - lc + i);
     }
     if (cnt <= p.decode_max_tokens) {
-      const int sp = row_splits(end, p.split_keys);
-      for (int sidx = 0; sidx < sp; ++sidx) {
-        if (d_off[r] + sidx >= p.decode_capacity) { raise_status(kStatusBadRow); break; }
-        int32_t* it = p.decode_items + 4 * (d_off[r] + sidx);
+      const RowWork w = row_work(p, r);
+      const int32_t shared = p.rows[kTickRowFields * r + 5], group = p.rows[kTickRowFields * r + 6];
+      const int nsplit = w.prefix_splits + w.tail_splits;
+      int at = d_off[r];
+      for (int k = 0; k < w.tail_splits; ++k, ++at) {  // this row's own keys [shared, end)
+        if (at >= p.decode_capacity) { raise_status(kStatusBadRow); break; }
+        int32_t* it = p.decode_items + kDecodeItemInts * at;
+        const int kb = shared + k * p.split_keys;
         it[0] = r;
-        it[1] = sidx;
-        it[2] = r_off[r] + sidx * cnt;
-        it[3] = sp;
+        it[1] = kb;
+        it[2] = min(end, kb + p.split_keys);
+        it[3] = r_off[r] + (w.prefix_splits + k) * cnt;
+        it[4] = nsplit;
+        it[5] = 0;
+      }
+      if (group > 0) {  // the group's shared keys [0, shared), once for its `group` rows
+        for (int k = 0; k < w.prefix_splits; ++k, ++at) {
+          if (at >= p.decode_capacity) { raise_status(kStatusBadRow); break; }
+          int32_t* it = p.decode_items + kDecodeItemInts * at;
+          it[0] = r;
+          it[1] = k * p.split_keys;
+          it[2] = min(shared, (k + 1) * p.split_keys);
+          it[3] = k;
+          it[4] = 0;
+          it[5] = group;
+        }
       }
     } else {
       const int tiles = (cnt + p.prefill_tile_tokens - 1) / p.prefill_tile_tokens;
@@ -198,7 +257,7 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
   const int64_t cells = static_cast<int64_t>(B) * p.width;
   for (int64_t c = tid; c < cells; c += kTickThreads) {
     const int r = static_cast<int>(c / p.width), j = static_cast<int>(c % p.width);
-    const int32_t slot = p.rows[5 * r], npages = p.rows[5 * r + 4];
+    const int32_t slot = p.rows[kTickRowFields * r], npages = p.rows[kTickRowFields * r + 4];
     int32_t v = 0;
     if (j < npages) {
       v = (j < p.arena_width && slot >= 0 && slot < p.arena_slots)
@@ -220,7 +279,8 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
       if (q_off[mid] <= t) lo = mid; else hi = mid;
     }
     const int r = lo;
-    const int32_t slot = p.rows[5 * r], len = p.rows[5 * r + 1], npages = p.rows[5 * r + 4];
+    const int32_t slot = p.rows[kTickRowFields * r], len = p.rows[kTickRowFields * r + 1];
+    const int32_t npages = p.rows[kTickRowFields * r + 4];
     const int32_t pos = len + (t - q_off[r]);
     const int32_t pidx = pos / p.page_size;
     int32_t page = 0;

@@ -14,6 +14,8 @@ import torch
 from helios_b200 import _native
 
 BF16 = torch.bfloat16
+TICK_ROW_FIELDS = 7  # slot, length, count, logit count, pages, shared prefix keys, group rows
+DECODE_ITEM_INTS = 6  # row, first key, end key, record base or prefix split, splits, group rows
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -50,9 +52,9 @@ def tick_pack(rows_dev: torch.Tensor, num_rows: int, updates_dev: torch.Tensor |
         out["block_table"].data_ptr(), out["cu_seq_q"].data_ptr(), out["cu_seq_k"].data_ptr(),
         out["seqused_k"].data_ptr(), out["positions"].data_ptr(), out["write_slots"].data_ptr(),
         out["token_row"].data_ptr(), out["logit_store"].data_ptr(), out["logit_store"].numel(),
-        out["decode_items"].data_ptr(), out["decode_items"].numel() // 4,
+        out["decode_items"].data_ptr(), out["decode_items"].numel() // DECODE_ITEM_INTS,
         out["prefill_items"].data_ptr(), out["prefill_items"].numel() // 3, _ptr(out.get("counts")),
-        _stream(rows_dev.device))
+        _ptr(out.get("row_records")), _stream(rows_dev.device))
     _native.check(rc, "hb_tick_pack")
 
 
@@ -103,6 +105,7 @@ def paged_attention(q: torch.Tensor, key_pool: torch.Tensor, value_pool: torch.T
     rc = lib().hb_paged_attention(
         q.data_ptr(), key_pool.data_ptr(), value_pool.data_ptr(), key_pool.shape[0], key_pool.shape[1],
         meta.block_table.data_ptr(), meta.block_table.shape[1], meta.cu_seq_q.data_ptr(), meta.seqused_k.data_ptr(),
+        meta.batch_size, meta.row_records.data_ptr(),
         meta.decode_items.data_ptr(), meta.launch_decode_items, meta.prefill_items.data_ptr(),
         meta.launch_prefill_items, _ptr(meta.attention_counts), meta.launch_partial_records, meta.split_keys, tokens,
         heads, kv_heads, dim, float(scale),

@@ -38,6 +38,7 @@ from helios_b200 import ops
 from helios_b200.config import Qwen3Config
 
 DECODE_QUERY_ROWS = 64      # query rows (tokens x group heads) one decode CTA holds
+MIN_SHARED_PAGES = 4        # common leading pages from which single-token decode rows share one prefix pass
 PREFILL_TILE_ROWS = 128     # query rows of one tcgen05 prefill tile (a CTA takes a pair of tiles)
 NUM_SMS_B200 = 148
 
@@ -361,7 +362,7 @@ class PagedBatchCache:
         the last tick, and the attention work partition. O(rows + new pages)."""
         pool, config = self.pool, self.pool.config
         page_size = pool.page_size
-        rows = np.empty((self.batch_size, 5), dtype=np.int32)
+        rows = np.zeros((self.batch_size, ops.TICK_ROW_FIELDS), dtype=np.int32)
         updates: list[int] = []
         for r, (cache, count, lc) in enumerate(zip(self.caches, counts, logit_counts)):
             n = len(cache.pages)
@@ -370,23 +371,68 @@ class PagedBatchCache:
                 for j in range(cache._synced, n):
                     updates += (slot, j, cache.pages[j].index)
                 cache._synced = n
-            rows[r] = (cache._slot, cache.length, count, lc, n)
+            rows[r, :5] = (cache._slot, cache.length, count, lc, n)
         group = config.n_heads // config.n_kv_heads
         decode_max = DECODE_QUERY_ROWS // group
         tile_tokens = PREFILL_TILE_ROWS // group
+        self._share_prefixes(rows, decode_max)
         ends = rows[:, 1].astype(np.int64) + rows[:, 2]
         cnts = rows[:, 2].astype(np.int64)
+        shared = rows[:, 5].astype(np.int64)
+        heads = rows[:, 6] > 0
         is_decode = cnts <= decode_max
-        split = choose_split_keys(int(ends[is_decode].sum()) * config.n_kv_heads, page_size)
-        splits = (ends[is_decode] + split - 1) // split
+        # Keys the decode work reads: each row's own keys, each shared prefix once.
+        read = ends - shared + np.where(heads, shared, 0)
+        split = choose_split_keys(int(read[is_decode].sum()) * config.n_kv_heads, page_size)
+        prefix_splits = (shared + split - 1) // split
+        tail_splits = (ends - shared + split - 1) // split
+        items = tail_splits + np.where(heads, prefix_splits, 0)
+        records = (prefix_splits + tail_splits) * cnts
         return {
             "rows": rows, "updates": np.asarray(updates, dtype=np.int32), "decode_max": decode_max,
-            "tile_tokens": tile_tokens, "split_keys": split, "num_decode_items": int(splits.sum()),
-            "partial_records": int((splits * cnts[is_decode]).sum()),
+            "tile_tokens": tile_tokens, "split_keys": split, "num_decode_items": int(items[is_decode].sum()),
+            "partial_records": int(records[is_decode].sum()),
             "num_prefill_items": int(((((cnts[~is_decode] + tile_tokens - 1) // tile_tokens) + 1) // 2).sum()),
             "total_tokens": int(cnts.sum()), "num_logits": int(rows[:, 3].sum()),
             "width": max(_pages_for(cache.capacity, page_size) for cache in self.caches),
         }
+
+    def _share_prefixes(self, rows: np.ndarray, decode_max: int) -> None:
+        """Fill the shared-prefix columns of ``rows``: runs of up to ``decode_max`` consecutive
+        single-token decode rows whose page lists start with the same MIN_SHARED_PAGES or more
+        pages (restored by aliasing) form a group; every member gets the group's common full
+        pages as shared prefix keys and the first member the group size. Their attention reads
+        those pages once for the whole group."""
+        page_size = self.pool.page_size
+        caches = self.caches
+
+        def full_pages(r: int) -> int:  # committed pages a row may share
+            return int(rows[r, 1]) // page_size if rows[r, 2] == 1 else 0
+
+        r, count = 0, len(caches)
+        while r < count:
+            lead = full_pages(r)
+            if lead < MIN_SHARED_PAGES:
+                r += 1
+                continue
+            head = caches[r].pages
+            common, j = lead, r + 1
+            while j < count and j - r < decode_max:
+                limit = min(common, full_pages(j))
+                pages = caches[j].pages
+                lcp = 0
+                while lcp < limit and pages[lcp].index == head[lcp].index:
+                    lcp += 1
+                if lcp < MIN_SHARED_PAGES:
+                    break
+                common = lcp
+                j += 1
+            if j - r >= 2:
+                rows[r:j, 5] = common * page_size
+                rows[r, 6] = j - r
+                r = j
+            else:
+                r += 1
 
     def _pack(self, counts: Sequence[int], logit_counts: Sequence[int]) -> None:
         """Upload the host descriptor and run the tick-pack kernel (kernel a)."""
@@ -435,6 +481,7 @@ class PagedBatchCache:
         self.token_row = out["token_row"]
         self.logit_rows = out["logit_indices"]
         self.decode_items = out["decode_items"]
+        self.row_records = out["row_records"]
         self.prefill_items = out["prefill_items"]
         self.attention_counts = out["counts"] if self.capacity_mode else None
         self.total_tokens = total
@@ -444,7 +491,8 @@ class PagedBatchCache:
         """Views of two reusable device buffers sized for this tick."""
         n_dec = max(1, self.launch_decode_items)
         n_pre = max(1, self.launch_prefill_items)
-        sizes32 = [rows * width, rows + 1, rows + 1, rows, max(tokens, 1), 4 * n_dec, 3 * n_pre, 4]
+        sizes32 = [rows * width, rows + 1, rows + 1, rows, max(tokens, 1), ops.DECODE_ITEM_INTS * n_dec, 3 * n_pre, 4,
+                   rows + 1]
         sizes64 = [max(tokens, 1), max(tokens, 1), max(logits, 1)]
         dev = self.pool.device
         if self._i32 is None or self._i32.numel() < sum(sizes32):
@@ -458,6 +506,7 @@ class PagedBatchCache:
         return {
             "block_table": v32[0].view(rows, width), "cu_seq_q": v32[1], "cu_seq_k": v32[2], "seqused_k": v32[3],
             "token_row": v32[4][:tokens], "decode_items": v32[5], "prefill_items": v32[6], "counts": v32[7][:3],
+            "row_records": v32[8],
             "positions": v64[0][:tokens], "write_slots": v64[1][:tokens], "logit_store": v64[2],
             "logit_indices": v64[2][:logits],
         }

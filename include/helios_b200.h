@@ -59,16 +59,25 @@ HB_API int hb_device_status(uint32_t* status, int clear);
  * (a) Tick packing. Replaces PackedBatchCache.prepare_packed
  * (src/helios/runtime/qwen3/paged_cache.py:418-494) and PagedBatchCache.prepare
  * (paged_cache.py:221-270), whose Python lists are rebuilt and copied every tick.
- *   rows     device int32 [num_rows][5]: arena slot, committed length, query count,
- *            logit count, pages held (after this tick's acquisitions)
+ *   rows     device int32 [num_rows][7]: arena slot, committed length, query count,
+ *            logit count, pages held (after this tick's acquisitions), shared prefix keys,
+ *            group rows. Consecutive single-token decode rows whose block tables start with the
+ *            same pages (restored by aliasing) may form a group: every member has shared prefix
+ *            keys L (a multiple of the page size, at most its length) and the first member has
+ *            group rows = n, the others 0; other rows have 0, 0
  *   updates  device int32 [num_updates][3]: arena slot, page position, page index
  *   arena    device int32 [arena_slots][arena_width]: per-request page lists
  * Outputs (all device): block_table int32 [num_rows][width] (zero-padded),
  * cu_seq_q/cu_seq_k int32 [num_rows+1], seqused_k int32 [num_rows], positions,
  * write_slots int64 [total_tokens], token_row int32 [total_tokens], logit_indices
- * int64 [logit_capacity], decode_items int32 [decode_capacity][4] (row, split,
- * partial base, splits) for rows with count <= decode_max_tokens, split every
- * split_keys keys, prefill_items int32 [prefill_capacity][3] (row, start of query
+ * int64 [logit_capacity], decode_items int32 [decode_capacity][6] for rows with count <=
+ * decode_max_tokens, split every split_keys keys: (row, first key, end key, record base,
+ * splits of the row, 0), and for each group (first row, first key, end key of a split of
+ * the shared keys, its split index, 0, n), run once for the group's n rows.
+ * row_records int32 [num_rows+1] (device, may be null when there are no decode rows) gets
+ * each row's first partial record: a decode row's records are its shared-prefix splits, then
+ * its own splits, each with one record per query token. prefill_items int32
+ * [prefill_capacity][3] (row, start of query
  * tile 2i, start of tile 2i+1 or -1) pairing adjacent tiles of prefill_tile_tokens
  * queries of a row. Entries past a capacity are not written. counts (device int32[3],
  * may be null) receives the number of decode items and prefill pairs written (capped at
@@ -81,7 +90,7 @@ HB_API int hb_tick_pack(const int32_t* rows, int32_t num_rows, const int32_t* up
                         int32_t* seqused_k, int64_t* positions, int64_t* write_slots, int32_t* token_row,
                         int64_t* logit_indices, int32_t logit_capacity, int32_t* decode_items,
                         int32_t decode_capacity, int32_t* prefill_items, int32_t prefill_capacity,
-                        int32_t* counts, cudaStream_t stream);
+                        int32_t* counts, int32_t* row_records, cudaStream_t stream);
 
 /*
  * (b) Fused per-head q/k RMSNorm + RoPE + paged KV append. Replaces, in
@@ -126,7 +135,8 @@ HB_API size_t hb_attention_workspace_bytes(int32_t partial_records, int32_t head
  */
 HB_API int hb_paged_attention(const void* q, const void* key_pool, const void* value_pool, int64_t num_pages,
                               int32_t page_size, const int32_t* block_table, int32_t width, const int32_t* cu_seq_q,
-                              const int32_t* seqused_k, const int32_t* decode_items, int32_t num_decode_items,
+                              const int32_t* seqused_k, int32_t num_rows, const int32_t* row_records,
+                              const int32_t* decode_items, int32_t num_decode_items,
                               const int32_t* prefill_items, int32_t num_prefill_items, const int32_t* counts,
                               int32_t partial_records, int32_t split_keys, int32_t total_tokens, int32_t heads,
                               int32_t kv_heads, int32_t head_dim, float scale, void* workspace,
@@ -159,6 +169,7 @@ HB_API int hb_attention_set_overlap(int32_t decode_sms);
 HB_API int hb_paged_attention_static_workspace(const void* q, const void* key_pool, const void* value_pool,
                                                int64_t num_pages, int32_t page_size, const int32_t* block_table,
                                                int32_t width, const int32_t* cu_seq_q, const int32_t* seqused_k,
+                                               int32_t num_rows, const int32_t* row_records,
                                                const int32_t* decode_items, int32_t num_decode_items,
                                                const int32_t* prefill_items, int32_t num_prefill_items,
                                                const int32_t* counts, int32_t partial_records, int32_t split_keys,

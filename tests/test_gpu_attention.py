@@ -15,7 +15,7 @@ import pytest
 import torch
 
 from helios_b200 import _native, ops
-from helios_b200.paged_cache import KVPagePool, PackedBatchCache
+from helios_b200.paged_cache import KVPagePool, PackedBatchCache, PagedKVCache
 from oracle.attention import paged_attention, write_pool
 from tests.golden.inputs import attention_inputs, digest
 from tests.helpers import attn_config, cache_with_pages, queue_pages
@@ -202,3 +202,60 @@ def _qkv(batch, seed):
     k = (torch.randn(1, 8, T, 128, generator=g) / 3).to(torch.bfloat16).to(DEV)
     v = torch.randn(1, 8, T, 128, generator=g).to(torch.bfloat16).to(DEV)
     return q, k, v
+
+
+def _shared_prefix_batch(tails, prefix_pages, extra_counts=(), seed=7, heads=32, kv_heads=8):
+    """Rows that restored one prefix snapshot (page aliasing) plus their own tails, one query
+    token each, then rows with `extra_counts` tokens and no shared pages."""
+    g = torch.Generator().manual_seed(seed)
+    cfg = attn_config(heads=heads, kv_heads=kv_heads)
+    need = prefix_pages + sum(math.ceil((prefix_pages * 256 + t + 1) / 256) - prefix_pages for t in tails)
+    need += sum(math.ceil((c + 300) / 256) for c in extra_counts) + 4
+    pool = KVPagePool(cfg, need, device=DEV)
+    pool.keys[0].copy_((torch.randn(pool.keys[0].shape, generator=g) / 3).to(torch.bfloat16))
+    pool.values[0].copy_(torch.randn(pool.values[0].shape, generator=g).to(torch.bfloat16))
+    prefix = PagedKVCache(pool, prefix_pages * 256)
+    prefix.pages.extend(pool.acquire(prefix_pages))
+    prefix.length = prefix_pages * 256
+    block = prefix.snapshot_block(0, prefix.length)
+    caches = []
+    for tail in tails:
+        c = PagedKVCache(pool, prefix.length + tail + 16)
+        c.restore_blocks([block])
+        c.pages.extend(pool.acquire(math.ceil((prefix.length + tail) / 256) - prefix_pages))
+        c.length = prefix.length + tail
+        caches.append(c)
+    for count in extra_counts:
+        c = PagedKVCache(pool, count + 600)
+        c.pages.extend(pool.acquire(1))
+        c.length = 256
+        caches.append(c)
+    batch = PackedBatchCache(caches)
+    batch.prepare_packed([1] * len(tails) + list(extra_counts))
+    return pool, batch, prefix
+
+
+@pytest.mark.parametrize("tails,prefix_pages,extra", [
+    ([10, 300, 700, 5, 256, 1000], 16, ()),                  # decode alone: one grid per unit
+    ([40] * 20, 6, ()),                                      # 20 rows: groups of 16 and 4
+    ([3, 500, 77, 1200, 64], 9, (700,)),                    # beside a prefill row: the persistent grid
+])
+def test_rows_sharing_a_prefix_match_the_oracle(tails, prefix_pages, extra):
+    pool, batch, prefix = _shared_prefix_batch(tails, prefix_pages, extra)
+    dec = batch.decode_items[: 6 * batch.num_decode_items].view(-1, 6)
+    assert (dec[:, 5] > 0).any()  # the prefix is read once per group
+    g = torch.Generator().manual_seed(99)
+    T = batch.total_tokens
+    q = torch.randn(1, 32, T, 128, generator=g).to(torch.bfloat16)
+    k = (torch.randn(1, 8, T, 128, generator=g) / 3).to(torch.bfloat16)
+    v = torch.randn(1, 8, T, 128, generator=g).to(torch.bfloat16)
+    kp_cpu, vp_cpu = pool.keys[0].cpu(), pool.values[0].cpu()
+    out = batch.attend(0, q.to(DEV), k.to(DEV), v.to(DEV))[0].transpose(0, 1).cpu()
+    assert _native.device_status() == 0
+    slots = batch.write_slots.cpu().tolist()
+    write_pool(kp_cpu, slots, k[0].transpose(0, 1))
+    write_pool(vp_cpu, slots, v[0].transpose(0, 1))
+    expected = paged_attention(q[0].transpose(0, 1).contiguous(), kp_cpu, vp_cpu, batch.block_table.cpu().tolist(),
+                               batch.cu_seq_q.cpu().tolist(), batch.seqused_k.cpu().tolist())
+    assert torch.isfinite(out.float()).all()
+    torch.testing.assert_close(out.float(), expected.float(), rtol=2e-2, atol=2e-2)

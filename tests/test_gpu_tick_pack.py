@@ -69,22 +69,25 @@ def test_work_items_cover_every_row_once():
         caches.append(cache_with_pages(pool, length + count + 10, length, [pool._free[-1 - i] for i in range(n)]))
     batch = PackedBatchCache(caches)
     batch.prepare_packed(counts)
-    dec = batch.decode_items[: 4 * batch.num_decode_items].view(-1, 4).tolist()
+    dec = batch.decode_items[: 6 * batch.num_decode_items].view(-1, 6).tolist()
     pre = batch.prefill_items[: 3 * batch.num_prefill_items].view(-1, 3).tolist()
+    rec = batch.row_records.tolist()
     group = 4
     seen = {}
-    for row, split, base, n in dec:
-        assert counts[row] <= 64 // group
-        seen.setdefault(row, []).append((split, base, n))
+    for row, kb, ke, base, n, members in dec:
+        assert counts[row] <= 64 // group and members == 0  # no shared pages in this tick
+        seen.setdefault(row, []).append((kb, ke, base, n))
     record = 0
     for row, count in enumerate(counts):
         end = lengths[row] + count
+        assert rec[row] == record
         if count <= 64 // group:
             items = seen[row]
             n = math.ceil(end / batch.split_keys)
-            assert [s for s, _, _ in items] == list(range(n))
-            assert all(k == n for _, _, k in items)
-            assert [b for _, b, _ in items] == [record + s * count for s in range(n)]
+            sk = batch.split_keys
+            assert [(kb, ke) for kb, ke, _, _ in items] == [(s * sk, min(end, (s + 1) * sk)) for s in range(n)]
+            assert all(k == n for _, _, _, k in items)
+            assert [b for _, _, b, _ in items] == [record + s * count for s in range(n)]
             record += n * count
         else:
             # Query tiles of 128 // group tokens, adjacent tiles (2i, 2i+1) paired (same key tiles).
@@ -92,7 +95,7 @@ def test_work_items_cover_every_row_once():
             m = math.ceil(count / tile)
             pairs = [(a, b) for r, a, b in pre if r == row]
             assert pairs == [(2 * i * tile, (2 * i + 1) * tile if 2 * i + 1 < m else -1) for i in range((m + 1) // 2)]
-    assert record == batch.partial_records
+    assert record == batch.partial_records == rec[len(counts)]
     meta = pack_tick(lengths, counts, [[p.index for p in c.pages] for c in caches], [c.capacity for c in caches])
     assert batch.write_slots.tolist() == meta["write_slots"]
     assert batch.token_row.tolist() == [r for r, c in enumerate(counts) for _ in range(c)]
@@ -116,3 +119,47 @@ def test_second_tick_uploads_only_new_pages_and_restore_resyncs():
     batch2.prepare_packed([5])
     assert batch2.block_table.tolist()[0][:2] == [snap.pages[0].index, c.pages[1].index]
     assert batch2.write_slots.tolist() == [c.pages[1].index * 256 + i for i in range(5)]
+
+
+def test_rows_sharing_restored_pages_form_one_prefix_pass():
+    """Single-token decode rows whose page lists start with the same restored pages: the group's
+    prefix keys get items once for all its rows, each row keeps items for its own keys only,
+    and its records are the prefix splits, then its own."""
+    pool = KVPagePool(attn_config(heads=32, kv_heads=8), 120, device=DEV)
+    prefix = PagedKVCache(pool, 2048)
+    prefix.pages.extend(pool.acquire(6))
+    prefix.length = 6 * 256
+    block = prefix.snapshot_block(0, 6 * 256)
+    tails = [40, 300, 700, 5, 256]
+    caches = []
+    for tail in tails:
+        c = PagedKVCache(pool, 4096)
+        c.restore_blocks([block])
+        c.pages.extend(pool.acquire(math.ceil((6 * 256 + tail) / 256) - 6))
+        c.length = 6 * 256 + tail
+        caches.append(c)
+    other = PagedKVCache(pool, 4096)  # a row with its own pages ends the group
+    other.pages.extend(pool.acquire(8))
+    other.length = 2000
+    batch = PackedBatchCache(caches + [other])
+    batch.prepare_packed([1] * 6)
+    sk = batch.split_keys
+    dec = batch.decode_items[: 6 * batch.num_decode_items].view(-1, 6).tolist()
+    rec = batch.row_records.tolist()
+    shared = 6 * 256
+    groups = [it for it in dec if it[5] > 0]
+    n_prefix = math.ceil(shared / sk)
+    assert groups == [[0, s * sk, min(shared, (s + 1) * sk), s, 0, 5] for s in range(n_prefix)]
+    for row, tail in enumerate(tails):
+        end = shared + tail + 1
+        own = [it for it in dec if it[0] == row and it[5] == 0]
+        n_own = math.ceil((end - shared) / sk)
+        assert [(kb, ke) for _, kb, ke, _, _, _ in own] == [(shared + k * sk, min(end, shared + (k + 1) * sk))
+                                                           for k in range(n_own)]
+        assert [b for _, _, _, b, _, _ in own] == [rec[row] + n_prefix + k for k in range(n_own)]
+        assert all(n == n_prefix + n_own for _, _, _, _, n, _ in own)
+        assert rec[row + 1] - rec[row] == n_prefix + n_own
+    own = [it for it in dec if it[0] == 5]
+    assert all(it[5] == 0 and it[1] % sk == 0 for it in own)  # the unshared row: plain splits from key 0
+    assert rec[6] == batch.partial_records
+    assert _native.device_status() == 0

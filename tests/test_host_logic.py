@@ -120,7 +120,7 @@ def test_descriptor_uploads_only_new_pages():
     b.pages.extend(pool.acquire(1)); b.length = 5
     batch = PackedBatchCache([a, b])
     d = batch._host_descriptor([1, 1], [1, 1])
-    assert d["rows"].tolist() == [[a._slot, 300, 1, 1, 2], [b._slot, 5, 1, 1, 1]]
+    assert d["rows"].tolist() == [[a._slot, 300, 1, 1, 2, 0, 0], [b._slot, 5, 1, 1, 1, 0, 0]]
     assert d["updates"].reshape(-1, 3).tolist() == [[a._slot, 0, a.pages[0].index], [a._slot, 1, a.pages[1].index],
                                                      [b._slot, 0, b.pages[0].index]]
     assert batch._host_descriptor([1, 1], [1, 1])["updates"].size == 0
@@ -148,6 +148,43 @@ def test_descriptor_partitions_attention_work():
     assert d["partial_records"] == math.ceil(1001 / split) * 1 + math.ceil(3016 / split) * 16
     assert d["num_prefill_items"] == 2048 // 32 // 2  # tiles of 32 tokens, paired
     assert d["total_tokens"] == 2065 and d["num_logits"] == 3 and d["width"] == 16
+
+
+def test_rows_restoring_one_prefix_are_grouped():
+    """Consecutive single-token decode rows that restored the same pages form one group: all
+    members get the common full pages as shared prefix keys, the first the group size. Rows
+    with fewer common pages, several tokens, or their own pages stay alone."""
+    cfg = tiny(n_heads=32, n_kv_heads=8)
+    pool = KVPagePool(cfg, 128, device=CPU)
+    prefix = PagedKVCache(pool, 4096)
+    prefix.pages.extend(pool.acquire(8))
+    prefix.length = 8 * 256
+    full, part = prefix.snapshot_block(0, 8 * 256), prefix.snapshot_block(0, 5 * 256)
+
+    def row(block, tail):
+        c = PagedKVCache(pool, 4096)
+        c.restore_blocks([block])
+        extra = math.ceil((block.length + tail) / 256) - len(c.pages)
+        c.pages.extend(pool.acquire(extra))
+        c.length = block.length + tail
+        return c
+
+    alone = PagedKVCache(pool, 4096)
+    alone.pages.extend(pool.acquire(9))
+    alone.length = 2100
+    caches = [row(full, 10), row(full, 300), row(part, 7), alone, row(full, 3), row(full, 40)]
+    counts = [1, 1, 1, 1, 1, 2]
+    d = PackedBatchCache(caches)._host_descriptor(counts, [1] * 6)
+    rows = d["rows"]
+    assert rows[:, 5].tolist() == [5 * 256, 5 * 256, 5 * 256, 0, 0, 0]  # the third row shares 5 pages
+    assert rows[:, 6].tolist() == [3, 0, 0, 0, 0, 0]  # row 4 is alone: row 5 has two tokens
+    split = d["split_keys"]
+    ends = [c.length + n for c, n in zip(caches, counts)]
+    shared = 5 * 256
+    prefix_splits = math.ceil(shared / split)
+    own = [math.ceil((e - shared) / split) for e in ends[:3]] + [math.ceil(e / split) for e in ends[3:]]
+    assert d["num_decode_items"] == prefix_splits + sum(own)
+    assert d["partial_records"] == 3 * prefix_splits + sum(o * n for o, n in zip(own, counts))
 
 
 def test_split_policy():
