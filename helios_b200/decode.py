@@ -44,7 +44,8 @@ class Decoder:
             raise ValueError("Paged decode caches must share one pool.")
         if len({id(cache) for cache in caches}) != len(caches):
             raise ValueError("Paged batches require distinct request caches.")
-        self.model.eval()
+        if self.model.training:  # a recursive eval() walks ~500 modules: about 1 ms per tick
+            self.model.eval()
         with torch.inference_mode():
             batch = self._paged_decode_batch
             if batch is None or batch.pool is not caches[0].pool:
@@ -93,7 +94,11 @@ def sample_rows(logits: torch.Tensor, samplings: Sequence[Sampling], *, uniforms
         raise ValueError("Each logit row needs its sampling settings.")
     device = logits.device
     settings = torch.tensor([[s.temperature, s.top_p] for s in samplings], dtype=torch.float32)
-    settings = settings.to(device)
+    if device.type == "cuda":
+        # From pinned memory the upload queues behind the tick instead of waiting for it.
+        settings = settings.pin_memory().to(device, non_blocking=True)
+    else:
+        settings = settings.to(device)
     if uniforms is None:
         uniforms = torch.rand(rows, dtype=torch.float32, device=device, generator=generator)
     elif uniforms.dtype != torch.float32 or uniforms.device != device:
@@ -136,9 +141,18 @@ def sample_and_verify(logits: torch.Tensor, chunks: Sequence[Sequence[int]], log
         per_row.extend([_GREEDY] * (lc - 1))
     device = logits.device
     predictions = sample_rows(logits, per_row, uniforms=uniforms)
-    tokens = torch.tensor([t for chunk in chunks for t in chunk], dtype=torch.long).to(device)
-    cu = torch.tensor(list(accumulate((len(c) for c in chunks), initial=0)), dtype=torch.int32).to(device)
-    offsets = torch.tensor(starts, dtype=torch.int32).to(device)
+    # One pinned upload of the draft tokens, chunk bounds and logit offsets (int64), queued
+    # behind the tick.
+    cu_host = list(accumulate((len(c) for c in chunks), initial=0))
+    packed = torch.tensor([t for chunk in chunks for t in chunk] + cu_host + starts, dtype=torch.long)
+    if device.type == "cuda":
+        packed = packed.pin_memory().to(device, non_blocking=True)
+    else:
+        packed = packed.to(device)
+    n_tok = cu_host[-1]
+    tokens = packed[:n_tok]
+    cu = packed[n_tok:n_tok + rows + 1].int()
+    offsets = packed[n_tok + rows + 1:].int()
     accepted, emitted = ops.verify_drafts(tokens, cu, offsets, predictions)
     host = torch.cat([accepted.long(), emitted]).cpu().tolist()  # the tick's one device->host transfer
     counts, flat = host[:rows], host[rows:]

@@ -320,7 +320,8 @@ class PagedBatchCache:
             raise RuntimeError(
                 f"KV page pool needs {total_missing} pages but only {self.pool.free_pages} are free.")
         for cache, missing in zip(self.caches, missing_pages, strict=True):
-            cache.pages.extend(self.pool.acquire(missing))
+            if missing:
+                cache.pages.extend(self.pool.acquire(missing))
             cache._pending_tokens = tokens
         self._pack([tokens] * self.batch_size, [1] * self.batch_size)
         self.max_q = tokens
@@ -362,16 +363,17 @@ class PagedBatchCache:
         the last tick, and the attention work partition. O(rows + new pages)."""
         pool, config = self.pool, self.pool.config
         page_size = pool.page_size
-        rows = np.zeros((self.batch_size, ops.TICK_ROW_FIELDS), dtype=np.int32)
         updates: list[int] = []
-        for r, (cache, count, lc) in enumerate(zip(self.caches, counts, logit_counts)):
+        fields: list[tuple] = []
+        for cache, count, lc in zip(self.caches, counts, logit_counts):
             n = len(cache.pages)
             if cache._synced < n:
                 slot = cache._slot
                 for j in range(cache._synced, n):
                     updates += (slot, j, cache.pages[j].index)
                 cache._synced = n
-            rows[r, :5] = (cache._slot, cache.length, count, lc, n)
+            fields.append((cache._slot, cache.length, count, lc, n, 0, 0))
+        rows = np.array(fields, dtype=np.int32).reshape(self.batch_size, ops.TICK_ROW_FIELDS)
         group = config.n_heads // config.n_kv_heads
         decode_max = DECODE_QUERY_ROWS // group
         tile_tokens = PREFILL_TILE_ROWS // group
@@ -394,7 +396,7 @@ class PagedBatchCache:
             "partial_records": int(records[is_decode].sum()),
             "num_prefill_items": int(((((cnts[~is_decode] + tile_tokens - 1) // tile_tokens) + 1) // 2).sum()),
             "total_tokens": int(cnts.sum()), "num_logits": int(rows[:, 3].sum()),
-            "width": max(_pages_for(cache.capacity, page_size) for cache in self.caches),
+            "width": _pages_for(max(cache.capacity for cache in self.caches), page_size),
         }
 
     def _share_prefixes(self, rows: np.ndarray, decode_max: int) -> None:
@@ -405,24 +407,31 @@ class PagedBatchCache:
         those pages once for the whole group."""
         page_size = self.pool.page_size
         caches = self.caches
-
-        def full_pages(r: int) -> int:  # committed pages a row may share
-            return int(rows[r, 1]) // page_size if rows[r, 2] == 1 else 0
+        # Committed pages a row may share: single-token rows only.
+        full = np.where(rows[:, 2] == 1, rows[:, 1] // page_size, 0).tolist()
+        if max(full, default=0) < MIN_SHARED_PAGES:
+            return
 
         r, count = 0, len(caches)
         while r < count:
-            lead = full_pages(r)
+            lead = full[r]
             if lead < MIN_SHARED_PAGES:
                 r += 1
                 continue
             head = caches[r].pages
             common, j = lead, r + 1
             while j < count and j - r < decode_max:
-                limit = min(common, full_pages(j))
+                limit = min(common, full[j])
                 pages = caches[j].pages
-                lcp = 0
-                while lcp < limit and pages[lcp].index == head[lcp].index:
-                    lcp += 1
+                # Restored pages are the same handle objects, so the slice comparison (element
+                # identity first, in C) settles the common case; the index walk finds a shorter
+                # common prefix.
+                if limit >= MIN_SHARED_PAGES and pages[:limit] == head[:limit]:
+                    lcp = limit
+                else:
+                    lcp = 0
+                    while lcp < limit and pages[lcp].index == head[lcp].index:
+                        lcp += 1
                 if lcp < MIN_SHARED_PAGES:
                     break
                 common = lcp
