@@ -417,14 +417,17 @@ __global__ void __launch_bounds__(kDecSubThreads, 2) decode_attention_kernel(Att
 
   pdl_wait();     // q, K and V from the norm/RoPE/append kernel ahead of this one
   pdl_trigger();  // the prefill kernel (or the split combine) may launch behind this grid
-  if (p.counts != nullptr && static_cast<int>(blockIdx.x) >= p.counts[0]) return;  // past this tick's items
+  // KV heads fastest: the CTAs of one item's heads run together and read the same pool rows
+  // (each its own 256 bytes of every 2 KB token row).
+  const int item = static_cast<int>(blockIdx.x) / p.kv_heads, head = static_cast<int>(blockIdx.x) % p.kv_heads;
+  if (p.counts != nullptr && item >= p.counts[0]) return;  // past this tick's items
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int4 ia;
   int2 ib;
   int q0, count, end;
-  decode_item(p, blockIdx.x, ia, ib, q0, count, end);
+  decode_item(p, item, ia, ib, q0, count, end);
   const int row = ia.x;
-  const DecodeUnit u = decode_unit<GROUP>(p, blockIdx.y, ia, ib, q0, count, end, warp);
+  const DecodeUnit u = decode_unit<GROUP>(p, head, ia, ib, q0, count, end, warp);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kDecStages; ++s) {

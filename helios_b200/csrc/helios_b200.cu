@@ -359,6 +359,8 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
     return rc;
   const int gs = group_slot(group);
   if (num_decode_items > 0 && decode_items == nullptr) return fail(HB_ERR_INVALID, "null decode items");
+  if (static_cast<int64_t>(num_decode_items) * kv_heads > INT32_MAX)
+    return fail(HB_ERR_UNSUPPORTED, "decode items x KV heads exceed 2^31");
   if (num_prefill_items > 0 && prefill_items == nullptr) return fail(HB_ERR_INVALID, "null prefill items");
 
   // Launch order decode -> prefill -> split combine on the caller's stream, each behind the
@@ -391,7 +393,7 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
                      hb::kDecPersistentSmemBytes, stream, p, kmap, vmap);                                       \
     } else {                                                                                                    \
       if (int rc = ensure_smem(hb::decode_attention_kernel<G>, hb::kDecSmemBytes, g_dec_smem[gs])) return rc;   \
-      e = launch_pdl(hb::decode_attention_kernel<G>, dim3(num_decode_items, kv_heads), dim3(hb::kDecSubThreads), \
+      e = launch_pdl(hb::decode_attention_kernel<G>, dim3(num_decode_items * kv_heads), dim3(hb::kDecSubThreads), \
                      hb::kDecSmemBytes, stream, p, kmap, vmap);                                                 \
     }                                                                                                           \
     if (e != cudaSuccess) return fail(HB_ERR_CUDA, "decode attention: %s", cudaGetErrorString(e));              \
