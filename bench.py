@@ -5,8 +5,8 @@
 Workload (BASELINE config 3): Qwen3-4B architecture, random-init bf16 weights;
 one tick = 32 decode rows (contexts uniform in [1024, 4096], their K/V already
 in the paged pool) + one 2048-token prefill chunk at offset 0 = 2080 tokens.
-A step is one tick: tick packing, 36 layers, logits for the 33 trailing rows and
-greedy sampling. Each tick starts a fresh prefill request (its pages are
+A step is one tick: tick packing, 36 layers and the greedy ids of the 33 trailing
+rows (lm_head GEMM with the argmax in its epilogue). Each tick starts a fresh prefill request (its pages are
 recycled afterwards) and advances every decode row by one token. The host half
 of each tick (page acquisition, descriptor upload, tick packing) runs every
 step; the device half replays from a CUDA graph captured during warm-up
@@ -14,8 +14,8 @@ step; the device half replays from a CUDA graph captured during warm-up
 
   value   tokens/s with the step's token ids already on the device, timed with
           CUDA events over K steps (max over ranks), summed over replicas.
-  e2e     the same ticks through the public API (``Decoder.packed_caches`` with
-          host token lists, fused sampler, device->host read of the sampled ids).
+  e2e     the same ticks through the public API (``Decoder.packed_caches_greedy`` with
+          host token lists, device->host read of the sampled ids).
   roofline  the split-K decode attention kernel at BASELINE config 2 (64 rows,
           contexts U[512, 8192], 32/8 heads, d=128, 4096-page pool), HBM-bound:
           algorithmic bytes / CUDA-event time against the measured copy peak.
@@ -186,12 +186,10 @@ class TickRunner:
     """Runs ticks either through the public API (host lists) or with device-resident ids."""
 
     def __init__(self, device, model, decoder, pool, caches, pending, chunk):
-        from helios_b200.config import Sampling
         from helios_b200.paged_cache import PackedBatchCache
 
         self.device, self.model, self.decoder, self.pool = device, model, decoder, pool
         self.caches, self.pending, self.chunk = caches, pending, chunk
-        self.samplings = [Sampling(temperature=0, top_p=1, max_new_tokens=1)] * (DECODE_ROWS + 1)
         self.batch = PackedBatchCache(caches)
         self.chunk_dev = torch.tensor(chunk, dtype=torch.long, device=device)
         self.pending_dev = torch.tensor(pending, dtype=torch.long, device=device)
@@ -206,16 +204,13 @@ class TickRunner:
 
     def device_step(self):
         """Token ids stay on the device; metadata still goes through tick packing."""
-        from helios_b200.decode import sample_rows
-
         prefill = self._fresh_prefill()
         batch = self.batch
         batch.caches, batch.batch_size = tuple(self.caches) + (prefill,), DECODE_ROWS + 1
         with torch.inference_mode():
             ids = torch.cat([self.pending_dev, self.chunk_dev]).unsqueeze(0)
             batch.prepare_packed([1] * DECODE_ROWS + [PREFILL])
-            logits = self.model(ids, cache=batch)
-            sampled = sample_rows(logits, self.samplings)
+            sampled = self.model.greedy_ids(ids, batch)
             self.pending_dev = sampled[:DECODE_ROWS]
         self.launches = self._count_launches(batch)
         batch.caches = ()
@@ -223,17 +218,14 @@ class TickRunner:
 
     def api_step(self):
         """Public API with host buffers: token lists in, sampled ids back on the host."""
-        from helios_b200.decode import sample_rows
-
         prefill = self._fresh_prefill()
         chunks = [[t] for t in self.pending] + [self.chunk]
         with torch.inference_mode():
-            logits = self.decoder.packed_caches(self.caches + [prefill], chunks)
-            ids = sample_rows(logits, self.samplings).cpu().tolist()
+            ids = self.decoder.packed_caches_greedy(self.caches + [prefill], chunks).cpu().tolist()
         self.pending = ids[:DECODE_ROWS]
         batch = self.decoder._packed_batch
-        # token ids + tick descriptor (rows and new arena entries) + per-row sampling settings
-        self.h2d_bytes = 8 * TOKENS_PER_STEP + batch.uploaded_bytes + 4 * 2 * (DECODE_ROWS + 1)
+        # token ids + tick descriptor (rows and new arena entries)
+        self.h2d_bytes = 8 * TOKENS_PER_STEP + batch.uploaded_bytes
         self.d2h_bytes = 8 * (DECODE_ROWS + 1)
         self.launches = self._count_launches(batch)
         prefill.close()
@@ -242,7 +234,8 @@ class TickRunner:
         attention = (batch.num_decode_items > 0) + (batch.num_decode_items > 0 and batch.partial_records > 0) \
             + (batch.num_prefill_items > 0)
         per_layer = 1 + attention + 2 + 1  # norm/rope/append, attention, add_rmsnorm x2, swiglu
-        return 3 + per_layer * self.model.config.n_layers + 1  # tick pack, embed, first norm, ..., sampler
+        # tick pack, embed, first norm, the layers, the lm_head GEMM with the argmax and its finalize
+        return 3 + per_layer * self.model.config.n_layers + 2
 
 
 def time_steps(step, steps: int, device: torch.device) -> float:

@@ -54,6 +54,7 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "hb_swiglu": (c_int, [P, P, I64, I64, P]),
     "hb_gemm_swiglu": (c_int, [P, I32, I32, P, I32, P, P]),
     "hb_attention_set_overlap": (c_int, [I32]),
+    "hb_lm_head_argmax": (c_int, [P, I32, I32, P, I32, P, P, P]),
     "hb_rope_gather": (c_int, [P, P, I64, I32, P, I32, I32, P, P, P]),
     "hb_gemm_qkv_norm_rope_append": (c_int, [P, I32, I32, P, I32, I32, I32, P, P, F32, P, P, I32, I64, P, P, P, P,
                                              P, I64, P]),

@@ -18,6 +18,7 @@
 #include "gemm_qkv.cuh"
 #include "gemm_swiglu.cuh"
 #include "hb_common.cuh"
+#include "lm_head_argmax.cuh"
 #include "model_ops.cuh"
 #include "norm_rope_append.cuh"
 #include "sampler.cuh"
@@ -119,7 +120,7 @@ int ensure_smem(K kernel, int bytes, bool (&done)[64]) {
   return HB_OK;
 }
 
-bool g_dec_smem[4][64], g_decp_smem[4][64], g_pre_smem[4][64], g_tick_smem[64], g_gemm_smem[64], g_qkv_smem[64];
+bool g_dec_smem[4][64], g_decp_smem[4][64], g_pre_smem[4][64], g_tick_smem[64], g_gemm_smem[64], g_qkv_smem[64], g_argmax_smem[64];
 
 constexpr int kDefaultOverlapDecodeSms = 100;
 
@@ -592,6 +593,27 @@ int hb_gemm_swiglu(const void* x, int32_t m, int32_t k, const void* w_gate_up, i
   hb::GemmSwigluParams p{m, k, (m + hb::kGemmTileM - 1) / hb::kGemmTileM, inter / hb::kGemmTileN,
                          static_cast<__nv_bfloat16*>(out), inter};
   return launch_fused_gemm<hb::SwigluEpilogue>(p, amap, bmap, g_gemm_smem, stream, "fused_gemm_kernel<swiglu>");
+}
+
+int hb_lm_head_argmax(const void* x, int32_t m, int32_t k, const void* weight, int32_t vocab,
+                      unsigned long long* best, int64_t* out_ids, cudaStream_t stream) {
+  if (m < 0 || k < 1 || vocab < 1) return fail(HB_ERR_INVALID, "bad lm_head sizes");
+  if (k % hb::kGemmTileK != 0)
+    return fail(HB_ERR_UNSUPPORTED, "lm_head argmax needs K %% %d == 0 (got %d)", hb::kGemmTileK, k);
+  if (m == 0) return HB_OK;
+  if (x == nullptr || weight == nullptr || best == nullptr || out_ids == nullptr || !aligned(x, 16) ||
+      !aligned(weight, 16) || !aligned(best, 8) || !aligned(out_ids, 8))
+    return fail(HB_ERR_INVALID, "lm_head argmax pointers must be non-null, x and weight 16-byte aligned");
+  CUtensorMap amap, bmap;
+  const uint64_t row_bytes = static_cast<uint64_t>(k) * 2;
+  if (int rc = encode_2d(&amap, x, k, m, row_bytes, hb::kGemmTileK, hb::kGemmTileM)) return rc;
+  if (int rc = encode_2d(&bmap, weight, k, vocab, row_bytes, hb::kGemmTileK, hb::kGemmTileN)) return rc;
+  hb::GemmArgmaxParams p{m, k, (m + hb::kGemmTileM - 1) / hb::kGemmTileM,
+                         (vocab + 2 * hb::kGemmTileN - 1) / (2 * hb::kGemmTileN), vocab, best};
+  if (int rc = launch_fused_gemm<hb::ArgmaxEpilogue>(p, amap, bmap, g_argmax_smem, stream, "fused_gemm_kernel<argmax>"))
+    return rc;
+  hb::argmax_finalize_kernel<<<(m + 127) / 128, 128, 0, stream>>>(best, m, out_ids);
+  return check_launch("argmax_finalize_kernel");
 }
 
 int hb_rope_gather(const float* cos, const float* sin, int64_t rope_rows, int32_t head_dim, const int64_t* positions,

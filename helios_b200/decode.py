@@ -38,6 +38,16 @@ class Decoder:
         return next(self.model.parameters()).device
 
     def decode_caches(self, caches: list[PagedKVCache], token_ids: list[int]) -> torch.Tensor:
+        """Logits ``[B, V]`` of one decode step of every cache (decode.py:220-258)."""
+        return self._decode(caches, token_ids, greedy=False)
+
+    def decode_caches_greedy(self, caches: list[PagedKVCache], token_ids: list[int]) -> torch.Tensor:
+        """The temperature-0 next token of every cache (int64 ``[B]``): ``decode_caches`` followed
+        by the argmax the reference samples greedy rows with (decode.py:458-460), with the argmax
+        in the lm_head GEMM's epilogue so the logits are never written."""
+        return self._decode(caches, token_ids, greedy=True)
+
+    def _decode(self, caches: list[PagedKVCache], token_ids: list[int], *, greedy: bool) -> torch.Tensor:
         if not caches or len(caches) != len(token_ids):
             raise ValueError("Every request cache needs exactly one pending token.")
         if any(not isinstance(cache, PagedKVCache) or cache.pool is not caches[0].pool for cache in caches):
@@ -56,12 +66,25 @@ class Decoder:
                 tokens = batch.metadata("token_ids", list(token_ids), torch.long).unsqueeze(1)
                 batch.prepare(1)
                 slots = tuple(range(len(caches)))
+                if greedy:
+                    return self.model.greedy_ids(tokens, batch, cache_slots=slots)
                 return self.model(tokens, cache=batch, cache_slots=slots)[:, -1, :]
             finally:
                 batch.caches = ()
 
     def packed_caches(self, caches: list[PagedKVCache], chunks: list[list[int]], *,
                       logit_counts: list[int] | None = None) -> torch.Tensor:
+        """Logits ``[sum(logit_counts), V]`` of one packed mixed tick (decode.py:260-291)."""
+        return self._packed(caches, chunks, logit_counts, greedy=False)
+
+    def packed_caches_greedy(self, caches: list[PagedKVCache], chunks: list[list[int]], *,
+                             logit_counts: list[int] | None = None) -> torch.Tensor:
+        """Temperature-0 token ids (int64 ``[sum(logit_counts)]``) of the logit rows
+        ``packed_caches`` returns, with the argmax in the lm_head GEMM's epilogue."""
+        return self._packed(caches, chunks, logit_counts, greedy=True)
+
+    def _packed(self, caches: list[PagedKVCache], chunks: list[list[int]], logit_counts: list[int] | None, *,
+                greedy: bool) -> torch.Tensor:
         if not caches or len(caches) != len(chunks) or any(not chunk for chunk in chunks):
             raise ValueError("Each packed cache needs a nonempty token chunk.")
         if len({id(cache) for cache in caches}) != len(caches) or any(
@@ -75,6 +98,8 @@ class Decoder:
             try:
                 tokens = batch.metadata("token_ids", [t for chunk in chunks for t in chunk], torch.long).unsqueeze(0)
                 batch.prepare_packed([len(chunk) for chunk in chunks], logit_counts)
+                if greedy:
+                    return self.model.greedy_ids(tokens, batch)
                 return self.model(tokens, cache=batch)
             finally:
                 batch.caches = ()

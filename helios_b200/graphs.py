@@ -45,20 +45,20 @@ class TickGraphs:
                 int(cache.block_table.shape[1]), cache.work_capacity, cache._i32.data_ptr(), cache._i64.data_ptr(),
                 0 if ws is None else ws.data_ptr(), int(cache.logit_rows.data_ptr()))
 
-    def run(self, ids: torch.Tensor, cache) -> torch.Tensor:
-        """Logits ``[logit rows, V]`` of a prepared tick. The returned tensor is the
-        graph's own output buffer: it holds this tick's logits until the next replay of
-        the same graph."""
+    def run(self, ids: torch.Tensor, cache, *, greedy: bool = False) -> torch.Tensor:
+        """Logits ``[logit rows, V]`` of a prepared tick (``greedy``: their argmax ids). The
+        returned tensor is the graph's own output buffer: it holds this tick's result until
+        the next replay of the same graph."""
         flat = ids.reshape(-1)
         if not cache.capacity_mode:
             # From the next prepare on, this cache lays out its buffers by capacity; this
             # tick (prepared without capacities) runs eagerly.
             cache.capacity_mode = True
-            return self.model._packed_logits(flat, cache)
-        key = self._key(cache)
+            return self.model._packed_logits(flat, cache, greedy=greedy)
+        key = self._key(cache) + (greedy,)
         entry = self._graphs.get(key)
         if entry is None:
-            entry = self._capture(flat, cache)
+            entry = self._capture(flat, cache, greedy)
             self._graphs[key] = entry
             while len(self._graphs) > self.max_graphs:
                 self._graphs.popitem(last=False)
@@ -70,7 +70,7 @@ class TickGraphs:
         self.replays += 1
         return logits
 
-    def _capture(self, flat: torch.Tensor, cache) -> tuple:
+    def _capture(self, flat: torch.Tensor, cache, greedy: bool) -> tuple:
         device = flat.device
         static_ids = flat.clone()
         side = torch.cuda.Stream(device)
@@ -79,12 +79,12 @@ class TickGraphs:
             # One eager pass first: library handles, kernel attributes and the caching
             # allocator's blocks are set up outside the capture. It writes the same K/V
             # rows the replay will write, so it changes nothing.
-            self.model._packed_logits(static_ids, cache)
+            self.model._packed_logits(static_ids, cache, greedy=greedy)
         torch.cuda.current_stream(device).wait_stream(side)
         graph = torch.cuda.CUDAGraph()
         if self._pool is None:
             self._pool = torch.cuda.graph_pool_handle()
         with torch.cuda.graph(graph, pool=self._pool):
-            logits = self.model._packed_logits(static_ids, cache)
+            logits = self.model._packed_logits(static_ids, cache, greedy=greedy)
         self.captures += 1
         return graph, static_ids, logits

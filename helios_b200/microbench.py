@@ -2,6 +2,7 @@
 
     python -m helios_b200.microbench [norm_rope] [swiglu] [add_rmsnorm] [prefill] [decode] [mixed[:N]] [prefix_decode] [sample]
                                      [gate_up_fused] [gate_up_cublas] [qkv_fused] [qkv_fused_full_tables] [qkv_cublas]
+                                     [lm_head_argmax33|128] [lm_head_cublas33|128]
 
 Each case captures 24 calls of one entry point into a CUDA graph, cycling over input sets
 whose total exceeds the 126 MB L2 where the kernel is memory-bound, and prints the median
@@ -223,6 +224,26 @@ def _sample(dev, g):
     return [make() for _ in range(4)], rows * vocab * 2
 
 
+def _lm_head(dev, g, rows: int, fused: bool):
+    """The Qwen3-4B greedy head over `rows` logit rows: the tied [151936, 2560] lm_head and the
+    argmax, either fused (hb_lm_head_argmax, no logits written) or cuBLAS + the sampler kernel at
+    temperature 0. Bytes: one read of the weight."""
+    vocab = 151936
+    weight = (torch.randn(vocab, HIDDEN, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+
+    def make():
+        x = torch.randn(rows, HIDDEN, device=dev, generator=g).to(torch.bfloat16)
+        if fused:
+            out = torch.empty(rows, dtype=torch.long, device=dev)
+            return lambda: ops.lm_head_argmax(x, weight, out)
+        zeros = torch.zeros(rows, device=dev)
+        ones = torch.ones(rows, device=dev)
+        out = torch.empty(rows, dtype=torch.long, device=dev)
+        return lambda: ops.sample(torch.nn.functional.linear(x, weight), zeros, ones, zeros, out)
+
+    return [make() for _ in range(2)], vocab * HIDDEN * 2
+
+
 def main(argv: list[str]) -> None:
     if not torch.cuda.is_available():
         raise SystemExit("the microbenchmarks need a CUDA device")
@@ -244,6 +265,10 @@ def main(argv: list[str]) -> None:
         "qkv_fused": lambda: _qkv(dev, g, True),
         "qkv_fused_full_tables": lambda: _qkv(dev, g, True, half_tables=False),
         "qkv_cublas": lambda: _qkv(dev, g, False),
+        "lm_head_argmax33": lambda: _lm_head(dev, g, 33, True),
+        "lm_head_cublas33": lambda: _lm_head(dev, g, 33, False),
+        "lm_head_argmax128": lambda: _lm_head(dev, g, 128, True),
+        "lm_head_cublas128": lambda: _lm_head(dev, g, 128, False),
     }
     for arg in argv or list(cases):
         # "mixed:48" times a case with the decode grid keeping 48 SMs beside the prefill grid

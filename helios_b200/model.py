@@ -194,8 +194,24 @@ class Qwen3Model(nn.Module):
         uniform paged batches return the last position of each row, ``[B, 1, V]``.
         Positions always come from the paged cache (``position_ids`` is accepted for
         signature compatibility; the reference derives the same values)."""
+        out = self._run(input_ids, cache, cache_slots, greedy=False)
+        return out if isinstance(cache, PackedBatchCache) else out.view(cache.batch_size, 1, -1)
+
+    def greedy_ids(self, input_ids: torch.Tensor, cache: PagedBatchCache,
+                   cache_slots: Sequence[int] | torch.Tensor | None = None) -> torch.Tensor:
+        """Temperature-0 token ids of the rows ``forward`` returns logits for (int64: ``[logit rows]``
+        for packed caches, ``[B]`` for uniform paged batches): the argmax of those bf16 logits with
+        ties to the lowest id (decode.py:458-460), from the lm_head GEMM with the argmax in its
+        epilogue, so the logits are never written (hb_lm_head_argmax)."""
+        return self._run(input_ids, cache, cache_slots, greedy=True)
+
+    def _run(self, input_ids: torch.Tensor, cache, cache_slots, *, greedy: bool) -> torch.Tensor:
         if isinstance(cache, PackedBatchCache):
-            return self._forward_packed(input_ids, cache)
+            if input_ids.shape != (1, sum(cache.counts)):
+                raise ValueError("Packed input does not match query lengths.")
+            out = self._device_half(input_ids, cache, greedy)
+            cache.advance_packed()
+            return out
         if not isinstance(cache, PagedBatchCache):
             raise TypeError("The B200 model runs over paged KV caches (PagedBatchCache / PackedBatchCache).")
         if cache_slots is not None:
@@ -206,28 +222,22 @@ class Qwen3Model(nn.Module):
         if max(c.length + tokens for c in cache.caches) > self.config.context_length:
             raise ValueError(f"Qwen3-4B supports at most {self.config.context_length:,} tokens per request.")
         # prepare(tokens) packed one logit row per sequence: its last position.
-        if self._graphs is not None and input_ids.is_cuda:
-            logits = self._graphs.run(input_ids, cache)
-        else:
-            logits = self._packed_logits(input_ids.reshape(-1), cache)
+        out = self._device_half(input_ids, cache, greedy)
         cache.advance(tokens, slots=cache_slots)
-        return logits.view(cache.batch_size, 1, -1)
+        return out
 
-    def _forward_packed(self, input_ids: torch.Tensor, cache: PackedBatchCache) -> torch.Tensor:
-        if input_ids.shape != (1, sum(cache.counts)):
-            raise ValueError("Packed input does not match query lengths.")
+    def _device_half(self, input_ids: torch.Tensor, cache: PagedBatchCache, greedy: bool) -> torch.Tensor:
         if self._graphs is not None and input_ids.is_cuda:
-            logits = self._graphs.run(input_ids, cache)
-        else:
-            logits = self._packed_logits(input_ids.reshape(-1), cache)
-        cache.advance_packed()
-        return logits
+            return self._graphs.run(input_ids, cache, greedy=greedy)
+        return self._packed_logits(input_ids.reshape(-1), cache, greedy=greedy)
 
-    def _packed_logits(self, ids: torch.Tensor, cache: PagedBatchCache) -> torch.Tensor:
-        """Device half of a prepared tick: logits of the cache's logit rows. It makes no host
-        synchronisation, so it can be captured into a CUDA graph."""
+    def _packed_logits(self, ids: torch.Tensor, cache: PagedBatchCache, *, greedy: bool = False) -> torch.Tensor:
+        """Device half of a prepared tick: logits of the cache's logit rows (or, ``greedy``, their
+        argmax ids). It makes no host synchronisation, so it can be captured into a CUDA graph."""
         _, normed = self._layers(ids, cache)
         rows = normed.index_select(0, cache.logit_rows)
+        if greedy:
+            return ops.lm_head_argmax(rows, self.output.weight)
         return F.linear(rows, self.output.weight)
 
     def _layers(self, ids: torch.Tensor, cache: PagedBatchCache) -> tuple[torch.Tensor, torch.Tensor]:

@@ -167,6 +167,34 @@ def gemm_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | No
     return out
 
 
+_ARGMAX_KEYS: dict[torch.device, torch.Tensor] = {}
+
+
+def lm_head_argmax(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Greedy token ids ``argmax_j bf16(x[r] . weight[j])`` (int64 ``[m]``; ties to the lowest id)
+    for the final-normed logit rows ``x [m, k]`` against the tied ``weight [vocab, k]``, with the
+    argmax in the tcgen05 GEMM's epilogue: the logits are never written (hb_lm_head_argmax)."""
+    _need(x, BF16, "x")
+    _need(weight, BF16, "weight")
+    m, k = x.shape
+    if weight.shape[1] != k:
+        raise ValueError("weight must be [vocab, hidden] matching x")
+    dev = x.device
+    keys = _ARGMAX_KEYS.get(dev)
+    if keys is None or keys.numel() < m:
+        if torch.cuda.is_current_stream_capturing():
+            # Memory allocated under capture belongs to the graph's pool; the keys outlive graphs.
+            raise RuntimeError("lm_head_argmax: run one call of this size before capturing it")
+        # Zeroed once; every call leaves the keys it used at zero.
+        keys = _ARGMAX_KEYS[dev] = torch.zeros(max(m, 256), dtype=torch.int64, device=dev)
+    if out is None:
+        out = torch.empty(m, dtype=torch.long, device=dev)
+    rc = lib().hb_lm_head_argmax(x.data_ptr(), m, k, weight.data_ptr(), weight.shape[0], keys.data_ptr(),
+                                 out.data_ptr(), _stream(dev))
+    _native.check(rc, "hb_lm_head_argmax")
+    return out
+
+
 def rope_gather(cos: torch.Tensor, sin: torch.Tensor, positions: torch.Tensor, *,
                 half_tables: bool) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-token rope rows for :func:`gemm_qkv_norm_rope_append`: ``[w / 4, T, 4]`` fp32 tables

@@ -202,6 +202,21 @@ HB_API int hb_gemm_swiglu(const void* x, int32_t m, int32_t k, const void* w_gat
                           cudaStream_t stream);
 
 /*
+ * Greedy decoding head (replaces the logits GEMM of Qwen3Model._forward_packed,
+ * src/helios/runtime/qwen3/model.py:108-110, and the temperature-0 argmax of
+ * Decoder._sample, src/helios/runtime/qwen3/decode.py:458-460, as Engine._execute_batch
+ * applies it, src/helios/runtime/engine.py:472-473).
+ * out_ids[r] = argmax_j bf16(x[r] . weight[j]) for the m rows of x [m, k] (bf16, the final-normed
+ * logit rows) against the tied embedding weight [vocab, k] (bf16): ties go to the lowest id and a
+ * NaN logit counts as the largest, as torch.argmax over the bf16 logits does. The logits are
+ * never written. best [m] (8-byte aligned) must be zero before the first call; every call leaves
+ * it zero. k % 64 == 0. Persistent tcgen05 GEMM with the argmax in its epilogue, then one small
+ * kernel, both on `stream`. A row with id -1 means the GEMM gave up (hb_device_status).
+ */
+HB_API int hb_lm_head_argmax(const void* x, int32_t m, int32_t k, const void* weight, int32_t vocab,
+                             unsigned long long* best, int64_t* out_ids, cudaStream_t stream);
+
+/*
  * Per-token rope rows for hb_gemm_qkv_norm_rope_append: out[g][t][0..3] = table[positions[t]][4g ..
  * 4g + 3] (fp32, zeros where the position is outside [0, rope_rows)) for g < width / 4, for the
  * cos and sin tables [rope_rows][head_dim] of apply_rope (src/helios/runtime/qwen3/layers.py:
@@ -250,7 +265,7 @@ HB_API int hb_page_copy(void* pool_base, int64_t tensor_stride_bytes, int32_t te
 
 /*
  * (d) Fused sampler. Replaces Decoder._sample (src/helios/runtime/qwen3/decode.py:457-473)
- * and the batched sampling in Engine._execute_batch (src/helios/runtime/engine.py:470-492):
+ * and the batched sampling in Engine._execute_batch (src/helios/runtime/engine.py:470-492).
  * temperature 0 -> argmax (first index); otherwise temperature softmax with the
  * reference's top-p keep rule, drawn by inverse CDF over kept tokens in index order
  * with the caller's uniforms[rows] in [0, 1). logits bf16 [rows][row_stride].
