@@ -162,8 +162,10 @@ HB_API int hb_attention_set_overlap(int32_t decode_sms);
  * exceed the array is rejected with HB_ERR_INVALID. The first call on a device looks
  * up the array's device address (cudaGetSymbolAddress) with that device current; make
  * that first call before any stream capture. Every call shares the one array and leaves
- * its contents behind (nothing in it needs to start at zero): calls that overlap on the
- * GPU, from different streams or threads, race on it.
+ * its contents behind. Of those, only the decode work ticket in the first 256 bytes must
+ * start at zero: the array is zero when the library loads and every call resets the ticket
+ * (the split-K partials are written before they are read). Calls that overlap on the GPU,
+ * from different streams or threads, race on the array.
  */
 #define HB_STATIC_WORKSPACE_BYTES (8u << 20)
 HB_API int hb_paged_attention_static_workspace(const void* q, const void* key_pool, const void* value_pool,
