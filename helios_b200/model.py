@@ -59,7 +59,11 @@ def rope_parameters(config: Qwen3Config) -> tuple[torch.Tensor, torch.Tensor]:
     return torch.cos(angles), torch.sin(angles)
 
 
-FUSED_GATE_UP_MIN_ROWS = 256  # token rows from which the fused tcgen05 gate|up + SwiGLU kernel is used
+# Token rows from which the fused tcgen05 gate|up + SwiGLU kernel is used. Measured at the
+# Qwen3-4B shape (gate|up weights cycled beyond L2): it matches cuBLAS + the SwiGLU kernel at
+# 128 and 1280 rows, trails it between (39 vs 30 us at 256, 87 vs 82 us at 1024) and leads
+# from 1536 rows (120 vs 126 us; 156 vs 182 us at the 2080-row tick).
+FUSED_GATE_UP_MIN_ROWS = 1280
 # Token rows from which the fused tcgen05 q|k|v + norm/RoPE/append kernel would be used. None:
 # not used. At the Qwen3-4B tick shape (2080 rows) it measured 58-62 us against 56 us for cuBLAS
 # plus the norm/RoPE/append kernel: its one-SM main loop is TMA-latency-bound (~24k cycles per

@@ -42,3 +42,25 @@ def test_rejects_unsupported_shapes():
     w = torch.zeros(256, 100, device=DEV, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="hb_gemm_swiglu"):
         ops.gemm_swiglu(x, w)
+
+
+@pytest.mark.parametrize("rows", [100, 1300])
+def test_feed_forward_takes_either_path_with_the_same_result(rows, monkeypatch):
+    """FeedForward switches to the fused kernel from FUSED_GATE_UP_MIN_ROWS rows (below it, cuBLAS and
+    the SwiGLU kernel): both routes give the reference's rounding chain."""
+    from helios_b200 import model as model_mod
+    from helios_b200.config import Qwen3Config
+
+    torch.manual_seed(5)
+    cfg = Qwen3Config(vocab_size=64, context_length=4096, hidden_size=256, n_heads=2, n_layers=1, hidden_dim=512,
+                      head_dim=128, n_kv_heads=1, dtype=torch.bfloat16)
+    ff = model_mod.FeedForward(cfg).to(DEV)
+    x = torch.randn(rows, 256, device=DEV).to(torch.bfloat16)
+    with torch.inference_mode():
+        default = ff(x)
+        monkeypatch.setattr(model_mod, "FUSED_GATE_UP_MIN_ROWS", 1)
+        fused = ff(x)
+        monkeypatch.setattr(model_mod, "FUSED_GATE_UP_MIN_ROWS", 1 << 30)
+        unfused = ff(x)
+    torch.testing.assert_close(fused.float(), unfused.float(), rtol=2e-2, atol=2e-2)
+    assert torch.equal(default, fused if rows >= model_mod.FUSED_GATE_UP_MIN_ROWS else unfused)
