@@ -28,6 +28,7 @@ STATUS_BITS = {
     1 << 3: "page index outside the pool",
     1 << 4: "token id outside the vocabulary",
     1 << 5: "row index outside its tensor",
+    1 << 6: "prefix index full",
 }
 
 P = c_void_p
@@ -54,6 +55,10 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "hb_swiglu": (c_int, [P, P, I64, I64, P]),
     "hb_gemm_swiglu": (c_int, [P, I32, I32, P, I32, P, P]),
     "hb_attention_set_overlap": (c_int, [I32]),
+    "hb_hash_token_blocks": (c_int, [P, P, I32, I32, P, P, P]),
+    "hb_prefix_index_insert": (c_int, [P, I32, P, P, I32, P]),
+    "hb_prefix_index_remove": (c_int, [P, I32, P, I32, P]),
+    "hb_prefix_index_lookup": (c_int, [P, I32, P, P, P, I32, P, P, P]),
     "hb_lm_head_argmax": (c_int, [P, I32, I32, P, I32, P, P, P]),
     "hb_rope_gather": (c_int, [P, P, I64, I32, P, I32, I32, P, P, P]),
     "hb_gemm_qkv_norm_rope_append": (c_int, [P, I32, I32, P, I32, I32, I32, P, P, F32, P, P, I32, I64, P, P, P, P,

@@ -27,6 +27,7 @@ enum StatusBits : unsigned int {
   kStatusBadPage = 1u << 3,       // a block-table page index lay outside the pool
   kStatusBadToken = 1u << 4,      // a token id lay outside the embedding table
   kStatusBadRow = 1u << 5,        // a row index lay outside its tensor
+  kStatusIndexFull = 1u << 6,     // a prefix-index insertion found no free slot
 };
 
 __device__ unsigned int g_status;

@@ -21,6 +21,7 @@
 #include "lm_head_argmax.cuh"
 #include "model_ops.cuh"
 #include "norm_rope_append.cuh"
+#include "prefix_index.cuh"
 #include "sampler.cuh"
 #include "tick_pack.cuh"
 
@@ -614,6 +615,50 @@ int hb_lm_head_argmax(const void* x, int32_t m, int32_t k, const void* weight, i
     return rc;
   hb::argmax_finalize_kernel<<<(m + 127) / 128, 128, 0, stream>>>(best, m, out_ids);
   return check_launch("argmax_finalize_kernel");
+}
+
+int hb_hash_token_blocks(const int32_t* tokens, const int64_t* offsets, int32_t prompts, int32_t block_size,
+                         const int64_t* block_offsets, uint8_t* digests, cudaStream_t stream) {
+  if (prompts < 0 || block_size < 1) return fail(HB_ERR_INVALID, "bad prompt count or block size");
+  if (prompts == 0) return HB_OK;
+  if (tokens == nullptr || offsets == nullptr || block_offsets == nullptr || digests == nullptr)
+    return fail(HB_ERR_INVALID, "null block-hash pointer");
+  hb::hash_blocks_kernel<<<(prompts + hb::kHashWarps - 1) / hb::kHashWarps, hb::kHashWarps * 32, 0, stream>>>(
+      tokens, offsets, prompts, block_size, block_offsets, digests);
+  return check_launch("hash_blocks_kernel");
+}
+
+static bool index_slots_ok(int32_t slots) { return slots >= 1 && (slots & (slots - 1)) == 0; }
+
+int hb_prefix_index_insert(uint32_t* table, int32_t slots, const uint8_t* digests, const int32_t* values, int32_t n,
+                           cudaStream_t stream) {
+  if (!index_slots_ok(slots) || n < 0) return fail(HB_ERR_INVALID, "index slots must be a power of two, n >= 0");
+  if (n == 0) return HB_OK;
+  if (table == nullptr || digests == nullptr || values == nullptr) return fail(HB_ERR_INVALID, "null index pointer");
+  hb::prefix_index_insert_kernel<<<(n + 127) / 128, 128, 0, stream>>>(table, slots, digests, values, n);
+  return check_launch("prefix_index_insert_kernel");
+}
+
+int hb_prefix_index_remove(uint32_t* table, int32_t slots, const uint8_t* digests, int32_t n, cudaStream_t stream) {
+  if (!index_slots_ok(slots) || n < 0) return fail(HB_ERR_INVALID, "index slots must be a power of two, n >= 0");
+  if (n == 0) return HB_OK;
+  if (table == nullptr || digests == nullptr) return fail(HB_ERR_INVALID, "null index pointer");
+  hb::prefix_index_remove_kernel<<<(n + 127) / 128, 128, 0, stream>>>(table, slots, digests, n);
+  return check_launch("prefix_index_remove_kernel");
+}
+
+int hb_prefix_index_lookup(const uint32_t* table, int32_t slots, const uint8_t* digests, const int64_t* block_offsets,
+                           const int32_t* full_blocks, int32_t prompts, int32_t* matched, int32_t* values,
+                           cudaStream_t stream) {
+  if (!index_slots_ok(slots) || prompts < 0)
+    return fail(HB_ERR_INVALID, "index slots must be a power of two, prompts >= 0");
+  if (prompts == 0) return HB_OK;
+  if (table == nullptr || digests == nullptr || block_offsets == nullptr || full_blocks == nullptr ||
+      matched == nullptr || values == nullptr)
+    return fail(HB_ERR_INVALID, "null index pointer");
+  hb::prefix_lookup_kernel<<<(prompts + 127) / 128, 128, 0, stream>>>(table, slots, digests, block_offsets,
+                                                                       full_blocks, prompts, matched, values);
+  return check_launch("prefix_lookup_kernel");
 }
 
 int hb_rope_gather(const float* cos, const float* sin, int64_t rope_rows, int32_t head_dim, const int64_t* positions,

@@ -2,7 +2,7 @@
 
     python -m helios_b200.microbench [norm_rope] [swiglu] [add_rmsnorm] [prefill] [decode] [mixed[:N]] [prefix_decode] [sample]
                                      [gate_up_fused] [gate_up_cublas] [qkv_fused] [qkv_fused_full_tables] [qkv_cublas]
-                                     [lm_head_argmax33|128] [lm_head_cublas33|128]
+                                     [lm_head_argmax33|128] [lm_head_cublas33|128] [prefix_hash]
 
 Each case captures 24 calls of one entry point into a CUDA graph, cycling over input sets
 whose total exceeds the 126 MB L2 where the kernel is memory-bound, and prints the median
@@ -244,6 +244,29 @@ def _lm_head(dev, g, rows: int, fused: bool):
     return [make() for _ in range(2)], vocab * HIDDEN * 2
 
 
+def _prefix_hash(dev, rows: int = 128):
+    """BASELINE config 4's admission keys: 128 prompts of 4096 shared + U[256, 1024] own tokens,
+    256-token blocks, keyed on the device (hb_hash_token_blocks). Bytes: the int32 tokens read."""
+    from helios_b200 import prefix_index
+
+    rng = torch.Generator().manual_seed(3)
+    shared = torch.randint(0, 151936, (4096,), generator=rng).tolist()
+    prompts = [shared + torch.randint(0, 151936, (int(n),), generator=rng).tolist()
+               for n in torch.randint(256, 1025, (rows,), generator=rng)]
+    tokens, offsets, block_offsets, _ = prefix_index._flatten(prompts, 256)
+    d_tok = torch.from_numpy(tokens).to(dev)
+    d_off = torch.from_numpy(offsets).to(dev)
+    d_boff = torch.from_numpy(block_offsets).to(dev)
+    digests = torch.empty((int(block_offsets[-1]), 32), dtype=torch.uint8, device=dev)
+
+    def call():
+        rc = _native.load().hb_hash_token_blocks(d_tok.data_ptr(), d_off.data_ptr(), rows, 256, d_boff.data_ptr(),
+                                                 digests.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        _native.check(rc, "hb_hash_token_blocks")
+
+    return [call], tokens.size * 4
+
+
 def main(argv: list[str]) -> None:
     if not torch.cuda.is_available():
         raise SystemExit("the microbenchmarks need a CUDA device")
@@ -265,6 +288,7 @@ def main(argv: list[str]) -> None:
         "qkv_fused": lambda: _qkv(dev, g, True),
         "qkv_fused_full_tables": lambda: _qkv(dev, g, True, half_tables=False),
         "qkv_cublas": lambda: _qkv(dev, g, False),
+        "prefix_hash": lambda: _prefix_hash(dev),
         "lm_head_argmax33": lambda: _lm_head(dev, g, 33, True),
         "lm_head_cublas33": lambda: _lm_head(dev, g, 33, False),
         "lm_head_argmax128": lambda: _lm_head(dev, g, 128, True),

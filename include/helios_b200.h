@@ -48,6 +48,7 @@ typedef hb_stream_t cudaStream_t;
 #define HB_STATUS_BAD_PAGE (1u << 3)
 #define HB_STATUS_BAD_TOKEN (1u << 4)
 #define HB_STATUS_BAD_ROW (1u << 5)
+#define HB_STATUS_INDEX_FULL (1u << 6)
 
 HB_API int hb_version(void);
 HB_API const char* hb_last_error(void);
@@ -217,6 +218,37 @@ HB_API int hb_gemm_swiglu(const void* x, int32_t m, int32_t k, const void* w_gat
  */
 HB_API int hb_lm_head_argmax(const void* x, int32_t m, int32_t k, const void* weight, int32_t vocab,
                              unsigned long long* best, int64_t* out_ids, cudaStream_t stream);
+
+/*
+ * Prefix-cache block keys (replaces hash_token_blocks / build_token_blocks,
+ * src/helios/runtime/prefix_cache.py:86-110, as PrefixCache.longest_prefix and
+ * store_completed_blocks call them, :208-260). Prompt p is tokens[offsets[p], offsets[p+1])
+ * (int32 ids >= 0); it is cut into blocks of block_size tokens, the last one possibly partial,
+ * and block i's key is SHA-256(key of block i-1 || "[t0,t1,...]"): the decimal ids joined by
+ * commas in brackets, the compact JSON the reference hashes, with no parent bytes for block 0.
+ * The 32-byte keys go to digests + 32 * (block_offsets[p] + i). One warp per prompt.
+ */
+HB_API int hb_hash_token_blocks(const int32_t* tokens, const int64_t* offsets, int32_t prompts, int32_t block_size,
+                                const int64_t* block_offsets, uint8_t* digests, cudaStream_t stream);
+
+/*
+ * Device-resident prefix index: an open-addressing table of `slots` (a power of two) 48-byte
+ * slots, uint32 [slots][12], zeroed before first use. Insert adds n keys (32-byte digests) with
+ * int32 values; each key must be absent from the table and appear once in the batch (the
+ * caller's host-side map knows), and the caller keeps at most slots / 2 keys live, else
+ * HB_STATUS_INDEX_FULL. Remove drops the keys it finds. Lookup replaces the probe loop of
+ * PrefixCache.longest_prefix (prefix_cache.py:214-221): for prompt p it probes the keys of its
+ * first full_blocks[p] blocks (digests laid out as hb_hash_token_blocks writes them) in order,
+ * stops at the first absent one, writes the values of the matched blocks to
+ * values[block_offsets[p] + i] and their count to matched[p].
+ */
+HB_API int hb_prefix_index_insert(uint32_t* table, int32_t slots, const uint8_t* digests, const int32_t* values,
+                                  int32_t n, cudaStream_t stream);
+HB_API int hb_prefix_index_remove(uint32_t* table, int32_t slots, const uint8_t* digests, int32_t n,
+                                  cudaStream_t stream);
+HB_API int hb_prefix_index_lookup(const uint32_t* table, int32_t slots, const uint8_t* digests,
+                                  const int64_t* block_offsets, const int32_t* full_blocks, int32_t prompts,
+                                  int32_t* matched, int32_t* values, cudaStream_t stream);
 
 /*
  * Per-token rope rows for hb_gemm_qkv_norm_rope_append: out[g][t][0..3] = table[positions[t]][4g ..

@@ -195,3 +195,28 @@ def test_sampler_deterministic_draw_is_inverse_cdf():
     # kept (nothing precedes it); at p=0.7 the second survives (0.644 precedes it).
     assert osampler.keep_mask(logits, 1.0, 0.5)[0].tolist() == [False, False, False, True]
     assert osampler.keep_mask(logits, 1.0, 0.7)[0].tolist() == [False, False, True, True]
+
+
+def test_prefix_keys_oracle_matches_the_reference(golden_dir):
+    """The hashlib restatement of hash_token_blocks gives the keys the reference computed."""
+    import json
+
+    from oracle.prefix_hash import block_keys
+
+    for case in json.loads((golden_dir / "prefix_hash.json").read_text()):
+        keys = block_keys(case["tokens"], case["block_size"])
+        assert [k.hex() for k in keys] == case["hashes"]
+        assert [""] + [k.hex() for k in keys[:-1]] == case["parents"] if keys else not case["parents"]
+
+
+def test_prefix_index_host_checks_match_the_reference():
+    import pytest
+
+    from helios_b200.prefix_index import _flatten
+
+    with pytest.raises(ValueError, match="block_size must be at least 1"):
+        _flatten([[1, 2]], 0)
+    with pytest.raises(ValueError, match="non-negative"):
+        _flatten([[1, -2]], 4)
+    tokens, offsets, block_offsets, full = _flatten([[1, 2, 3], [], [4] * 9], 4)
+    assert offsets.tolist() == [0, 3, 3, 12] and block_offsets.tolist() == [0, 1, 1, 4] and full.tolist() == [0, 0, 2]
