@@ -97,3 +97,14 @@ def test_decode_caches_greedy_is_the_argmax_of_decode_caches(golden_dir):
     ids = decoder.decode_caches_greedy(caches_b, tokens)
     assert ids.tolist() == logits.argmax(-1).tolist()
     assert [c.length for c in caches_a] == [c.length for c in caches_b]
+
+
+def test_nan_logits_win_at_their_lowest_id():
+    """A NaN logit counts as the largest, as torch.argmax treats it; of several, the lowest id."""
+    g = torch.Generator(device=DEV).manual_seed(11)
+    x = torch.randint(-1, 2, (5, 128), device=DEV, generator=g).to(torch.bfloat16)
+    w = torch.randint(-1, 2, (1000, 128), device=DEV, generator=g).to(torch.bfloat16)
+    w[700, 3] = float("nan")
+    w[300, 5] = float("nan")
+    ids = ops.lm_head_argmax(x, w)
+    assert ids.tolist() == F.linear(x, w).argmax(-1).tolist() == [300] * 5
