@@ -364,7 +364,7 @@ class PagedBatchCache:
         pool, config = self.pool, self.pool.config
         page_size = pool.page_size
         updates: list[int] = []
-        fields: list[tuple] = []
+        fields: list[int] = []
         for cache, count, lc in zip(self.caches, counts, logit_counts):
             n = len(cache.pages)
             if cache._synced < n:
@@ -372,7 +372,7 @@ class PagedBatchCache:
                 for j in range(cache._synced, n):
                     updates += (slot, j, cache.pages[j].index)
                 cache._synced = n
-            fields.append((cache._slot, cache.length, count, lc, n, 0, 0))
+            fields += (cache._slot, cache.length, count, lc, n, 0, 0)
         rows = np.array(fields, dtype=np.int32).reshape(self.batch_size, ops.TICK_ROW_FIELDS)
         group = config.n_heads // config.n_kv_heads
         decode_max = DECODE_QUERY_ROWS // group
@@ -420,13 +420,15 @@ class PagedBatchCache:
                 continue
             head = caches[r].pages
             common, j = lead, r + 1
+            shared = head[:common]  # the group's common pages so far, sliced once per change
             while j < count and j - r < decode_max:
-                limit = min(common, full[j])
+                fj = full[j]
+                limit = common if fj >= common else fj
                 pages = caches[j].pages
                 # Restored pages are the same handle objects, so the slice comparison (element
                 # identity first, in C) settles the common case; the index walk finds a shorter
                 # common prefix.
-                if limit >= MIN_SHARED_PAGES and pages[:limit] == head[:limit]:
+                if limit >= MIN_SHARED_PAGES and pages[:limit] == (shared if limit == common else shared[:limit]):
                     lcp = limit
                 else:
                     lcp = 0
@@ -434,7 +436,9 @@ class PagedBatchCache:
                         lcp += 1
                 if lcp < MIN_SHARED_PAGES:
                     break
-                common = lcp
+                if lcp != common:
+                    common = lcp
+                    shared = head[:common]
                 j += 1
             if j - r >= 2:
                 rows[r:j, 5] = common * page_size
