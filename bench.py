@@ -307,27 +307,10 @@ def prefill_attention_roofline(device: torch.device, peak_tflops: float, iters: 
 def decode_attention_roofline(device: torch.device, peak_gbs: float, iters: int = 20) -> dict:
     """BASELINE config 2 through the C ABI: 64 rows x 1 query, contexts U[512, 8192], 4096 pages."""
     from helios_b200 import ops
-    from helios_b200.config import Qwen3Config
-    from helios_b200.paged_cache import KVPagePool, PackedBatchCache, PagedKVCache
+    from helios_b200.workloads import config2_batch
 
-    cfg = Qwen3Config(n_layers=1, context_length=8192 + 64)
-    g = torch.Generator().manual_seed(1)
-    pool = KVPagePool(cfg, 4096, device=device)
-    gen = torch.Generator(device=device).manual_seed(1)
-    pool.storage.normal_(0.0, 1.0 / math.sqrt(128), generator=gen)
-    contexts = torch.randint(512, 8193, (64,), generator=g).tolist()
-    perm = torch.randperm(4096, generator=g).tolist()
-    pool._free = list(reversed(perm))  # acquire() pops: pages come in permutation order
-    caches = []
-    for ctx in contexts:
-        cache = PagedKVCache(pool, ctx)
-        cache.pages.extend(pool.acquire(math.ceil((ctx - 1) / 256)))
-        cache.length = ctx - 1
-        caches.append(cache)
-    batch = PackedBatchCache(caches)
+    pool, batch, q, contexts = config2_batch(device)
     with torch.inference_mode():
-        batch.prepare_packed([1] * 64)
-        q = (torch.randn(64, 32, 128, generator=g) / math.sqrt(128)).to(torch.bfloat16).to(device)
         out = torch.empty_like(q)
         for _ in range(3):
             ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out)
@@ -348,7 +331,7 @@ def decode_attention_roofline(device: torch.device, peak_gbs: float, iters: int 
             "workload": "BASELINE config 2: 64 rows x 1 query, context U[512,8192], 32/8 heads, d=128, 4096 pages",
             "algorithmic_bytes_per_call": kv_bytes + io_bytes, "us_per_call": round(seconds * 1e6, 2),
             "split_keys": batch.split_keys, "decode_items": batch.num_decode_items}
-    del pool, batch, caches
+    del pool, batch
     torch.cuda.empty_cache()
     return info
 

@@ -384,17 +384,62 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
   p.num_decode = num_decode_items;
   p.decode_ctas = std::max(1, std::min(overlap_sms, decode_grid));
   p.prefill_after_decode = num_decode_items > 0 ? 1 : 0;
+
+  // Everything that can fail before a launch (the prefill tensor map, the shared-memory
+  // opt-ins) is done first, so an early return never leaves the decode grid queued without
+  // the combine that resets its work ticket.
+  CUtensorMap qmap;
+  if (num_prefill_items > 0) {
+#define HB_PREFILL_PREP(G)                                                                                      \
+  do {                                                                                                          \
+    if (int rc = encode_3d(&qmap, q, head_dim, heads, total_tokens, head_dim * 2,                               \
+                           static_cast<uint64_t>(heads) * head_dim * 2, 64, G, hb::kPreRows / G))               \
+      return rc;                                                                                                \
+    if (int rc = ensure_smem(hb::prefill_attention_kernel<G>, hb::kPreSmemBytes, g_pre_smem[gs])) return rc;     \
+  } while (0)
+    switch (group) {
+      case 1: HB_PREFILL_PREP(1); break;
+      case 2: HB_PREFILL_PREP(2); break;
+      case 4: HB_PREFILL_PREP(4); break;
+      default: HB_PREFILL_PREP(8); break;
+    }
+#undef HB_PREFILL_PREP
+  }
+  if (num_decode_items > 0) {
+#define HB_DECODE_PREP(G)                                                                                       \
+  do {                                                                                                          \
+    if (beside) {                                                                                               \
+      if (int rc = ensure_smem(hb::decode_persistent_kernel<G>, hb::kDecPersistentSmemBytes, g_decp_smem[gs]))  \
+        return rc;                                                                                              \
+    } else if (int rc = ensure_smem(hb::decode_attention_kernel<G>, hb::kDecSmemBytes, g_dec_smem[gs])) {       \
+      return rc;                                                                                                \
+    }                                                                                                           \
+  } while (0)
+    switch (group) {
+      case 1: HB_DECODE_PREP(1); break;
+      case 2: HB_DECODE_PREP(2); break;
+      case 4: HB_DECODE_PREP(4); break;
+      default: HB_DECODE_PREP(8); break;
+    }
+#undef HB_DECODE_PREP
+  }
+
+  // Once the persistent decode grid is queued, its work ticket is nonzero until the combine
+  // grid resets it. If a later launch fails, a 4-byte memset queued behind the decode grid
+  // resets it instead (it allocates nothing), so the next call on this workspace starts at 0.
+  bool ticket_queued = false;
+  auto fail_after_decode = [&](int rc) {
+    if (ticket_queued) cudaMemsetAsync(workspace, 0, sizeof(int32_t), stream);
+    return rc;
+  };
   if (num_decode_items > 0) {
 #define HB_DECODE(G)                                                                                            \
   do {                                                                                                          \
     cudaError_t e;                                                                                              \
     if (beside) {                                                                                               \
-      if (int rc = ensure_smem(hb::decode_persistent_kernel<G>, hb::kDecPersistentSmemBytes, g_decp_smem[gs]))  \
-        return rc;                                                                                              \
       e = launch_pdl(hb::decode_persistent_kernel<G>, dim3(decode_grid), dim3(hb::kDecPersistentThreads),       \
                      hb::kDecPersistentSmemBytes, stream, p, kmap, vmap);                                       \
     } else {                                                                                                    \
-      if (int rc = ensure_smem(hb::decode_attention_kernel<G>, hb::kDecSmemBytes, g_dec_smem[gs])) return rc;   \
       e = launch_pdl(hb::decode_attention_kernel<G>, dim3(num_decode_items * kv_heads), dim3(hb::kDecSubThreads), \
                      hb::kDecSmemBytes, stream, p, kmap, vmap);                                                 \
     }                                                                                                           \
@@ -407,19 +452,16 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
       default: HB_DECODE(8); break;
     }
 #undef HB_DECODE
+    ticket_queued = beside;
   }
   if (num_prefill_items > 0) {
-    CUtensorMap qmap;
     const dim3 grid(kv_heads, num_prefill_items);
 #define HB_PREFILL(G)                                                                                           \
   do {                                                                                                          \
-    if (int rc = encode_3d(&qmap, q, head_dim, heads, total_tokens, head_dim * 2,                               \
-                           static_cast<uint64_t>(heads) * head_dim * 2, 64, G, hb::kPreRows / G))               \
-      return rc;                                                                                                \
-    if (int rc = ensure_smem(hb::prefill_attention_kernel<G>, hb::kPreSmemBytes, g_pre_smem[gs])) return rc;     \
     const cudaError_t e = launch_pdl(hb::prefill_attention_kernel<G>, grid, dim3(hb::kPreThreads),              \
                                      hb::kPreSmemBytes, stream, p, qmap, kmap, vmap);                           \
-    if (e != cudaSuccess) return fail(HB_ERR_CUDA, "prefill_attention_kernel: %s", cudaGetErrorString(e));      \
+    if (e != cudaSuccess)                                                                                       \
+      return fail_after_decode(fail(HB_ERR_CUDA, "prefill_attention_kernel: %s", cudaGetErrorString(e)));      \
   } while (0)
     switch (group) {
       case 1: HB_PREFILL(1); break;
@@ -434,7 +476,8 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
 #define HB_COMBINE(G)                                                                                          \
   do {                                                                                                         \
     const cudaError_t e = launch_pdl(hb::decode_combine_kernel<G>, grid, dim3(128), 0, stream, p);             \
-    if (e != cudaSuccess) return fail(HB_ERR_CUDA, "decode_combine_kernel: %s", cudaGetErrorString(e));        \
+    if (e != cudaSuccess)                                                                                      \
+      return fail_after_decode(fail(HB_ERR_CUDA, "decode_combine_kernel: %s", cudaGetErrorString(e)));       \
   } while (0)
     switch (group) {
       case 1: HB_COMBINE(1); break;

@@ -7,6 +7,14 @@ plus ``_sample`` (:457-473). Sampling runs in the fused CUDA sampler; a
 caller-supplied ``uniforms`` tensor makes a draw deterministic, otherwise one
 uniform per row is drawn on the device (no host synchronisation).
 
+The rest of the reference decoder's surface that its ``Engine``, ``Generator`` and
+warmup call (``begin_prefill`` :133-187, ``prefill_chunk`` :189-218, ``prefill``
+:106-131, ``generate`` :68-104, ``decode`` :322-394, ``release_cache`` :403-408,
+``_synchronize`` :435-439, ``device``) is here with the same arguments, results,
+exceptions and timing semantics, so those callers run unchanged over this decoder
+(``helios_b200.reference_engine`` swaps it in). Request caches are always paged:
+there is no dense-KV path.
+
 ``sample_rows`` is the batched sampling of ``Engine._execute_batch``
 (src/helios/runtime/engine.py:470-492): per-row temperature and top-p in one
 launch instead of grouping rows by equal settings. ``sample_and_verify`` adds the
@@ -15,7 +23,9 @@ speculative verification of drafted rows (engine.py:488-520) on the device.
 
 from __future__ import annotations
 
+import time
 from collections.abc import Sequence
+from dataclasses import dataclass
 from itertools import accumulate
 
 import torch
@@ -24,6 +34,49 @@ from helios_b200 import ops
 from helios_b200.config import Sampling
 from helios_b200.model import Qwen3Model
 from helios_b200.paged_cache import KVPagePool, PackedBatchCache, PagedBatchCache, PagedKVCache
+
+
+@dataclass
+class PrefillState:
+    """What ``begin_prefill`` hands the engine (decode.py:48-53)."""
+    cache: PagedKVCache
+    next_token_offset: int
+    restore_seconds: float
+    restored_tokens: int
+
+
+@dataclass
+class PrefillResult:
+    """A whole-prompt prefill (decode.py:39-45): the last position's logits ``[1, V]``."""
+    cache: PagedKVCache
+    logits: torch.Tensor
+    prefill_seconds: float
+    restore_seconds: float
+    restored_tokens: int
+
+
+@dataclass
+class DecodedTokens:
+    """The decode loop's output (decode.py:56-62)."""
+    first_token_at: float
+    token_intervals: tuple[float, ...]
+    output_ids: list[int]
+    finish_reason: str
+    inter_token_seconds: list[float]
+
+
+@dataclass
+class DecodeResult:
+    """One request's generation (decode.py:25-36)."""
+    first_token_at: float
+    token_intervals: tuple[float, ...]
+    output_ids: list[int]
+    finish_reason: str
+    prefill_seconds: float
+    inter_token_seconds: list[float]
+    restore_seconds: float
+    restored_tokens: int
+    cache: PagedKVCache
 
 
 class Decoder:
@@ -36,6 +89,142 @@ class Decoder:
     @property
     def device(self) -> torch.device:
         return next(self.model.parameters()).device
+
+    # ---- single-request generation and admission (decode.py:68-218, :322-439)
+    def generate(self, input_ids: list[int], eos_token_id: int, sampling: Sampling, *, max_total_tokens: int,
+                 prefix_hit=None, request_id: str = "internal") -> DecodeResult:
+        """Prefill then decode one request (decode.py:68-104); the cache stays open for the caller."""
+        prefill = self.prefill(input_ids, sampling, max_total_tokens=max_total_tokens, prefix_hit=prefix_hit)
+        try:
+            decoded = self.decode(prefill, eos_token_id, sampling, request_id=request_id)
+        except Exception:
+            self.release_cache(prefill.cache)
+            raise
+        return DecodeResult(first_token_at=decoded.first_token_at, token_intervals=decoded.token_intervals,
+                            output_ids=decoded.output_ids, finish_reason=decoded.finish_reason,
+                            prefill_seconds=prefill.prefill_seconds, inter_token_seconds=decoded.inter_token_seconds,
+                            restore_seconds=prefill.restore_seconds, restored_tokens=prefill.restored_tokens,
+                            cache=prefill.cache)
+
+    def prefill(self, input_ids: list[int], sampling: Sampling, *, max_total_tokens: int,
+                prefix_hit=None) -> PrefillResult:
+        """``begin_prefill`` plus one chunk of the rest of the prompt (decode.py:106-131)."""
+        state = self.begin_prefill(input_ids, sampling, max_total_tokens=max_total_tokens, prefix_hit=prefix_hit)
+        try:
+            logits, seconds = self.prefill_chunk(state.cache, input_ids[state.next_token_offset:])
+        except Exception:
+            self.release_cache(state.cache)
+            raise
+        return PrefillResult(cache=state.cache, logits=logits, prefill_seconds=seconds,
+                             restore_seconds=state.restore_seconds, restored_tokens=state.restored_tokens)
+
+    def begin_prefill(self, input_ids: list[int], sampling: Sampling, *, max_total_tokens: int,
+                      prefix_hit=None) -> PrefillState:
+        """Open a paged request cache of ``len(input_ids) + max_new_tokens`` positions and alias the
+        prefix-cache hit's pages into it (decode.py:133-187). ``prefix_hit`` is the reference's
+        ``PrefixCacheHit`` (``blocks`` of ``tokens`` + ``snapshot``). On an exact full-prompt hit the
+        last block is left out, so the final prompt token still runs and yields logits."""
+        capacity = len(input_ids) + sampling.max_new_tokens
+        if capacity > max_total_tokens:
+            raise ValueError(f"Request needs {capacity:,} KV-cache tokens, but the profiled "
+                             f"limit is {max_total_tokens:,}.")
+        if self.page_pool is None:
+            raise RuntimeError("The B200 decoder needs a KV page pool (Decoder.page_pool).")
+        cache = PagedKVCache(self.page_pool, capacity)
+        try:
+            blocks = tuple(prefix_hit.blocks) if prefix_hit is not None else ()
+            if blocks:
+                if any(len(block.tokens) != block.snapshot.length for block in blocks):
+                    raise ValueError("Prefix-cache token and KV block lengths do not match.")
+                cached = [token for block in blocks for token in block.tokens]
+                if len(cached) > len(input_ids):
+                    raise ValueError("Prefix-cache hit is longer than the request prompt.")
+                if list(input_ids[:len(cached)]) != cached:
+                    raise ValueError("Prefix-cache hit does not match the request tokens.")
+                if len(cached) == len(input_ids):
+                    blocks = blocks[:-1]
+            started = time.perf_counter()
+            cache.restore_blocks(tuple(block.snapshot for block in blocks))
+            restore_seconds = time.perf_counter() - started
+            return PrefillState(cache=cache, next_token_offset=cache.length, restore_seconds=restore_seconds,
+                                restored_tokens=cache.length)
+        except Exception:
+            self.release_cache(cache)
+            raise
+
+    def prefill_chunk(self, cache: PagedKVCache, input_ids_slice: Sequence[int] | torch.Tensor
+                      ) -> tuple[torch.Tensor, float]:
+        """Run one prompt chunk of one request; returns its last position's logits ``[1, V]`` and
+        the synchronised wall time (decode.py:189-218). The chunk runs as a one-row packed tick,
+        so only its last position goes through the lm_head."""
+        if isinstance(input_ids_slice, torch.Tensor):
+            tokens = input_ids_slice.to(dtype=torch.long)
+            if tokens.ndim == 1:
+                tokens = tokens.unsqueeze(0)
+        else:
+            tokens = torch.tensor(list(input_ids_slice), dtype=torch.long).unsqueeze(0)
+        if tokens.ndim != 2 or tokens.shape[0] != 1 or tokens.shape[1] < 1:
+            raise ValueError("Prefill chunks must contain at least one token with shape [1, tokens].")
+        if self.model.training:
+            self.model.eval()
+        self._synchronize()
+        started = time.perf_counter()
+        logits = self._packed([cache], [tokens[0].tolist()], None, greedy=False)
+        self._validate_forward_shapes(tokens[:, -1:], logits.unsqueeze(1))
+        self._synchronize()
+        return logits, time.perf_counter() - started
+
+    def decode(self, prefill: PrefillResult, eos_token_id: int, sampling: Sampling, *,
+               request_id: str = "internal") -> DecodedTokens:
+        """Sample from the prefill logits, then decode one token per step until EOS or
+        ``max_new_tokens`` (decode.py:322-394), timing each step between synchronisations."""
+        first_token_at = last_token_at = None
+        intervals: list[float] = []
+        generated: list[int] = []
+        inter_token_seconds: list[float] = []
+        finish_reason = "length"
+        logits, cache = prefill.logits, prefill.cache
+        for index in range(sampling.max_new_tokens):
+            next_token = self._sample(logits, sampling)
+            token_id = int(next_token.item())
+            sampled_at = time.perf_counter()
+            if first_token_at is None:
+                first_token_at = sampled_at
+            if token_id == eos_token_id:
+                finish_reason = "eos"
+                break
+            if last_token_at is not None:
+                intervals.append(sampled_at - last_token_at)
+            last_token_at = sampled_at
+            generated.append(token_id)
+            if index + 1 < sampling.max_new_tokens:
+                self._synchronize()
+                started = time.perf_counter()
+                logits = self.decode_caches([cache], [token_id])
+                self._validate_forward_shapes(next_token, logits.unsqueeze(1))
+                self._synchronize()
+                inter_token_seconds.append(time.perf_counter() - started)
+        return DecodedTokens(first_token_at=first_token_at, token_intervals=tuple(intervals), output_ids=generated,
+                             finish_reason=finish_reason, inter_token_seconds=inter_token_seconds)
+
+    @staticmethod
+    def release_cache(cache: PagedKVCache) -> None:
+        """Return a request cache's pages to the pool (decode.py:403-408)."""
+        cache.close()
+
+    def _synchronize(self) -> None:
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+
+    def _validate_forward_shapes(self, input_ids: torch.Tensor, logits: torch.Tensor) -> None:
+        """Shape checks of one forward (decode.py:441-455), same messages."""
+        if input_ids.ndim != 2 or input_ids.shape[0] != 1 or input_ids.shape[1] < 1:
+            raise RuntimeError("Decoder input must have shape [1, tokens] with at least one token.")
+        if input_ids.dtype != torch.long:
+            raise RuntimeError("Decoder input token IDs must use torch.long.")
+        expected = (1, 1, self.model.config.vocab_size)
+        if tuple(logits.shape) != expected:
+            raise RuntimeError(f"Decoder logits must have shape {expected}; received {tuple(logits.shape)}.")
 
     def decode_caches(self, caches: list[PagedKVCache], token_ids: list[int]) -> torch.Tensor:
         """Logits ``[B, V]`` of one decode step of every cache (decode.py:220-258)."""

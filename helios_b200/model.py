@@ -52,9 +52,13 @@ class RMSNorm(nn.Module):
 
 
 def rope_parameters(config: Qwen3Config) -> tuple[torch.Tensor, torch.Tensor]:
-    """Same tables as layers.py:43-51: angles = pos * theta^(-2i/d), duplicated halves."""
-    inverse = 1.0 / (config.rope_base ** (torch.arange(0, config.head_dim, 2, dtype=torch.float32) / config.head_dim))
-    angles = torch.arange(config.context_length, dtype=torch.float32).unsqueeze(1) * inverse.unsqueeze(0)
+    """Same tables as layers.py:43-51: angles = pos * theta^(-2i/d), duplicated halves.
+    Always computed on the CPU, as the reference builds them before moving the model, so
+    the fp32 tables are the reference's bit for bit whatever device the model lives on."""
+    cpu = torch.device("cpu")
+    inverse = 1.0 / (config.rope_base ** (torch.arange(0, config.head_dim, 2, dtype=torch.float32, device=cpu)
+                                          / config.head_dim))
+    angles = torch.arange(config.context_length, dtype=torch.float32, device=cpu).unsqueeze(1) * inverse.unsqueeze(0)
     angles = torch.cat((angles, angles), dim=1)
     return torch.cos(angles), torch.sin(angles)
 
@@ -175,13 +179,34 @@ class Qwen3Model(nn.Module):
         self.output = nn.Linear(config.hidden_size, config.vocab_size, bias=False, dtype=config.dtype)
         self.output.weight = self.token_embedding.weight
         cos, sin = rope_parameters(config)
-        self.register_buffer("cos", cos, persistent=False)
-        self.register_buffer("sin", sin, persistent=False)
         # Each row's second half repeats its first (duplicated angles): the fused q|k|v
         # kernel may then read half of every row. Checked on the host tables once.
         half = config.head_dim // 2
         self.rope_half_tables = bool(torch.equal(cos[:, :half], cos[:, half:]) and torch.equal(sin[:, :half], sin[:, half:]))
+        device = self.token_embedding.weight.device  # the device the module is being built on
+        self.register_buffer("cos", cos.to(device), persistent=False)
+        self.register_buffer("sin", sin.to(device), persistent=False)
         self._graphs = None  # TickGraphs once enable_cuda_graphs() is called
+
+    @classmethod
+    def from_state_dict(cls, config: Qwen3Config, state_dict: dict[str, torch.Tensor],
+                        device: torch.device | str) -> "Qwen3Model":
+        """A model on ``device`` holding ``state_dict`` (reference names, e.g. a reference
+        ``Qwen3Model.state_dict()`` or a loaded checkpoint), without drawing random weights
+        first: the modules are built on the meta device, materialised on ``device`` and
+        filled. Every parameter must be in ``state_dict``."""
+        with torch.device("meta"):
+            model = cls(config)
+        model = model.to_empty(device=device)
+        model.output.weight = model.token_embedding.weight  # materialising unties them
+        cos, sin = rope_parameters(config)
+        model.cos.copy_(cos)
+        model.sin.copy_(sin)
+        missing, unexpected = model.load_state_dict(state_dict, strict=False)
+        missing = [k for k in missing if k not in ("output.weight",)]
+        if missing or unexpected:
+            raise ValueError(f"state dict does not match the model: missing {missing}, unexpected {unexpected}")
+        return model.eval()
 
     def enable_cuda_graphs(self, max_graphs: int = 4) -> None:
         """Replay the device half of packed ticks from CUDA graphs (see helios_b200.graphs).

@@ -30,6 +30,36 @@ from helios_b200.paged_cache import KVPagePool, PagedKVCache
 PREFIX_TOKENS, REQUESTS, TAIL = 4096, 128, (256, 1024)
 
 
+def config2_batch(device: torch.device):
+    """BASELINE config 2's inputs: one attention layer of the Qwen3-4B shape (32/8 heads,
+    d=128), a 4096-page pool of N(0, 1/128) K/V (seed 1), 64 rows with contexts U[512, 8192]
+    (the query token included) whose pages come from a random permutation of the pool, and
+    one N(0, 1/128) query token per row. Returns ``(pool, batch, q, contexts)`` with the
+    batch prepared (``prepare_packed([1] * 64)``)."""
+    from helios_b200.config import Qwen3Config
+    from helios_b200.paged_cache import PackedBatchCache
+
+    cfg = Qwen3Config(n_layers=1, context_length=8192 + 64)
+    g = torch.Generator().manual_seed(1)
+    pool = KVPagePool(cfg, 4096, device=device)
+    gen = torch.Generator(device=device).manual_seed(1)
+    pool.storage.normal_(0.0, 1.0 / math.sqrt(128), generator=gen)
+    contexts = torch.randint(512, 8193, (64,), generator=g).tolist()
+    perm = torch.randperm(4096, generator=g).tolist()
+    pool._free = list(reversed(perm))  # acquire() pops: pages come in permutation order
+    caches = []
+    for ctx in contexts:
+        cache = PagedKVCache(pool, ctx)
+        cache.pages.extend(pool.acquire(math.ceil((ctx - 1) / 256)))
+        cache.length = ctx - 1
+        caches.append(cache)
+    batch = PackedBatchCache(caches)
+    with torch.inference_mode():
+        batch.prepare_packed([1] * 64)
+    q = (torch.randn(64, 32, 128, generator=g) / math.sqrt(128)).to(torch.bfloat16).to(device)
+    return pool, batch, q, contexts
+
+
 def config4(ticks: int, share: bool, warmup: int = 3) -> dict:
     device = torch.device("cuda", 0)
     cfg = qwen3_4b_config()

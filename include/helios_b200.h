@@ -165,8 +165,12 @@ HB_API int hb_attention_set_overlap(int32_t decode_sms);
  * that first call before any stream capture. Every call shares the one array and leaves
  * its contents behind. Of those, only the decode work ticket in the first 256 bytes must
  * start at zero: the array is zero when the library loads and every call resets the ticket
- * (the split-K partials are written before they are read). Calls that overlap on the GPU,
+ * (the split-K partials are written before they are read; a call that fails after queuing
+ * the decode grid queues a 4-byte reset of the ticket). Calls that overlap on the GPU,
  * from different streams or threads, race on the array.
+ * The device address is cached per device number for the life of the process: after
+ * cudaDeviceReset, or when another context is made current on that device (driver API),
+ * the cached address is stale and this entry point must not be called again.
  */
 #define HB_STATIC_WORKSPACE_BYTES (8u << 20)
 HB_API int hb_paged_attention_static_workspace(const void* q, const void* key_pool, const void* value_pool,

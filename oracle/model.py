@@ -20,6 +20,7 @@ TEST INFRASTRUCTURE ONLY (see ``oracle/__init__.py``).
 
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
 import torch
@@ -46,17 +47,28 @@ class OracleConfig:
     dtype: torch.dtype = torch.bfloat16
 
 
-def build_state_dict(config: OracleConfig, seed: int, *, layers: int | None = None) -> dict[str, torch.Tensor]:
+def build_state_dict(config: OracleConfig, seed: int, *, layers: int | None = None,
+                     rng_checkpoints: list[torch.Tensor] | None = None,
+                     threads: int = 1) -> dict[str, torch.Tensor]:
     """Reference random-init weights for ``torch.manual_seed(seed)``.
 
     ``layers`` truncates the stack (the first ``layers`` blocks are identical to
     the full model's, since blocks are created in order).
+
+    The reference draws every tensor from the one CPU generator in creation order,
+    which takes minutes at the Qwen3-4B shape. With ``rng_checkpoints`` (the generator
+    state before the embedding and before each block, from ``rng_checkpoints``) the
+    embedding and the blocks are drawn from their own generators, set to those states,
+    on ``threads`` threads: the same draws, so the same bits.
     """
-    torch.manual_seed(seed)
     c = config
+    n = c.n_layers if layers is None else layers
+    if rng_checkpoints is not None:
+        return _build_from_checkpoints(c, n, rng_checkpoints, threads)
+    torch.manual_seed(seed)
     sd: dict[str, torch.Tensor] = {}
     sd["token_embedding.weight"] = nn.Embedding(c.vocab_size, c.hidden_size, dtype=c.dtype).weight.data
-    for i in range(c.n_layers if layers is None else layers):
+    for i in range(n):
         p = f"blocks.{i}."
         sd[p + "attention.query.weight"] = nn.Linear(c.hidden_size, c.n_heads * c.head_dim, bias=False, dtype=c.dtype).weight.data
         sd[p + "attention.key.weight"] = nn.Linear(c.hidden_size, c.n_kv_heads * c.head_dim, bias=False, dtype=c.dtype).weight.data
@@ -69,6 +81,73 @@ def build_state_dict(config: OracleConfig, seed: int, *, layers: int | None = No
         sd[p + "feed_forward.down.weight"] = nn.Linear(c.hidden_dim, c.hidden_size, bias=False, dtype=c.dtype).weight.data
         sd[p + "input_norm.scale"] = torch.ones(c.hidden_size)
         sd[p + "post_attention_norm.scale"] = torch.ones(c.hidden_size)
+    sd["final_norm.scale"] = torch.ones(c.hidden_size)
+    sd["output.weight"] = sd["token_embedding.weight"]
+    return sd
+
+
+def _linear_weight(out_features: int, in_features: int, dtype: torch.dtype, generator: torch.Generator) -> torch.Tensor:
+    """``nn.Linear(in, out, bias=False).weight`` drawn from ``generator`` (Linear.reset_parameters)."""
+    w = torch.empty((out_features, in_features), dtype=dtype)
+    nn.init.kaiming_uniform_(w, a=math.sqrt(5), generator=generator)
+    return w
+
+
+def _block_state(c: OracleConfig, i: int, generator: torch.Generator) -> dict[str, torch.Tensor]:
+    p = f"blocks.{i}."
+    qd, kvd = c.n_heads * c.head_dim, c.n_kv_heads * c.head_dim
+    return {
+        p + "attention.query.weight": _linear_weight(qd, c.hidden_size, c.dtype, generator),
+        p + "attention.key.weight": _linear_weight(kvd, c.hidden_size, c.dtype, generator),
+        p + "attention.value.weight": _linear_weight(kvd, c.hidden_size, c.dtype, generator),
+        p + "attention.output.weight": _linear_weight(c.hidden_size, qd, c.dtype, generator),
+        p + "attention.q_norm.scale": torch.ones(c.head_dim),
+        p + "attention.k_norm.scale": torch.ones(c.head_dim),
+        p + "feed_forward.gate.weight": _linear_weight(c.hidden_dim, c.hidden_size, c.dtype, generator),
+        p + "feed_forward.up.weight": _linear_weight(c.hidden_dim, c.hidden_size, c.dtype, generator),
+        p + "feed_forward.down.weight": _linear_weight(c.hidden_size, c.hidden_dim, c.dtype, generator),
+        p + "input_norm.scale": torch.ones(c.hidden_size),
+        p + "post_attention_norm.scale": torch.ones(c.hidden_size),
+    }
+
+
+def rng_checkpoints(config: OracleConfig, seed: int) -> list[torch.Tensor]:
+    """CPU generator states before the embedding and before each block of the
+    reference's seed-``seed`` initialisation (one serial pass over every draw)."""
+    torch.manual_seed(seed)
+    states = [torch.get_rng_state()]
+    c = config
+    nn.Embedding(c.vocab_size, c.hidden_size, dtype=c.dtype)
+    generator = torch.default_generator
+    for i in range(c.n_layers):
+        states.append(torch.get_rng_state())
+        _block_state(c, i, generator)
+    return states
+
+
+def _build_from_checkpoints(c: OracleConfig, n: int, states: list[torch.Tensor], threads: int) -> dict[str, torch.Tensor]:
+    from concurrent.futures import ThreadPoolExecutor
+
+    if len(states) < n + 1:
+        raise ValueError("Need a generator state for the embedding and for every block.")
+
+    def embedding():
+        g = torch.Generator()
+        g.set_state(states[0])
+        w = torch.empty((c.vocab_size, c.hidden_size), dtype=c.dtype)
+        nn.init.normal_(w, generator=g)
+        return {"token_embedding.weight": w}
+
+    def block(i):
+        g = torch.Generator()
+        g.set_state(states[i + 1])
+        return _block_state(c, i, g)
+
+    with ThreadPoolExecutor(max(1, threads)) as pool:
+        parts = list(pool.map(lambda job: job(), [embedding] + [lambda i=i: block(i) for i in range(n)]))
+    sd: dict[str, torch.Tensor] = {}
+    for part in parts:
+        sd.update(part)
     sd["final_norm.scale"] = torch.ones(c.hidden_size)
     sd["output.weight"] = sd["token_embedding.weight"]
     return sd

@@ -17,8 +17,15 @@ directory, what its own code computes:
                      reference's dense-KV path and on its packed CPU path, plus 16
                      greedy steps.
   bf16_tick.npz   -- a bf16 mixed tick at the Qwen3-4B head shape (d=128, 4 query
-                     heads per KV head) on the reference's packed CPU path, plus 16
+                     heads per KV head) on the reference's packed CPU path, plus 64
                      greedy decode steps.
+  qwen3_4b_init.npz -- (``make_golden.py qwen3_4b_init``) digests of the reference's
+                     seed-0 Qwen3-4B weights and the generator states that let a test
+                     redraw them in parallel.
+  qwen3_4b_tick.npz -- (``make_golden.py qwen3_4b_tick``) BASELINE config 3's model
+                     (Qwen3-4B shape, seed-0 bf16) and tick shape on the reference's
+                     packed CPU path: 8 prefilled decode rows plus a 2048-token chunk,
+                     then 64 greedy steps.
   attention.npz   -- ``PackedBatchCache.attend`` (CPU branch) output for seeded bf16
                      inputs over decode, drafted and chunked-prefill rows.
   sampler.npz     -- kept token sets of ``Decoder._sample`` (captured from the
@@ -58,7 +65,7 @@ from helios.runtime.qwen3.paged_cache import (  # noqa: E402
 )
 from helios.runtime.types import Sampling  # noqa: E402
 
-from oracle.model import OracleConfig, build_state_dict  # noqa: E402
+from oracle.model import OracleConfig, build_state_dict, rng_checkpoints  # noqa: E402
 from tests.golden.inputs import attention_inputs, digest  # noqa: E402
 
 torch.set_num_threads(max(1, os.cpu_count() or 1))
@@ -266,6 +273,85 @@ def bf16_tick() -> dict:
     }
 
 
+def qwen3_4b_tick(steps: int = 64, rows: int = 8) -> dict:
+    """BASELINE config 3's model and tick shape on the reference's packed CPU path.
+
+    Qwen3-4B architecture (36 layers, hidden 2560, 32/8 heads, d=128, inter 9728, vocab
+    151936, tied), random-init bf16 from seed 0. ``rows`` decode rows whose prompts
+    (contexts U[1024, 4096], seed 3) are prefilled through the reference's own paged
+    path, then one packed tick of those rows' pending tokens plus a fresh 2048-token
+    prefill chunk at offset 0, then ``steps - 1`` greedy decode ticks of all rows.
+    Recorded: the tick's logits at every 37th vocabulary column, and per step and row
+    the greedy id, the winning logit and the runner-up logit (so a test can tell a
+    decided step from a near tie)."""
+    import time
+
+    cfg = Qwen3Config()
+    started = time.time()
+    torch.manual_seed(0)
+    model = Qwen3Model(cfg).eval()
+    print(f"init {time.time() - started:.1f} s", flush=True)
+    g = torch.Generator().manual_seed(3)
+    contexts = torch.randint(1024, 4097, (rows,), generator=g).tolist()
+    prompts = [rand_ids(g, c, cfg.vocab_size) for c in contexts]
+    pending = rand_ids(g, rows, cfg.vocab_size)
+    chunk = rand_ids(g, 2048, cfg.vocab_size)
+    pages = sum(-(-(c + steps + 1) // 256) for c in contexts) + -(-(2048 + steps) // 256) + 4
+    pool = KVPagePool(cfg, pages, device=torch.device("cpu"))
+    decoder = Decoder(model)
+    decoder.page_pool = pool
+    columns = np.arange(0, cfg.vocab_size, 37)
+    with torch.inference_mode():
+        caches = []
+        for prompt in prompts:
+            pc = PagedKVCache(pool, len(prompt) + 1 + steps)
+            decoder.packed_caches([pc], [prompt])
+            caches.append(pc)
+            print(f"prefilled {len(prompt)} at {time.time() - started:.1f} s", flush=True)
+        caches.append(PagedKVCache(pool, 2048 + steps))
+        logits = decoder.packed_caches(caches, [[t] for t in pending] + [chunk]).float()
+        print(f"tick at {time.time() - started:.1f} s", flush=True)
+        tick_logits = logits[:, torch.as_tensor(columns)].numpy()
+        ids, best, second = [], [], []
+
+        def record(out):
+            top = out.topk(2, dim=-1)
+            ids.append(out.argmax(-1).tolist())
+            best.append(top.values[:, 0].tolist())
+            second.append(top.values[:, 1].tolist())
+
+        record(logits)
+        for step in range(steps - 1):
+            record(decoder.packed_caches(caches, [[t] for t in ids[-1]]).float())
+            if step % 8 == 7:
+                print(f"step {step + 2} at {time.time() - started:.1f} s", flush=True)
+    return {
+        "prompt_lengths": np.array(contexts), "prompts": np.concatenate([np.array(p) for p in prompts]).astype(np.int32),
+        "pending": np.array(pending, dtype=np.int32), "chunk": np.array(chunk, dtype=np.int32),
+        "columns": columns.astype(np.int32), "tick_logits": tick_logits.astype(np.float32),
+        "greedy": np.array(ids, dtype=np.int32).T, "greedy_max": np.array(best, dtype=np.float32).T,
+        "greedy_second": np.array(second, dtype=np.float32).T,
+        "page_counts": np.array([len(c.pages) for c in caches]),
+    }
+
+
+def qwen3_4b_init() -> dict:
+    """The reference's seed-0 Qwen3-4B weights, as SHA-256 digests per tensor, and the CPU
+    generator's state before the embedding and before each block, so a test can redraw the
+    weights on many threads (``oracle.model.build_state_dict(rng_checkpoints=...)``) in
+    seconds and prove them bit-identical to the reference's serial initialisation."""
+    import hashlib
+
+    cfg = Qwen3Config()
+    torch.manual_seed(0)
+    sd = Qwen3Model(cfg).state_dict()
+    names = [k for k in sd if k not in ("cos", "sin")]
+    digests = [hashlib.sha256(sd[k].contiguous().view(torch.uint8).numpy().tobytes()).hexdigest() for k in names]
+    ocfg = OracleConfig(**{k: getattr(cfg, k) for k in OracleConfig.__dataclass_fields__})
+    states = torch.stack(rng_checkpoints(ocfg, 0)).numpy()
+    return {"names": np.array(names), "sha256": np.array(digests), "rng_states": states}
+
+
 def attention_case() -> dict:
     """``PackedBatchCache.attend`` CPU branch on seeded bf16 inputs (group 4, d=128)."""
     cfg = Qwen3Config(vocab_size=64, context_length=4096, hidden_size=64, n_heads=4, n_layers=1,
@@ -336,6 +422,14 @@ def sampler_cases() -> dict:
 
 
 def main() -> None:
+    if sys.argv[1:] == ["qwen3_4b_tick"]:
+        # Minutes of CPU work (the reference's bf16 forward of ~22k prompt tokens at the
+        # Qwen3-4B shape), so it is written on request only.
+        np.savez_compressed(HERE / "qwen3_4b_tick.npz", **qwen3_4b_tick())
+        return
+    if sys.argv[1:] == ["qwen3_4b_init"]:
+        np.savez_compressed(HERE / "qwen3_4b_init.npz", **qwen3_4b_init())
+        return
     (HERE / "metadata.json").write_text(json.dumps(metadata_cases()))
     np.savez_compressed(HERE / "config1.npz", **config1())
     np.savez_compressed(HERE / "bf16_tick.npz", **bf16_tick())

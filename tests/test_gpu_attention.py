@@ -259,3 +259,25 @@ def test_rows_sharing_a_prefix_match_the_oracle(tails, prefix_pages, extra):
                                batch.cu_seq_q.cpu().tolist(), batch.seqused_k.cpu().tolist())
     assert torch.isfinite(out.float()).all()
     torch.testing.assert_close(out.float(), expected.float(), rtol=2e-2, atol=2e-2)
+
+
+def test_config2_exact_inputs_match_oracle():
+    """BASELINE config 2 exactly as the bench times it (helios_b200.workloads.config2_batch:
+    seed 1, 64 rows x 1 query, contexts U[512, 8192], pages from a permutation of a
+    4096-page pool) against the fp32 oracle, row by row."""
+    from helios_b200.workloads import config2_batch
+
+    pool, batch, q, contexts = config2_batch(DEV)
+    out = torch.empty_like(q)
+    with torch.inference_mode():
+        ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out)
+    torch.cuda.synchronize()
+    assert batch.seqused_k.tolist() == contexts
+    want = paged_attention(q.cpu(), pool.keys[0].cpu(), pool.values[0].cpu(), batch.block_table.cpu().tolist(),
+                           batch.cu_seq_q.cpu().tolist(), contexts)
+    got = out.cpu().float()
+    err = (got - want.float()).abs()
+    print(f"config 2 decode attention vs oracle: max abs {err.max().item():.3e}, "
+          f"max |out| {want.float().abs().max().item():.3e}")
+    torch.testing.assert_close(got, want.float(), rtol=1e-2, atol=1e-4)
+    assert _native.device_status() == 0

@@ -5,8 +5,8 @@ mixed tick (decode rows, a drafted row, a continued chunk and a fresh prefill)
 at the Qwen3-4B head shape, and its greedy continuation for 64 steps. The B200
 model loads the reference's seed-0 random-init weights (rebuilt by the oracle,
 whose weight construction the CPU suite pins against the reference), replays
-the same prompts through paged prefill ticks, and must give logits within
-2e-2 of each row's logit scale and identical greedy ids.
+the same prompts through paged prefill ticks, and must give logits within 2 bf16
+ulps of each row's largest logit and identical greedy ids.
 """
 
 import numpy as np
@@ -24,6 +24,11 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda")
 SHAPE = dict(vocab_size=4096, context_length=4096, hidden_size=512, n_heads=8, n_layers=2, hidden_dim=1024,
              head_dim=128, n_kv_heads=2, rope_base=1e6, rms_norm_eps=1e-6, dtype=torch.bfloat16)
+
+
+def _ulp(x: torch.Tensor) -> torch.Tensor:
+    """bf16 spacing (8 significand bits) at magnitude ``x``."""
+    return torch.exp2(torch.floor(torch.log2(x.clamp(min=torch.finfo(torch.float32).tiny))) - 7)
 
 
 def _split(flat, lengths):
@@ -67,7 +72,9 @@ def test_mixed_tick_logits_and_greedy_match_reference(golden_dir):
     logits = decoder.packed_caches(caches, chunks, logit_counts=logit_counts).float().cpu()
     ref = torch.from_numpy(g["logits"])
     diff = (logits - ref).abs().max(-1).values
-    assert (diff <= 2e-2 * ref.abs().max(-1).values).all(), diff
+    ulp = _ulp(ref.abs().max(-1).values)
+    print(f"bf16 tick logits vs reference: max {float((diff / ulp).max()):.3f} ulp of the row max")
+    assert (diff <= 2 * ulp).all(), diff / ulp
     last = np.cumsum(logit_counts) - 1
     heads = logits[torch.as_tensor(last)]
     greedy, maxima = [heads.argmax(-1).tolist()], [heads.max(-1).values.tolist()]
@@ -76,9 +83,11 @@ def test_mixed_tick_logits_and_greedy_match_reference(golden_dir):
         greedy.append(out.argmax(-1).tolist())
         maxima.append(out.max(-1).values.tolist())
     assert (np.array(greedy).T == g["greedy"]).all()
-    # The winning logit of every row at every step tracks the reference's.
-    want = g["greedy_max"]
-    assert (np.abs(np.array(maxima).T - want) <= 2e-2 * np.abs(want).clip(min=1.0)).all()
+    # The winning logit of every row at every step tracks the reference's, within 2 ulps.
+    want = torch.from_numpy(g["greedy_max"])
+    err = (torch.tensor(maxima).T - want).abs() / _ulp(want.abs())
+    print(f"winning logits over {steps} steps: max {float(err.max()):.3f} ulp")
+    assert (err <= 2).all()
     assert [p.index for c in caches for p in c.pages] == g["page_tables"].tolist()
     assert _native.device_status() == 0
 

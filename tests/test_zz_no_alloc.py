@@ -4,9 +4,15 @@
 memory (a host that has handed the whole GPU to its own pool, or a latency-bound
 caller that must not pay for cudaMalloc's synchronisation): its split-K partials
 live in a fixed array inside the library. Through the C ABI it must give the same
-output as ``hb_paged_attention`` with a caller workspace, call after call, even
-though every call reuses the array the previous call left behind; and it must
-refuse work whose partials do not fit the array.
+output as ``hb_paged_attention`` with a caller workspace, bit for bit (both run the
+same kernels on the same work split), call after call, even though every call
+reuses the array the previous call left behind; it must leave the device's memory
+use unchanged; and it must refuse work whose partials do not fit the array.
+
+Three launch shapes use the array differently and each is covered: decode rows
+beside a prefill row (the persistent decode grid and its work ticket), the same
+work with the decode/prefill overlap switched off (one decode CTA per unit), and a
+decode-only tick whose long rows split (per-unit decode grid plus the combine).
 
 This file is collected last, so a run that stops at the first failure has
 already run every other test.
@@ -25,6 +31,7 @@ from tests.helpers import attn_config, cache_with_pages
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda")
 LIMIT_BYTES = 8 << 20  # HB_STATIC_WORKSPACE_BYTES
+DEFAULT_OVERLAP_SMS = 100
 
 
 def _static_attention(q, key_pool, value_pool, batch, out):
@@ -39,11 +46,14 @@ def _static_attention(q, key_pool, value_pool, batch, out):
         out.data_ptr(), torch.cuda.current_stream().cuda_stream)
 
 
-def _batch(seed):
-    """Decode rows long enough to split (so the workspace carries partials) plus a prefill row."""
+def _batch(seed, *, prefill=True):
+    """Decode rows long enough to split (so the workspace carries partials), with or
+    without a prefill row."""
     g = torch.Generator().manual_seed(seed)
-    lengths = torch.randint(2000, 9000, (40,), generator=g).tolist() + [0]
-    counts = [1] * 36 + [3, 5, 8, 16] + [200]
+    lengths = torch.randint(2000, 9000, (40,), generator=g).tolist()
+    counts = [1] * 36 + [3, 5, 8, 16]
+    if prefill:
+        lengths, counts = lengths + [0], counts + [200]
     pages = sum(math.ceil((l + c) / 256) for l, c in zip(lengths, counts)) + 4
     pool = KVPagePool(attn_config(heads=32, kv_heads=8), pages, device=DEV)
     pool.storage.normal_(0.0, 0.3)
@@ -58,22 +68,55 @@ def _batch(seed):
     return pool, batch, sum(counts)
 
 
-def test_static_workspace_matches_caller_workspace_on_consecutive_calls():
-    pool, batch, tokens = _batch(0)
+def _memory():
+    torch.cuda.synchronize()
+    return torch.cuda.mem_get_info()[0], torch.cuda.memory_stats().get("allocation.all.allocated", 0)
+
+
+def _check_two_calls(pool, batch, tokens, seed):
     assert batch.partial_records > 0 and batch.num_decode_items > 40  # split rows use the workspace
     need = ops.workspace_bytes(batch.partial_records, 32, 128)
     assert 0 < need <= LIMIT_BYTES
-    g = torch.Generator(device=DEV).manual_seed(1)
-    for _ in range(2):  # the second call reuses what the first left in the array
-        q = torch.randn(tokens, 32, 128, device=DEV, generator=g).to(torch.bfloat16)
-        want = torch.empty_like(q)
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    qs = [torch.randn(tokens, 32, 128, device=DEV, generator=g).to(torch.bfloat16) for _ in range(2)]
+    wants = [torch.empty_like(q) for q in qs]
+    gots = [torch.full_like(q, float("nan")) for q in qs]
+    for q, want in zip(qs, wants):
         ops.paged_attention(q, pool.keys[0], pool.values[0], batch, want)
-        got = torch.full_like(q, float("nan"))
+    # One call first, so that everything the library loads lazily is loaded before measuring.
+    _native.check(_static_attention(qs[0], pool.keys[0], pool.values[0], batch, gots[0]),
+                  "hb_paged_attention_static_workspace")
+    before = _memory()
+    for q, got in zip(qs, gots):  # the second call reuses what the first left in the array
+        got.fill_(float("nan"))
         _native.check(_static_attention(q, pool.keys[0], pool.values[0], batch, got),
                       "hb_paged_attention_static_workspace")
-        torch.cuda.synchronize()
-        torch.testing.assert_close(got.float(), want.float(), rtol=2e-2, atol=2e-2)
+    after = _memory()
+    assert after == before, (before, after)
+    for got, want in zip(gots, wants):
+        assert torch.equal(got, want)
     assert _native.device_status() == 0
+
+
+def test_static_workspace_matches_caller_workspace_beside_prefill():
+    pool, batch, tokens = _batch(0)
+    assert batch.num_prefill_items > 0
+    _check_two_calls(pool, batch, tokens, 1)
+
+
+def test_static_workspace_matches_caller_workspace_without_overlap():
+    pool, batch, tokens = _batch(3)
+    _native.check(_native.load().hb_attention_set_overlap(0), "hb_attention_set_overlap")
+    try:
+        _check_two_calls(pool, batch, tokens, 4)
+    finally:
+        _native.check(_native.load().hb_attention_set_overlap(DEFAULT_OVERLAP_SMS), "hb_attention_set_overlap")
+
+
+def test_static_workspace_matches_caller_workspace_decode_only():
+    pool, batch, tokens = _batch(5, prefill=False)
+    assert batch.num_prefill_items == 0
+    _check_two_calls(pool, batch, tokens, 6)
 
 
 def test_static_workspace_rejects_partials_beyond_its_size():
