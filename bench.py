@@ -19,14 +19,22 @@ step; the device half replays from a CUDA graph captured during warm-up
   roofline  the split-K decode attention kernel at BASELINE config 2 (64 rows,
           contexts U[512, 8192], 32/8 heads, d=128, 4096-page pool), HBM-bound:
           algorithmic bytes / CUDA-event time against the measured copy peak.
-  cpu_baseline  the oracle's CPU restatement of the same tick (the reference's
-          algorithm, PyTorch on the host cores), timed on a bounded sample of
-          decoder layers and scaled to 36 (rank 0, N=1 only).
+  cpu_baseline  the same tick on the reference's own packed CPU path, imported
+          unchanged from baseline/_ref (else the oracle's CPU restatement), timed on a
+          bounded sample of decoder layers and scaled to 36 (rank 0, N=1 only).
+  per_rank  each replica's own ms per tick and median SM clock (N>1: what limits scaling).
+  config4  BASELINE config 4 end to end (helios_b200.workloads.config4): restore cost of
+          128 prefix-hit requests, their tail prefill, 128 sampled decode steps.
+  config5  BASELINE config 5 at 64 req/s per GPU, 256 requests per GPU, on the reference's
+          Engine over this path, all replicas (helios_b200.load): tokens/s and p50 TTFT.
+  reference_gpu_dense  the reference's own GPU path for the same tick (its dense-KV CUDA
+          path, imported unchanged; its paged varlen_attn path needs torch >= 2.13).
 
 Multi-GPU: one process per GPU (torchrun), independent replicas, no collective
 on the data path; the process group only aligns the ranks and takes max time.
-``--impl reference`` times the CPU oracle of the same tick on rank 0 (other
-ranks exit) and prints the same metric with ``"impl": "reference"``.
+``--impl reference`` times the reference's own packed CPU path (imported unchanged; the
+oracle's restatement when the reference is absent) on the host cores, rank 0 only (other
+ranks exit), and prints the same metric with ``"impl": "reference"``.
 """
 
 from __future__ import annotations
@@ -56,6 +64,8 @@ CONTEXT = (1024, 4096)
 TOKENS_PER_STEP = DECODE_ROWS + PREFILL
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 DATA = "synthetic: random-init weights, uniform token ids, random K/V standing in for the decode rows' prefill"
+CONFIG5_RATE = 64.0            # requests/s per GPU for the bench's config-5 point
+CONFIG5_REQUESTS_PER_GPU = 256
 
 
 def peaks() -> tuple[dict, str]:
@@ -109,6 +119,11 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
         return False
+
+    def summary_cached(self) -> dict:
+        if not hasattr(self, "_summary"):
+            self._summary = self.summary()
+        return self._summary
 
     def summary(self) -> dict:
         if self.proc is None or self.file is None:
@@ -336,6 +351,166 @@ def decode_attention_roofline(device: torch.device, peak_gbs: float, iters: int 
     return info
 
 
+# ------------------------------------------------------------------------- the reference's own code
+def reference_package():
+    """``helios_b200.reference_engine`` with the reference importable (baseline/_ref or
+    HELIOS_REFERENCE_SRC), else None."""
+    try:
+        from helios_b200 import reference_engine
+
+        reference_engine.import_reference()
+        return reference_engine
+    except Exception:  # noqa: BLE001 - any import failure means the reference is absent
+        return None
+
+
+def _tile_fill(t: torch.Tensor, gen: torch.Generator, scale: float) -> None:
+    """Fill ``t`` with a tiled block of N(0, scale) values (finite, no denormals): timing
+    inputs only, far cheaper than the reference's serial initialisation on the CPU."""
+    block = (torch.randn(1 << 16, generator=gen) * scale).to(t.dtype)
+    flat = t.view(-1)
+    reps = -(-flat.numel() // block.numel())
+    flat.copy_(block.repeat(reps)[:flat.numel()])
+
+
+class ReferenceCpuTick:
+    """BASELINE config 3's tick on the reference's own packed CPU path, imported unchanged
+    (``Decoder.packed_caches`` -> ``PackedBatchCache.prepare_packed`` -> ``Qwen3Model._forward_packed``
+    with the CPU branch of ``PackedBatchCache.attend``, src/helios/runtime/qwen3/decode.py:260-291,
+    paged_cache.py:418-546), on ``layers`` decoder layers of the Qwen3-4B shape. Forward hooks
+    time each decoder layer, so a step's time scales to 36 layers as
+    (whole step - its layers) + 36 x (mean layer time)."""
+
+    def __init__(self, layers: int, seed: int = 0, threads: int | None = None, steps: int = 64) -> None:
+        if reference_package() is None:
+            raise RuntimeError("the reference package is not importable")
+        from helios.runtime.qwen3.config import Qwen3Config as RefConfig
+        from helios.runtime.qwen3.decode import Decoder as RefDecoder
+        from helios.runtime.qwen3.layers import rope_parameters as ref_rope
+        from helios.runtime.qwen3.model import Qwen3Model as RefModel
+        from helios.runtime.qwen3.paged_cache import KVPagePool as RefPool
+        from helios.runtime.qwen3.paged_cache import PagedKVCache as RefCache
+
+        self.threads = threads or os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        self.layers = layers
+        cfg = RefConfig(n_layers=layers)
+        with torch.device("meta"):
+            model = RefModel(cfg)
+        model = model.to_empty(device="cpu")
+        model.output.weight = model.token_embedding.weight
+        gen = torch.Generator().manual_seed(seed)
+        with torch.no_grad():
+            for name, param in model.named_parameters():
+                if name.endswith("scale"):
+                    param.fill_(1.0)
+                else:
+                    _tile_fill(param, gen, 0.02 if "embedding" not in name else 1.0)
+            cos, sin = ref_rope(cfg)
+            model.cos.copy_(cos)
+            model.sin.copy_(sin)
+        self.model = model.eval()
+        g = torch.Generator().manual_seed(seed)
+        contexts = torch.randint(CONTEXT[0], CONTEXT[1] + 1, (DECODE_ROWS,), generator=g).tolist()
+        pages = sum(math.ceil((c + steps + 1) / 256) for c in contexts) + math.ceil((PREFILL + 8) / 256) + 2
+        self.pool = RefPool(cfg, pages, device=torch.device("cpu"))
+        for layer in range(layers):
+            _tile_fill(self.pool.keys[layer], gen, 0.3)
+            _tile_fill(self.pool.values[layer], gen, 0.3)
+        self.caches = []
+        for ctx in contexts:
+            cache = RefCache(self.pool, ctx + steps + 1)
+            cache.pages.extend(self.pool.acquire(math.ceil((ctx - 1) / 256)))
+            cache.length = ctx - 1
+            self.caches.append(cache)
+        self.decoder = RefDecoder(self.model)
+        self.decoder.page_pool = self.pool
+        self.cache_cls = RefCache
+        self.pending = torch.randint(0, cfg.vocab_size, (DECODE_ROWS,), generator=g).tolist()
+        self.chunk = torch.randint(0, cfg.vocab_size, (PREFILL,), generator=g).tolist()
+        self._block_seconds = 0.0
+        self._started = 0.0
+
+        def pre(module, args):
+            self._started = time.perf_counter()
+
+        def post(module, args, output):
+            self._block_seconds += time.perf_counter() - self._started
+
+        for block in self.model.blocks:
+            block.register_forward_pre_hook(pre)
+            block.register_forward_hook(post)
+
+    def step(self) -> float:
+        """One tick; returns its time scaled to 36 decoder layers."""
+        prefill = self.cache_cls(self.pool, PREFILL + 8)
+        self._block_seconds = 0.0
+        started = time.perf_counter()
+        logits = self.decoder.packed_caches(self.caches + [prefill], [[t] for t in self.pending] + [self.chunk])
+        ids = logits.float().argmax(-1).tolist()
+        total = time.perf_counter() - started
+        prefill.close()
+        self.pending = ids[:DECODE_ROWS]
+        layer = self._block_seconds / self.layers
+        return total - self._block_seconds + 36 * layer
+
+
+def reference_gpu_dense(device: torch.device, steps: int, warmup: int = 3, seed: int = 0) -> dict:
+    """The reference's own GPU path for BASELINE config 3's tick, imported unchanged: its
+    paged ``varlen_attn`` path needs torch >= 2.13 (``block_table``), absent from this image,
+    so the comparator is its dense-KV CUDA path (what its decoder runs without a page pool):
+    ``Decoder.decode_caches`` over 32 dense caches (``_decode_dense``: one batched decode
+    forward, src/helios/runtime/qwen3/decode.py:293-320) plus one 2048-token prefill through
+    ``Decoder._forward_cache`` (SDPA, layers.py:169-191), greedy ids read back each step,
+    eager as the reference runs. Random-init Qwen3-4B weights; random K/V in the decode rows'
+    contexts. CUDA events around ``steps`` ticks."""
+    if reference_package() is None:
+        raise RuntimeError("the reference package is not importable")
+    from helios.runtime.qwen3.cache import KVCache
+    from helios.runtime.qwen3.config import Qwen3Config as RefConfig
+    from helios.runtime.qwen3.decode import Decoder as RefDecoder
+    from helios.runtime.qwen3.model import Qwen3Model as RefModel
+
+    cfg = RefConfig()
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = RefModel(cfg).eval()
+    decoder = RefDecoder(model)
+    g = torch.Generator().manual_seed(seed)
+    contexts = torch.randint(CONTEXT[0], CONTEXT[1] + 1, (DECODE_ROWS,), generator=g).tolist()
+    total = warmup + steps + 1
+    gen = torch.Generator(device=device).manual_seed(seed)
+    caches = []
+    for ctx in contexts:
+        cache = KVCache(cfg, ctx + total, device=device)
+        for layer in cache._layers:
+            layer.keys[:, :, :ctx - 1].normal_(0.0, 0.3, generator=gen)
+            layer.values[:, :, :ctx - 1].normal_(0.0, 0.3, generator=gen)
+        cache.length = ctx - 1
+        caches.append(cache)
+    pending = torch.randint(0, cfg.vocab_size, (DECODE_ROWS,), generator=g).tolist()
+    chunk = torch.randint(0, cfg.vocab_size, (1, PREFILL), generator=g).to(device)
+
+    def tick():
+        nonlocal pending
+        with torch.inference_mode():
+            decode_logits = decoder.decode_caches(caches, pending)
+            prefill_logits = decoder._forward_cache(chunk, KVCache(cfg, PREFILL + 8, device=device))[:, -1, :]
+            ids = torch.cat([decode_logits.argmax(-1), prefill_logits.argmax(-1)]).tolist()
+        pending = ids[:DECODE_ROWS]
+
+    for _ in range(warmup):
+        tick()
+    seconds = time_steps(tick, steps, device)
+    del caches, model, decoder
+    torch.cuda.empty_cache()
+    return {"value": round(TOKENS_PER_STEP * steps / seconds, 1), "unit": UNIT,
+            "ms_per_step": round(1e3 * seconds / steps, 3), "steps": steps,
+            "path": "the reference's dense-KV CUDA path imported unchanged (Decoder.decode_caches -> _decode_dense "
+                    "for the 32 decode rows + Decoder._forward_cache SDPA prefill of the 2048-token chunk), eager; "
+                    "its varlen_attn paged path needs torch >= 2.13 and is not in this image"}
+
+
 # ------------------------------------------------------------------------- CPU (oracle) tick
 def cpu_tick_sample(layers: int, seed: int = 0, threads: int | None = None) -> dict:
     """The oracle's dense CPU restatement of the same tick on ``layers`` decoder layers.
@@ -386,6 +561,21 @@ def cpu_tokens_per_s(sample: dict, layers_total: int = 36) -> float:
 
 
 def cpu_baseline() -> dict:
+    if reference_package() is not None:
+        first = ReferenceCpuTick(1)
+        first.step()
+        one = first.step()
+        layer_s = first._block_seconds
+        # Grow the sample toward ~10 s of CPU work, capped at 4 layers.
+        layers = int(max(1, min(4, 10.0 // max(layer_s, 1e-3))))
+        tick = ReferenceCpuTick(layers) if layers > 1 else first
+        if layers > 1:
+            tick.step()
+        seconds = statistics.mean(tick.step() for _ in range(2)) if layers > 1 else one
+        return {"value": round(TOKENS_PER_STEP / seconds, 2), "unit": UNIT, "cores": tick.threads,
+                "kind": "reference",
+                "sample": f"the reference's own packed CPU path imported unchanged (bf16), {layers} of 36 decoder "
+                          f"layers of the full 2080-token tick timed by forward hooks and scaled to 36 layers"}
     first = cpu_tick_sample(1)
     # Grow the sample toward ~10 s of CPU work, capped at 4 layers.
     layers = int(max(1, min(4, 10.0 // max(first["layer_seconds"], 1e-3))))
@@ -411,21 +601,34 @@ def run_reference(args) -> None:
     rank, _, _ = replicas.world()
     if rank != 0:
         return
-    for _ in range(args.warmup):
-        cpu_tick_sample(1)
-    times, sample = [], None
-    for _ in range(args.steps):
-        sample = cpu_tick_sample(1)
-        times.append(TOKENS_PER_STEP / cpu_tokens_per_s(sample))
+    times = []
+    if reference_package() is not None:
+        tick = ReferenceCpuTick(1, steps=args.warmup + args.steps + 1)
+        for _ in range(args.warmup):
+            tick.step()
+        times = [tick.step() for _ in range(args.steps)]
+        kind, cores = "reference", tick.threads
+        sample_text = ("each step: the full 2080-token tick through the reference's own packed CPU path "
+                       "(imported unchanged, bf16) with 1 of 36 decoder layers, scaled to 36 layers by its "
+                       "measured layer time")
+    else:
+        for _ in range(args.warmup):
+            cpu_tick_sample(1)
+        sample = None
+        for _ in range(args.steps):
+            sample = cpu_tick_sample(1)
+            times.append(TOKENS_PER_STEP / cpu_tokens_per_s(sample))
+        kind, cores = "port", sample["threads"]
+        sample_text = ("each step: 1 of 36 decoder layers of the full tick (+ embedding and logit rows), scaled to "
+                       "36 layers; the oracle's CPU restatement of the reference algorithm (reference not importable)")
     value = TOKENS_PER_STEP / statistics.mean(times)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * statistics.mean(times), 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": DATA,
         "config": workload_config(args.gpus),
-        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": sample["threads"], "kind": "port",
-                         "sample": "each step: 1 of 36 decoder layers of the full tick (+ embedding and logit rows), "
-                                   "scaled to 36 layers; the oracle's CPU restatement of the reference algorithm"},
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": cores, "kind": kind,
+                         "sample": sample_text},
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -448,6 +651,7 @@ def run_b200(args) -> None:
         clocks.mark_start()
         seconds = time_steps(runner.device_step, args.steps, device)
         clocks.mark_end()
+    seconds_local = seconds
     seconds = replicas.max_over_ranks(seconds, device)
     value = size * TOKENS_PER_STEP * args.steps / seconds
     # End to end through the public API, host token lists in, sampled ids out.
@@ -456,14 +660,20 @@ def run_b200(args) -> None:
     e2e_seconds = replicas.max_over_ranks(time_steps(runner.api_step, args.steps, device), device)
     e2e_value = size * TOKENS_PER_STEP * args.steps / e2e_seconds
     h2d, d2h, launches = runner.h2d_bytes, runner.d2h_bytes, runner.launches
+    own_ms = 1e3 * seconds_local / args.steps
     pk, pk_kind = peaks()
     flops = 2 * 3.633e9 * TOKENS_PER_STEP  # dense projections + MLP, all layers
     del runner, model, decoder, pool, caches
     torch.cuda.empty_cache()
+    per_rank = replicas.gather_objects({"rank": rank, "ms_per_step": round(own_ms, 3),
+                                        "sm_mhz": clocks.summary_cached().get("sm_mhz")}, device)
     roof = decode_attention_roofline(device, pk["hbm_gbs"]) if rank == 0 else None
     prefill_roof = prefill_attention_roofline(device, pk["bf16_tflops"]) if rank == 0 else None
     if roof is not None:
         roof["peak_kind"] = prefill_roof["peak_kind"] = pk_kind
+    extras = {}
+    if not args.no_extras:
+        extras = run_extras(args, device, rank, size)
     cpu = cpu_baseline() if (rank == 0 and size == 1 and not args.no_cpu) else None
     if rank == 0:
         step_s = seconds / args.steps
@@ -478,14 +688,50 @@ def run_b200(args) -> None:
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(1000 * e2e_seconds / args.steps, 3)},
             "gpu_launches": args.steps * launches,
-            "clocks": clocks.summary(),
+            "clocks": clocks.summary_cached(),
+            "per_rank": per_rank,
             "tick_tensor_roofline": {"bound": "tensor", "flops_per_step": flops,
                                      "achieved_tflops": round(flops / step_s / 1e12, 1),
                                      "peak_tflops": pk["bf16_tflops_sustained"], "peak_kind": pk_kind,
                                      "frac": round(flops / step_s / 1e12 / pk["bf16_tflops_sustained"], 4)},
+            **extras,
         }
         print(json.dumps(line), flush=True)
     replicas.shutdown()
+
+
+def run_extras(args, device: torch.device, rank: int, size: int) -> dict:
+    """The other BASELINE configs and the reference's own GPU path, each under its own key.
+    Every rank takes the same collective steps (config 5 runs on all replicas)."""
+    out = {}
+    from helios_b200 import replicas
+
+    if rank == 0:
+        from helios_b200.workloads import config4
+
+        try:
+            out["config4"] = config4(steps=128, device=device)
+        except Exception as error:  # noqa: BLE001 - reported in the line, the headline stands
+            out["config4"] = {"error": f"{type(error).__name__}: {error}"}
+        torch.cuda.empty_cache()
+    replicas.barrier(device)
+    if reference_package() is not None:
+        from helios_b200 import load
+
+        point = load.measure(CONFIG5_RATE, CONFIG5_REQUESTS_PER_GPU * size, device=device)
+        if rank == 0:
+            point["workload"] = (f"BASELINE config 5 at {CONFIG5_RATE:g} req/s per GPU, "
+                                 f"{CONFIG5_REQUESTS_PER_GPU} requests per GPU (the full sweep: "
+                                 "python -m helios_b200.load)")
+            out["config5"] = point
+        torch.cuda.empty_cache()
+        if rank == 0:
+            out["reference_gpu_dense"] = reference_gpu_dense(device, steps=min(args.steps, 8))
+    elif rank == 0:
+        out["config5"] = out["reference_gpu_dense"] = {"unavailable": "the reference package is not importable "
+                                                                      "(baseline/_ref or HELIOS_REFERENCE_SRC)"}
+    replicas.barrier(device)
+    return out
 
 
 def main() -> None:
@@ -495,6 +741,8 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     parser.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    parser.add_argument("--no-extras", action="store_true",
+                        help="skip configs 4 and 5 and the reference's GPU path (headline tick only)")
     parser.add_argument("--decode-sms", type=int, default=None,
                         help="SMs the decode attention grid keeps beside prefill work (0: all; default: the library's)")
     args = parser.parse_args()

@@ -62,6 +62,17 @@ def sum_over_ranks(value: float, device: torch.device | None = None) -> float:
     return float(t.item())
 
 
+def gather_objects(value, device: torch.device | None = None) -> list:
+    """Every rank's ``value`` (picklable host data: per-replica results such as token counts
+    and time-to-first-token samples), in rank order, on every rank. Measurement plumbing on
+    the host, not a data-path exchange."""
+    if not (dist.is_available() and dist.is_initialized()):
+        return [value]
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, value)
+    return out
+
+
 def shutdown() -> None:
     if dist.is_available() and dist.is_initialized():
         dist.destroy_process_group()

@@ -1,15 +1,24 @@
 """Model-level workloads beyond the bench's mixed tick.
 
-    python -m helios_b200.workloads config4 [--ticks N] [--no-share]
+    python -m helios_b200.workloads config4 [--steps N] [--no-share]
+    python -m helios_b200.workloads config4-decode [--ticks N] [--no-share]
 
-``config4``: BASELINE config 4's decode phase on the Qwen3-4B architecture (random init,
-bf16). 128 requests share a 4096-token prefix (16 pages stored once and restored into every
-request by page aliasing), each with its own tail of U[256, 1024] tokens. Random K/V stand in
-for the prefix and tail prefill. Every tick decodes one token per request through
-``Decoder.decode_caches`` (CUDA-graph replay of the device half), then samples them with
-temperature 0.2 and top-p 0.95 (kernel d). The timed ticks are bracketed by CUDA events.
-``--no-share`` switches off the shared-prefix grouping (every row reads the prefix pages
-itself) for comparison. Prints one JSON line.
+``config4``: BASELINE config 4 end to end on the Qwen3-4B architecture (random init, bf16,
+seed 3). One request prefills the common 4096-token prefix through packed ticks and its 16
+full pages are stored as prefix-cache blocks, keyed on the device (``DevicePrefixIndex``,
+the reference's SHA-256 block chain). Then 128 requests, each the prefix plus its own tail
+of U[256, 1024] tokens, are admitted: one device lookup finds each request's 16 stored
+blocks and ``restore_blocks`` aliases their pages (no K/V bytes move). The tails are
+prefilled through packed ticks of at most 2048 tokens (chunked, as the reference engine's
+budget does), and every request then decodes ``steps`` (128) tokens with temperature 0.2
+and top-p 0.95, one decode tick per step (CUDA-graph replay) sampled by kernel d, each
+step's ids read back to the host. Reports the restore cost (lookup + aliasing, and the
+bytes it uploads), the tail prefill time and the decode tokens/s, each timed with CUDA
+events.
+
+``config4-decode``: the decode phase alone with random K/V standing in for the prefix and
+tail prefill (the earlier measurement). ``--no-share`` switches off the shared-prefix
+grouping (every row reads the prefix pages itself) for comparison. Each prints one JSON line.
 """
 
 from __future__ import annotations
@@ -18,6 +27,7 @@ import argparse
 import json
 import math
 import sys
+import time
 
 import torch
 
@@ -60,7 +70,137 @@ def config2_batch(device: torch.device):
     return pool, batch, q, contexts
 
 
-def config4(ticks: int, share: bool, warmup: int = 3) -> dict:
+def _cuda_timer(device):
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    return start, end
+
+
+def config4(steps: int = 128, share: bool = True, device: torch.device | None = None, seed: int = 3,
+            warmup: int = 3) -> dict:
+    """BASELINE config 4 as specified (see the module docstring); returns its measurements."""
+    from helios_b200.prefix_index import DevicePrefixIndex
+
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    cfg = qwen3_4b_config()
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = Qwen3Model(cfg).eval()
+    model.enable_cuda_graphs()
+    decoder = Decoder(model)
+    g = torch.Generator().manual_seed(seed)
+    prefix = torch.randint(0, cfg.vocab_size, (PREFIX_TOKENS,), generator=g).tolist()
+    tails = torch.randint(TAIL[0], TAIL[1] + 1, (REQUESTS,), generator=g).tolist()
+    prompts = [prefix + torch.randint(0, cfg.vocab_size, (t,), generator=g).tolist() for t in tails]
+    prefix_pages = PREFIX_TOKENS // 256
+    total_steps = warmup + steps
+    pages = prefix_pages + 1 + sum(math.ceil((len(p) + total_steps + 1) / 256) - prefix_pages for p in prompts) + 8
+    pool = decoder.page_pool = KVPagePool(cfg, pages, device=device)
+    saved = paged_cache.MIN_SHARED_PAGES
+    if not share:
+        paged_cache.MIN_SHARED_PAGES = 1 << 30
+    try:
+        with torch.inference_mode():
+            # The first request: the prefix prefilled in 2048-token packed ticks, its full
+            # blocks stored and keyed on the device.
+            donor = PagedKVCache(pool, PREFIX_TOKENS + 1)
+            for at in range(0, PREFIX_TOKENS, 2048):
+                decoder.packed_caches([donor], [prefix[at:at + 2048]])
+            blocks = [donor.snapshot_block(b * 256, (b + 1) * 256) for b in range(prefix_pages)]
+            index = DevicePrefixIndex(4 * prefix_pages, 256, device)
+            from helios_b200.prefix_index import hash_token_blocks
+
+            keys = hash_token_blocks([prefix], 256, device)[0]
+            index.add(keys, list(range(prefix_pages)))
+            donor.close()
+            torch.cuda.synchronize(device)
+
+            # Admission: one device lookup for all 128 prompts, then aliasing restores.
+            start, end = _cuda_timer(device)
+            t0 = time.perf_counter()
+            start.record()
+            hits = index.lookup(prompts)
+            caches = []
+            for prompt, (_, values) in zip(prompts, hits):
+                cache = PagedKVCache(pool, len(prompt) + total_steps + 1)
+                cache.restore_blocks([blocks[v] for v in values])
+                caches.append(cache)
+            end.record()
+            torch.cuda.synchronize(device)
+            restore_wall = time.perf_counter() - t0
+            restore_gpu = start.elapsed_time(end) / 1e3
+            restored = [c.length for c in caches]
+
+            # Tails: packed ticks of at most 2048 prompt tokens, rows chunked across ticks.
+            offsets = list(restored)
+            ticks = 0
+            first_logits = {}
+            start, end = _cuda_timer(device)
+            start.record()
+            pending = list(range(REQUESTS))
+            while pending:
+                budget, rows, chunks = 2048, [], []
+                for r in list(pending):
+                    if budget == 0:
+                        break
+                    n = min(budget, len(prompts[r]) - offsets[r])
+                    rows.append(r)
+                    chunks.append(prompts[r][offsets[r]:offsets[r] + n])
+                    offsets[r] += n
+                    budget -= n
+                    if offsets[r] == len(prompts[r]):
+                        pending.remove(r)
+                logits = decoder.packed_caches([caches[r] for r in rows], chunks)
+                for i, r in enumerate(rows):
+                    if offsets[r] == len(prompts[r]):
+                        first_logits[r] = logits[i].clone()  # graph outputs are reused by later replays
+                ticks += 1
+            heads = torch.stack([first_logits[r] for r in range(REQUESTS)])
+            end.record()
+            torch.cuda.synchronize(device)
+            prefill_seconds = start.elapsed_time(end) / 1e3
+            tail_tokens = sum(len(p) for p in prompts) - sum(restored)
+
+            samplings = [Sampling(temperature=0.2, top_p=0.95, max_new_tokens=total_steps + 1)] * REQUESTS
+            sample_gen = torch.Generator(device=device).manual_seed(seed)
+            ids = sample_rows(heads, samplings, generator=sample_gen).tolist()
+
+            def tick(token_ids):
+                out = decoder.decode_caches(caches, token_ids)
+                return sample_rows(out, samplings, generator=sample_gen).tolist()
+
+            for _ in range(warmup):  # eager tick, graph capture, first replay
+                ids = tick(ids)
+            torch.cuda.synchronize(device)
+            start, end = _cuda_timer(device)
+            start.record()
+            for _ in range(steps):
+                ids = tick(ids)
+            end.record()
+            torch.cuda.synchronize(device)
+            decode_seconds = start.elapsed_time(end) / 1e3
+    finally:
+        paged_cache.MIN_SHARED_PAGES = saved
+    return {
+        "workload": "BASELINE config 4: 128 requests = shared 4096-token prefix (16 blocks, device-keyed) + own "
+                    "tail U[256,1024]; tails prefilled in packed ticks of <= 2048 tokens; 128 decode steps at "
+                    "T=0.2 top-p 0.95, seed 3",
+        "restore": {"blocks_per_request": prefix_pages, "restored_tokens_per_request": min(restored),
+                    "us_gpu": round(restore_gpu * 1e6, 1), "us_wall": round(restore_wall * 1e6, 1),
+                    "kv_bytes_moved": 0,
+                    "metadata_bytes": REQUESTS * prefix_pages * 4,
+                    "what": "one hb_hash_token_blocks + hb_prefix_index_lookup over the 128 prompts, then page "
+                            "aliasing; the restored page ids reach the device arena with the next tick's "
+                            "descriptor (4 bytes per page)"},
+        "tail_prefill": {"tokens": tail_tokens, "ticks": ticks, "seconds": round(prefill_seconds, 4),
+                         "tokens_per_s": round(tail_tokens / prefill_seconds, 1)},
+        "decode": {"steps": steps, "ms_per_step": round(1e3 * decode_seconds / steps, 3),
+                   "tokens_per_s": round(REQUESTS * steps / decode_seconds, 1),
+                   "timing": "CUDA events around the decode steps; each step's sampled ids read back to the host"},
+        "shared_prefix_grouping": share,
+    }
+
+
+def config4_decode(ticks: int, share: bool, warmup: int = 3) -> dict:
     device = torch.device("cuda", 0)
     cfg = qwen3_4b_config()
     torch.manual_seed(3)
@@ -124,13 +264,17 @@ def config4(ticks: int, share: bool, warmup: int = 3) -> dict:
 
 def main(argv: list[str]) -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("workload", choices=("config4",))
+    parser.add_argument("workload", choices=("config4", "config4-decode"))
     parser.add_argument("--ticks", type=int, default=16)
+    parser.add_argument("--steps", type=int, default=128)
     parser.add_argument("--no-share", action="store_true")
     args = parser.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("the workloads need a CUDA device")
-    print(json.dumps(config4(args.ticks, not args.no_share)), flush=True)
+    if args.workload == "config4":
+        print(json.dumps(config4(args.steps, not args.no_share)), flush=True)
+    else:
+        print(json.dumps(config4_decode(args.ticks, not args.no_share)), flush=True)
 
 
 if __name__ == "__main__":

@@ -212,3 +212,23 @@ def test_sampling_bounds_match_reference():
     for bad in (dict(max_new_tokens=0), dict(temperature=2.5), dict(top_p=0)):
         with pytest.raises(ValueError):
             Sampling(**bad)
+
+
+def test_config5_request_distributions():
+    """BASELINE config 5's load: lognormal prompts (median 600, sigma 0.8, clipped to
+    [16, 8192]), max_new_tokens U[64, 512], Poisson arrivals at the given rate."""
+    import numpy as np
+
+    from helios_b200 import load
+
+    reqs = load.make_requests(4000, 151936, seed=5)
+    lengths = np.array([len(p) for p, _ in reqs])
+    limits = np.array([m for _, m in reqs])
+    assert lengths.min() >= 16 and lengths.max() <= 8192
+    assert 560 <= np.median(lengths) <= 640
+    assert limits.min() >= 64 and limits.max() <= 512 and 270 <= limits.mean() <= 306
+    assert all(1 <= t < 151936 for p, _ in reqs[:50] for t in p)  # never the EOS id 0
+    arrivals = load.arrival_times(4000, 32.0, seed=5)
+    assert np.all(np.diff(arrivals) > 0)
+    assert abs(arrivals[-1] / 4000 - 1 / 32.0) < 0.1 / 32.0
+    assert load.make_requests(3, 4096, seed=1) == load.make_requests(3, 4096, seed=1)

@@ -32,6 +32,8 @@ def _worker(rank: int, size: int, port: int, queue) -> None:
         replicas.barrier()
         slowest = replicas.max_over_ranks(1.0 + r)
         total = replicas.sum_over_ranks(float(len(mine)))
+        gathered = replicas.gather_objects({"rank": r, "ttft": [0.1 * r, 0.2 * r]})
+        assert gathered == [{"rank": k, "ttft": [0.1 * k, 0.2 * k]} for k in range(n)]
         queue.put((r, mine, slowest, total))
     finally:
         replicas.shutdown()
@@ -59,4 +61,5 @@ def test_single_process_needs_no_group():
     assert replicas.world()[1] == 1 or os.environ.get("WORLD_SIZE")
     assert not replicas.init("gloo") if "WORLD_SIZE" not in os.environ else True
     assert replicas.max_over_ranks(3.5) == 3.5
+    assert replicas.gather_objects({"x": 1}) == [{"x": 1}]
     assert replicas.shard([1, 2, 3], 0, 1) == [1, 2, 3]
