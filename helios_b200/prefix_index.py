@@ -49,7 +49,8 @@ def _flatten(token_lists: Sequence[Sequence[int]], block_size: int):
     block_offsets = np.zeros(len(lengths) + 1, dtype=np.int64)
     np.cumsum(blocks, out=block_offsets[1:])
     full = np.array([n // block_size for n in lengths], dtype=np.int32)
-    flat = np.fromiter((t for tokens in token_lists for t in tokens), dtype=np.int64, count=int(offsets[-1]))
+    parts = [np.fromiter(tokens, dtype=np.int64, count=n) for tokens, n in zip(token_lists, lengths)]
+    flat = np.concatenate(parts) if parts else np.zeros(0, dtype=np.int64)
     if flat.size and (flat.min() < 0 or flat.max() > _MAX_TOKEN):
         raise ValueError("Token IDs must be non-negative integers." if flat.min() < 0
                          else "Token IDs above 2^31 - 1 are not supported.")

@@ -85,7 +85,6 @@ def config4(steps: int = 128, share: bool = True, device: torch.device | None = 
     torch.manual_seed(seed)
     with torch.device(device):
         model = Qwen3Model(cfg).eval()
-    model.enable_cuda_graphs()
     decoder = Decoder(model)
     g = torch.Generator().manual_seed(seed)
     prefix = torch.randint(0, cfg.vocab_size, (PREFIX_TOKENS,), generator=g).tolist()
@@ -114,6 +113,8 @@ def config4(steps: int = 128, share: bool = True, device: torch.device | None = 
             donor.close()
             torch.cuda.synchronize(device)
 
+            index.lookup(prompts[:2])  # first call: pinned staging and kernel set-up, untimed
+            torch.cuda.synchronize(device)
             # Admission: one device lookup for all 128 prompts, then aliasing restores.
             start, end = _cuda_timer(device)
             t0 = time.perf_counter()
@@ -130,7 +131,10 @@ def config4(steps: int = 128, share: bool = True, device: torch.device | None = 
             restore_gpu = start.elapsed_time(end) / 1e3
             restored = [c.length for c in caches]
 
-            # Tails: packed ticks of at most 2048 prompt tokens, rows chunked across ticks.
+            # Tails: packed ticks of at most 2048 prompt tokens, rows chunked across ticks. Every
+            # tail tick has its own shape, so they run eagerly (a graph would be captured per
+            # tick and never replayed); the decode steps below replay graphs.
+            model._graphs = None
             offsets = list(restored)
             ticks = 0
             first_logits = {}
@@ -160,6 +164,7 @@ def config4(steps: int = 128, share: bool = True, device: torch.device | None = 
             prefill_seconds = start.elapsed_time(end) / 1e3
             tail_tokens = sum(len(p) for p in prompts) - sum(restored)
 
+            model.enable_cuda_graphs()
             samplings = [Sampling(temperature=0.2, top_p=0.95, max_new_tokens=total_steps + 1)] * REQUESTS
             sample_gen = torch.Generator(device=device).manual_seed(seed)
             ids = sample_rows(heads, samplings, generator=sample_gen).tolist()
