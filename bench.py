@@ -68,6 +68,15 @@ CONFIG5_RATE = 64.0            # requests/s per GPU for the bench's config-5 poi
 CONFIG5_REQUESTS_PER_GPU = 256
 
 
+_T0 = time.time()
+
+
+def stage(text: str) -> None:
+    """Progress line on stderr, tagged with the rank and seconds since start (rank 0's
+    JSON line stays the only stdout output)."""
+    print(f"[bench rank {os.environ.get('RANK', '0')} +{time.time() - _T0:6.1f}s] {text}", file=sys.stderr, flush=True)
+
+
 def peaks() -> tuple[dict, str]:
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -640,11 +649,15 @@ def run_b200(args) -> None:
     rank, size, local = replicas.world()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    replicas.init("nccl" if size > 1 else "gloo")
+    # Rank 0 alone runs the rooflines and configs 4 and the reference's GPU path while the
+    # others wait at a barrier, so the group's timeout leaves room for those stages.
+    replicas.init("nccl" if size > 1 else "gloo", timeout_s=600.0)
+    stage("replica build")
     steps_total = args.warmup * 2 + args.steps * 2 + 4
     model, decoder, pool, caches, pending, chunk = build_replica(device, seed=1000 + rank, steps_total=steps_total)
     runner = TickRunner(device, model, decoder, pool, caches, pending, chunk)
     with ClockSampler(local) as clocks:
+        stage("warm-up ticks")
         for _ in range(args.warmup):
             runner.device_step()
         torch.cuda.synchronize(device)
@@ -654,6 +667,7 @@ def run_b200(args) -> None:
     seconds_local = seconds
     seconds = replicas.max_over_ranks(seconds, device)
     value = size * TOKENS_PER_STEP * args.steps / seconds
+    stage(f"timed ticks done: {1e3 * seconds_local / args.steps:.3f} ms per tick")
     # End to end through the public API, host token lists in, sampled ids out.
     for _ in range(max(3, args.warmup // 2)):  # eager tick, graph capture, first replay
         runner.api_step()
@@ -667,6 +681,7 @@ def run_b200(args) -> None:
     torch.cuda.empty_cache()
     per_rank = replicas.gather_objects({"rank": rank, "ms_per_step": round(own_ms, 3),
                                         "sm_mhz": clocks.summary_cached().get("sm_mhz")}, device)
+    stage("rooflines")
     roof = decode_attention_roofline(device, pk["hbm_gbs"]) if rank == 0 else None
     prefill_roof = prefill_attention_roofline(device, pk["bf16_tflops"]) if rank == 0 else None
     if roof is not None:
@@ -674,6 +689,8 @@ def run_b200(args) -> None:
     extras = {}
     if not args.no_extras:
         extras = run_extras(args, device, rank, size)
+    if rank == 0 and size == 1 and not args.no_cpu:
+        stage("CPU baseline")
     cpu = cpu_baseline() if (rank == 0 and size == 1 and not args.no_cpu) else None
     if rank == 0:
         step_s = seconds / args.steps
@@ -710,6 +727,7 @@ def run_extras(args, device: torch.device, rank: int, size: int) -> dict:
         from helios_b200.workloads import config4
 
         try:
+            stage("config 4")
             out["config4"] = config4(steps=128, device=device)
         except Exception as error:  # noqa: BLE001 - reported in the line, the headline stands
             out["config4"] = {"error": f"{type(error).__name__}: {error}"}
@@ -718,7 +736,9 @@ def run_extras(args, device: torch.device, rank: int, size: int) -> dict:
     if reference_package() is not None:
         from helios_b200 import load
 
+        stage("config 5")
         point = load.measure(CONFIG5_RATE, CONFIG5_REQUESTS_PER_GPU * size, device=device)
+        stage("config 5 done")
         if rank == 0:
             point["workload"] = (f"BASELINE config 5 at {CONFIG5_RATE:g} req/s per GPU, "
                                  f"{CONFIG5_REQUESTS_PER_GPU} requests per GPU (the full sweep: "
@@ -726,6 +746,7 @@ def run_extras(args, device: torch.device, rank: int, size: int) -> dict:
             out["config5"] = point
         torch.cuda.empty_cache()
         if rank == 0:
+            stage("reference GPU dense path")
             out["reference_gpu_dense"] = reference_gpu_dense(device, steps=min(args.steps, 8))
     elif rank == 0:
         out["config5"] = out["reference_gpu_dense"] = {"unavailable": "the reference package is not importable "

@@ -38,6 +38,12 @@ TICK_BUDGET, MAX_BATCH = 2048, 128
 EOS = 0  # prompts draw ids from [1, vocab); an EOS the model samples ends its request early
 
 
+def _log(text: str) -> None:
+    import sys
+
+    print(f"[load] {text}", file=sys.stderr, flush=True)
+
+
 def make_requests(n: int, vocab: int, seed: int) -> list[tuple[list[int], int]]:
     """``n`` (prompt ids, max_new_tokens) pairs with BASELINE config 5's distributions."""
     rng = np.random.default_rng(seed)
@@ -118,11 +124,13 @@ def measure(rate: float, total_requests: int, *, seed: int = 5, device: torch.de
         if warmup_requests:  # kernels, library handles and allocator blocks, outside the measurement
             warm = make_requests(warmup_requests, vocab, seed + 100 + rank)
             run_replica(engine, warm, np.zeros(len(warm)))
+        _log(f"rank {rank}: warm-up done")
         requests = make_requests(total_requests, vocab, seed)
         arrivals = arrival_times(total_requests, rate * size, seed)
         mine = replicas.shard(list(range(total_requests)), rank, size)
         replicas.barrier(device)
         out = run_replica(engine, [requests[i] for i in mine], arrivals[mine] - (arrivals[mine][0] if mine else 0))
+        _log(f"rank {rank}: {out['requests']} requests, {out['output_tokens']} tokens in {out['span_s']:.2f} s")
     finally:
         if own_engine:
             engine.close()
