@@ -281,6 +281,37 @@ def time_steps(step, steps: int, device: torch.device) -> float:
     return start.elapsed_time(end) / 1000.0
 
 
+def graph_seconds_per_call(call, device: torch.device, iters: int, warmup: int = 3) -> float:
+    """Device time of one ``call`` (a launch sequence of one kernel call) with no host gaps:
+    ``iters`` calls captured in one CUDA graph, replayed three times between CUDA events on
+    the capturing stream; the median replay is divided by ``iters``. Eager back-to-back calls
+    would also time the host's launch work between short kernels."""
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            call()
+    torch.cuda.current_stream(device).wait_stream(side)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(iters):
+            call()
+    graph.replay()
+    torch.cuda.synchronize(device)
+    times = []
+    stream = torch.cuda.current_stream(device)
+    for _ in range(3):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize(device)
+        times.append(start.elapsed_time(end) / 1e3 / iters)
+    del graph
+    return sorted(times)[1]
+
+
 def measured_traffic(kernel: str) -> int | None:
     """DRAM bytes (read + write) per launch of `kernel` from the committed ncu capture of the
     same workload (profiles/roofline_traffic.json), or None when there is none."""
@@ -308,16 +339,8 @@ def prefill_attention_roofline(device: torch.device, peak_tflops: float, iters: 
         batch.prepare_packed([PREFILL])
         q = torch.randn(PREFILL, cfg.n_heads, cfg.head_dim, device=device, generator=gen).to(torch.bfloat16)
         out = torch.empty_like(q)
-        for _ in range(3):
-            ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out)
-        torch.cuda.synchronize(device)
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        for _ in range(iters):
-            ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out)
-        end.record()
-        torch.cuda.synchronize(device)
-    seconds = start.elapsed_time(end) / 1000.0 / iters
+        seconds = graph_seconds_per_call(lambda: ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out),
+                                         device, iters)
     flops = 4 * cfg.n_heads * cfg.head_dim * (PREFILL * (PREFILL + 1) // 2)
     achieved = flops / seconds / 1e12
     del pool, batch
@@ -325,7 +348,8 @@ def prefill_attention_roofline(device: torch.device, peak_tflops: float, iters: 
     return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_tflops, "unit": "TFLOP/s",
             "frac": round(achieved / peak_tflops, 4), "kernel": "prefill_attention_kernel (tcgen05/TMEM)",
             "workload": "BASELINE config 3 prefill half: one 2048-token row at offset 0, 32/8 heads, d=128",
-            "flops_per_call": flops, "us_per_call": round(seconds * 1e6, 2)}
+            "flops_per_call": flops, "us_per_call": round(seconds * 1e6, 2),
+            "timing": f"median of 3 CUDA-graph replays of {iters} calls, CUDA events"}
 
 
 def decode_attention_roofline(device: torch.device, peak_gbs: float, iters: int = 20) -> dict:
@@ -336,16 +360,8 @@ def decode_attention_roofline(device: torch.device, peak_gbs: float, iters: int 
     pool, batch, q, contexts = config2_batch(device)
     with torch.inference_mode():
         out = torch.empty_like(q)
-        for _ in range(3):
-            ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out)
-        torch.cuda.synchronize(device)
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        for _ in range(iters):
-            ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out)
-        end.record()
-        torch.cuda.synchronize(device)
-    seconds = start.elapsed_time(end) / 1000.0 / iters
+        seconds = graph_seconds_per_call(lambda: ops.paged_attention(q, pool.keys[0], pool.values[0], batch, out),
+                                         device, iters)
     kv_bytes = sum(contexts) * 8 * 128 * 2 * 2
     io_bytes = 2 * 64 * 32 * 128 * 2 + 64 * batch.block_table.shape[1] * 4
     achieved = (kv_bytes + io_bytes) / seconds / 1e9
@@ -354,7 +370,8 @@ def decode_attention_roofline(device: torch.device, peak_gbs: float, iters: int 
             "kernel": "decode_attention_kernel (+ decode_combine_kernel), hb_paged_attention on decode rows",
             "workload": "BASELINE config 2: 64 rows x 1 query, context U[512,8192], 32/8 heads, d=128, 4096 pages",
             "algorithmic_bytes_per_call": kv_bytes + io_bytes, "us_per_call": round(seconds * 1e6, 2),
-            "split_keys": batch.split_keys, "decode_items": batch.num_decode_items}
+            "split_keys": batch.split_keys, "decode_items": batch.num_decode_items,
+            "timing": f"median of 3 CUDA-graph replays of {iters} calls, CUDA events"}
     del pool, batch
     torch.cuda.empty_cache()
     return info

@@ -65,6 +65,27 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Two fp32 fused multiply-adds in one instruction (sm_100 f32x2: two lanes of work per issue
+// slot), d = a * b + c elementwise.
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                     float c1) {
+  asm("{.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+// Three-input maximum (sm_100): half the instructions of a two-input reduction.
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 template <int GROUP>
 __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(AttentionParams p,
                                                                           const __grid_constant__ CUtensorMap qmap,
@@ -331,9 +352,9 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
       float m8[8];
 #pragma unroll
       for (int c = 0; c < 8; ++c)
-        m8[c] = fmaxf(fmaxf(fmaxf(s[c], s[c + 8]), fmaxf(s[c + 16], s[c + 24])),
-                      fmaxf(fmaxf(s[c + 32], s[c + 40]), fmaxf(s[c + 48], s[c + 56])));
-      const float mine = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])), fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        m8[c] = max3(max3(s[c], s[c + 8], s[c + 16]), max3(s[c + 24], s[c + 32], s[c + 40]),
+                     fmaxf(s[c + 48], s[c + 56]));
+      const float mine = max3(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
       xmax[t][j & 1][half][r] = mine;
       mbar_arrive(&xbar[t][quad][j & 1]);
       if (!mbar_wait(&xbar[t][quad][j & 1], (j >> 1) & 1, &abort_flag)) { ok = false; break; }
@@ -369,10 +390,11 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
         uint32_t pw[16];
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
-          const float e0 = fast_exp2(fmaf(s[chunk * 32 + 2 * c], p.scale_log2, neg));
-          const float e1 = fast_exp2(fmaf(s[chunk * 32 + 2 * c + 1], p.scale_log2, neg));
-          s8[(2 * c) & 7] += e0;
-          s8[(2 * c + 1) & 7] += e1;
+          float x0, x1;
+          fma2(x0, x1, s[chunk * 32 + 2 * c], s[chunk * 32 + 2 * c + 1], p.scale_log2, p.scale_log2, neg, neg);
+          const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
+          const int a = (2 * c) & 7;
+          fma2(s8[a], s8[a + 1], e0, e1, 1.f, 1.f, s8[a], s8[a + 1]);
           pw[c] = pack_bf16(e0, e1);
         }
         tmem_st16u(tSP + half * 32 + chunk * 16, pw);
