@@ -262,11 +262,15 @@ class TickRunner:
         return 3 + per_layer * self.model.config.n_layers + 2
 
 
-def time_steps(step, steps: int, device: torch.device) -> float:
+def time_steps(step, steps: int, device: torch.device, *, all_ranks: bool = True) -> float:
+    """Seconds for ``steps`` calls of ``step``, CUDA events on the current stream. With
+    ``all_ranks`` every rank must call it (the region is bracketed by barriers); legs that
+    rank 0 runs alone pass False, so they take no collective step."""
     from helios_b200 import replicas
 
     torch.cuda.synchronize(device)
-    replicas.barrier(device)
+    if all_ranks:
+        replicas.barrier(device)
     torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
@@ -276,7 +280,8 @@ def time_steps(step, steps: int, device: torch.device) -> float:
         torch.cuda.nvtx.range_pop()
     end.record()
     torch.cuda.synchronize(device)
-    replicas.barrier(device)
+    if all_ranks:
+        replicas.barrier(device)
     torch.cuda.synchronize(device)
     return start.elapsed_time(end) / 1000.0
 
@@ -527,7 +532,7 @@ def reference_gpu_dense(device: torch.device, steps: int, warmup: int = 3, seed:
 
     for _ in range(warmup):
         tick()
-    seconds = time_steps(tick, steps, device)
+    seconds = time_steps(tick, steps, device, all_ranks=False)  # rank 0 alone runs this leg
     del caches, model, decoder
     torch.cuda.empty_cache()
     return {"value": round(TOKENS_PER_STEP * steps / seconds, 1), "unit": UNIT,
