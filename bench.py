@@ -745,7 +745,8 @@ def run_extras(args, device: torch.device, rank: int, size: int) -> dict:
     out = {}
     from helios_b200 import replicas
 
-    if rank == 0:
+    # Config 4 and the reference's GPU path do not depend on N: one GPU measures them (N=1).
+    if rank == 0 and size == 1:
         from helios_b200.workloads import config4
 
         try:
@@ -767,7 +768,7 @@ def run_extras(args, device: torch.device, rank: int, size: int) -> dict:
                                  "python -m helios_b200.load)")
             out["config5"] = point
         torch.cuda.empty_cache()
-        if rank == 0:
+        if rank == 0 and size == 1:
             stage("reference GPU dense path")
             out["reference_gpu_dense"] = reference_gpu_dense(device, steps=min(args.steps, 8))
     elif rank == 0:

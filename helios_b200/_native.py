@@ -41,6 +41,7 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "hb_version": (c_int, []),
     "hb_last_error": (ctypes.c_char_p, []),
     "hb_device_status": (c_int, [ctypes.POINTER(c_uint32), c_int]),
+    "hb_selftest_wait_timeout": (c_int, [I64, P, P]),
     "hb_tick_pack": (c_int, [P, I32, P, I32, P, I32, I32, I32, I32, I32, I32, I32, I32, I32,
                              P, P, P, P, P, P, P, P, I32, P, I32, P, I32, P, P, P]),
     "hb_qk_norm_rope_append": (c_int, [P, I64, I64, P, I64, I64, P, I64, I64, P, P, F32, P, P, I64, P, P,

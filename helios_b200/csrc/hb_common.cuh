@@ -94,13 +94,14 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 
 // Bounded wait. Returns false (and raises the abort flag and status bit) on
 // timeout, or immediately when another thread of the CTA already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          long long limit_cycles = kWaitLimitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - start > kWaitLimitCycles) {
+    if (clock64() - start > limit_cycles) {
       *abort_flag = 1;
       raise_status(kStatusWaitTimeout);
       return false;

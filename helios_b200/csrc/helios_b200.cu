@@ -193,6 +193,24 @@ int launch_rmsnorm(const hb::RowNormParams& p, cudaStream_t stream, const char* 
   return check_launch(what);
 }
 
+// One thread waits for phase 0 of a fresh mbarrier that no thread arrives at: the bounded
+// wait must run out after limit_cycles, raise the wait-timeout status bit and return.
+__global__ void wait_timeout_selftest_kernel(long long limit_cycles, int32_t* result) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    hb::mbar_init(&bar, 1);
+    abort_flag = 0;
+    hb::fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool ok = hb::mbar_wait(&bar, 0, &abort_flag, limit_cycles);
+    result[0] = ok ? 1 : 0;
+    result[1] = abort_flag;
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -212,6 +230,16 @@ int hb_device_status(uint32_t* status, int clear) {
     e = cudaMemcpyToSymbol(hb::g_status, &zero, sizeof(uint32_t));
     if (e != cudaSuccess) return fail(HB_ERR_CUDA, "clear status: %s", cudaGetErrorString(e));
   }
+  return HB_OK;
+}
+
+int hb_selftest_wait_timeout(int64_t limit_cycles, int32_t* result, cudaStream_t stream) {
+  if (limit_cycles < 1 || limit_cycles > (int64_t(1) << 31))
+    return fail(HB_ERR_INVALID, "limit_cycles %lld outside [1, 2^31]", static_cast<long long>(limit_cycles));
+  if (result == nullptr || !aligned(result, 4)) return fail(HB_ERR_INVALID, "result must be a device int32[2]");
+  wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(limit_cycles, result);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(HB_ERR_CUDA, "wait_timeout_selftest_kernel: %s", cudaGetErrorString(e));
   return HB_OK;
 }
 

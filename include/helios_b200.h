@@ -57,6 +57,16 @@ HB_API const char* hb_last_error(void);
 HB_API int hb_device_status(uint32_t* status, int clear);
 
 /*
+ * Self-test of the kernels' error path (no counterpart in the reference). One thread of a
+ * one-CTA kernel waits, through the same bounded mbarrier wait the attention and GEMM
+ * kernels use, for a barrier phase that nothing completes, with a limit of limit_cycles SM
+ * clock cycles (1 .. 2^31, a few milliseconds at most). The wait gives up, sets
+ * HB_STATUS_WAIT_TIMEOUT and the kernel returns normally; result (device int32[2]) receives
+ * whether the wait succeeded (0 expected) and the CTA's abort flag (1 expected).
+ */
+HB_API int hb_selftest_wait_timeout(int64_t limit_cycles, int32_t* result, cudaStream_t stream);
+
+/*
  * (a) Tick packing. Replaces PackedBatchCache.prepare_packed
  * (src/helios/runtime/qwen3/paged_cache.py:418-494) and PagedBatchCache.prepare
  * (paged_cache.py:221-270), whose Python lists are rebuilt and copied every tick.
