@@ -169,6 +169,9 @@ def gemm_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | No
 
 STREAM_GEMM_MAX_ROWS = 256
 _STREAM_WS: dict[torch.device, torch.Tensor] = {}
+# Buffers a larger call replaced: kept alive, since a CUDA graph captured earlier still
+# launches kernels on their addresses.
+_RETIRED: list[torch.Tensor] = []
 
 
 def stream_gemm_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
@@ -179,6 +182,8 @@ def stream_gemm_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
         if torch.cuda.is_current_stream_capturing():
             # Memory allocated under capture belongs to the graph's pool; the workspace outlives graphs.
             raise RuntimeError("stream_gemm: run one call of this size before capturing it")
+        if ws is not None:
+            _RETIRED.append(ws)
         ws = _STREAM_WS[device] = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
     return ws
 
@@ -207,7 +212,7 @@ def stream_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = Non
     return out
 
 
-_ARGMAX_KEYS: dict[torch.device, torch.Tensor] = {}
+_ARGMAX_KEYS: dict[torch.device, torch.Tensor] = {}  # grown like the stream GEMM workspace
 
 
 def lm_head_argmax(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -226,6 +231,8 @@ def lm_head_argmax(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | No
             # Memory allocated under capture belongs to the graph's pool; the keys outlive graphs.
             raise RuntimeError("lm_head_argmax: run one call of this size before capturing it")
         # Zeroed once; every call leaves the keys it used at zero.
+        if keys is not None:
+            _RETIRED.append(keys)
         keys = _ARGMAX_KEYS[dev] = torch.zeros(max(m, 256), dtype=torch.int64, device=dev)
     if out is None:
         out = torch.empty(m, dtype=torch.long, device=dev)
