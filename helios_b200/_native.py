@@ -54,8 +54,6 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "hb_rmsnorm": (c_int, [P, I64, P, P, F32, P, I32, I32, P]),
     "hb_add_rmsnorm": (c_int, [P, P, P, F32, P, P, I32, I32, P]),
     "hb_swiglu": (c_int, [P, P, I64, I64, P]),
-    "hb_stream_gemm_workspace_bytes": (c_size_t, [I32, I32, I32]),
-    "hb_stream_gemm": (c_int, [P, I32, I32, P, I32, P, P, c_size_t, P]),
     "hb_gemm_swiglu": (c_int, [P, I32, I32, P, I32, P, P]),
     "hb_attention_set_overlap": (c_int, [I32]),
     "hb_hash_token_blocks": (c_int, [P, P, I32, I32, P, P, P]),

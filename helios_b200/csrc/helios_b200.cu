@@ -16,7 +16,6 @@
 #include "attention_decode.cuh"
 #include "attention_prefill.cuh"
 #include "gemm_qkv.cuh"
-#include "gemm_stream.cuh"
 #include "gemm_swiglu.cuh"
 #include "hb_common.cuh"
 #include "lm_head_argmax.cuh"
@@ -122,7 +121,6 @@ int ensure_smem(K kernel, int bytes, bool (&done)[64]) {
   return HB_OK;
 }
 
-bool g_stream_smem[64];
 bool g_dec_smem[4][64], g_decp_smem[4][64], g_pre_smem[4][64], g_tick_smem[64], g_gemm_smem[64], g_qkv_smem[64], g_argmax_smem[64];
 
 constexpr int kDefaultOverlapDecodeSms = 100;
@@ -646,94 +644,6 @@ int hb_sample(const void* logits, int64_t row_stride, int32_t rows, int32_t voca
                      out_ids};
   hb::sample_kernel<<<rows, hb::kSampleThreads, 0, stream>>>(p);
   return check_launch("sample_kernel");
-}
-
-}  // extern "C" (reopened below)
-
-namespace {
-
-// Work split of hb_stream_gemm on this device: grid, units per CTA, ring stages, the most parts
-// any weight tile is split into, and the workspace bytes.
-struct StreamPlan {
-  int grid, per_cta, stages, max_parts, n_pad, tiles, ksteps;
-  size_t counter_bytes, workspace_bytes;
-};
-
-int stream_plan(int32_t m, int32_t n, int32_t k, StreamPlan* plan) {
-  if (m < 1 || m > hb::kStreamMaxTokens || n < 1 || k < 1)
-    return fail(HB_ERR_INVALID, "stream GEMM sizes m=%d n=%d k=%d (m must be 1..%d)", m, n, k, hb::kStreamMaxTokens);
-  if (n % hb::kStreamTileRows != 0 || k % hb::kStreamTileK != 0)
-    return fail(HB_ERR_UNSUPPORTED, "stream GEMM needs n %% %d == 0 and k %% %d == 0 (got %d, %d)",
-                hb::kStreamTileRows, hb::kStreamTileK, n, k);
-  const int sms = sm_count();
-  if (sms <= 0) return fail(HB_ERR_CUDA, "cannot read the SM count");
-  StreamPlan p{};
-  p.n_pad = (m + 31) / 32 * 32;
-  p.tiles = n / hb::kStreamTileRows;
-  p.ksteps = k / hb::kStreamTileK;
-  const int64_t total = static_cast<int64_t>(p.tiles) * p.ksteps;
-  if (total > INT32_MAX / 2) return fail(HB_ERR_UNSUPPORTED, "stream GEMM too large");
-  const int grid0 = static_cast<int>(std::min<int64_t>(sms, total));
-  p.per_cta = static_cast<int>((total + grid0 - 1) / grid0);
-  p.grid = static_cast<int>((total + p.per_cta - 1) / p.per_cta);
-  p.stages = std::min<int>(hb::kStreamMaxStages, hb::kStreamSmemBudget / hb::stream_stage_bytes(p.n_pad));
-  p.max_parts = 1;
-  for (int t = 0; t < p.tiles; ++t) {
-    const int first = static_cast<int>((static_cast<int64_t>(t) * p.ksteps) / p.per_cta);
-    const int last = static_cast<int>((static_cast<int64_t>(t + 1) * p.ksteps - 1) / p.per_cta);
-    p.max_parts = std::max(p.max_parts, last - first + 1);
-  }
-  p.counter_bytes = (static_cast<size_t>(p.tiles) * 4 + 255) / 256 * 256;
-  p.workspace_bytes = p.counter_bytes + (p.max_parts > 1 ? static_cast<size_t>(p.tiles) * p.max_parts *
-                                                                hb::kStreamTileRows * p.n_pad * sizeof(float)
-                                                          : 0);
-  *plan = p;
-  return HB_OK;
-}
-
-}  // namespace
-
-extern "C" {
-
-size_t hb_stream_gemm_workspace_bytes(int32_t m, int32_t n, int32_t k) {
-  StreamPlan plan;
-  return stream_plan(m, n, k, &plan) == HB_OK ? plan.workspace_bytes : 0;
-}
-
-int hb_stream_gemm(const void* x, int32_t m, int32_t k, const void* w, int32_t n, void* out, void* workspace,
-                   size_t workspace_bytes, cudaStream_t stream) {
-  if (m == 0) return HB_OK;
-  StreamPlan plan;
-  if (int rc = stream_plan(m, n, k, &plan)) return rc;
-  if (x == nullptr || w == nullptr || out == nullptr || workspace == nullptr || !aligned(x, 16) ||
-      !aligned(w, 16) || !aligned(out, 16) || !aligned(workspace, 256))
-    return fail(HB_ERR_INVALID, "stream GEMM pointers must be non-null, 16-byte aligned (workspace 256)");
-  if (workspace_bytes < plan.workspace_bytes)
-    return fail(HB_ERR_INVALID, "stream GEMM workspace holds %zu bytes, needs %zu", workspace_bytes,
-                plan.workspace_bytes);
-  CUtensorMap wmap, xmap;
-  const uint64_t row_bytes = static_cast<uint64_t>(k) * 2;
-  if (int rc = encode_2d(&wmap, w, k, n, row_bytes, hb::kStreamTileK, hb::kStreamTileRows)) return rc;
-  if (int rc = encode_2d(&xmap, x, k, m, row_bytes, hb::kStreamTileK, plan.n_pad)) return rc;
-  hb::StreamGemmParams p{};
-  p.m = m;
-  p.n_pad = plan.n_pad;
-  p.n = n;
-  p.k = k;
-  p.tiles = plan.tiles;
-  p.ksteps = plan.ksteps;
-  p.per_cta = plan.per_cta;
-  p.stages = plan.stages;
-  p.max_parts = plan.max_parts;
-  p.out = static_cast<__nv_bfloat16*>(out);
-  p.counters = static_cast<int32_t*>(workspace);
-  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + plan.counter_bytes);
-  const uint32_t smem = static_cast<uint32_t>(plan.stages) * hb::stream_stage_bytes(plan.n_pad) + 1024;
-  if (int rc = ensure_smem(hb::stream_gemm_kernel, hb::kStreamSmemBudget + 1024, g_stream_smem)) return rc;
-  const cudaError_t e = launch_pdl(hb::stream_gemm_kernel, dim3(plan.grid), dim3(hb::kStreamThreads), smem, stream,
-                                   p, wmap, xmap);
-  if (e != cudaSuccess) return fail(HB_ERR_CUDA, "stream_gemm_kernel: %s", cudaGetErrorString(e));
-  return check_launch("stream_gemm_kernel");
 }
 
 int hb_gemm_swiglu(const void* x, int32_t m, int32_t k, const void* w_gate_up, int32_t inter, void* out,

@@ -244,15 +244,13 @@ def _lm_head(dev, g, rows: int, fused: bool):
     return [make() for _ in range(2)], vocab * HIDDEN * 2
 
 
-def _projection(dev, g, m: int, n: int, k: int, stream: bool):
-    """One decode-tick projection [m, k] x [n, k]^T: the stream GEMM or cuBLAS (F.linear).
-    Four weights cycled, 4 x n x k x 2 bytes, beyond L2 for the Qwen3-4B shapes."""
+def _projection(dev, g, m: int, n: int, k: int):
+    """One decode-tick projection [m, k] x [n, k]^T on cuBLAS, as the model runs it. Four
+    weights cycled, 4 x n x k x 2 bytes, beyond L2 for the Qwen3-4B shapes."""
     def make():
         x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
         w = (torch.randn(n, k, device=dev, generator=g) / k ** 0.5).to(torch.bfloat16)
         out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
-        if stream:
-            return lambda: ops.stream_gemm(x, w, out)
         return lambda: torch.matmul(x, w.T, out=out)
     return [make() for _ in range(4)], n * k * 2
 
@@ -292,9 +290,9 @@ def main(argv: list[str]) -> None:
         "swiglu": lambda: _swiglu(dev, g),
         "add_rmsnorm": lambda: _add_rmsnorm(dev, g),
         "prefill": lambda: _attention(dev, [0], [2048], 1),
-        **{f"proj_{name}{m}_{impl}": (lambda m=m, n=n, k=k, impl=impl: _projection(dev, g, m, n, k, impl == "stream"))
+        **{f"proj_{name}{m}": (lambda m=m, n=n, k=k: _projection(dev, g, m, n, k))
            for name, n, k in (("qkv", 6144, 2560), ("o", 2560, 4096), ("gateup", 19456, 2560), ("down", 2560, 9728))
-           for m in (32, 128, 256) for impl in ("stream", "cublas")},
+           for m in (32, 128, 256)},
         "decode": lambda: _attention(dev, decode_lengths, [1] * 32, 2),
         "mixed": lambda: _attention(dev, decode_lengths + [0], [1] * 32 + [2048], 2),
         "prefix_decode": lambda: _prefix_decode(dev, 2),

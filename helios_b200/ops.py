@@ -167,52 +167,12 @@ def gemm_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | No
     return out
 
 
-STREAM_GEMM_MAX_ROWS = 256
-_STREAM_WS: dict[torch.device, torch.Tensor] = {}
 # Buffers a larger call replaced: kept alive, since a CUDA graph captured earlier still
 # launches kernels on their addresses.
 _RETIRED: list[torch.Tensor] = []
 
 
-def stream_gemm_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """The device's shared, grow-only workspace of :func:`stream_gemm` (zeroed once; every call
-    leaves its tile counters at zero, and calls on one stream run one after another)."""
-    ws = _STREAM_WS.get(device)
-    if ws is None or ws.numel() < nbytes:
-        if torch.cuda.is_current_stream_capturing():
-            # Memory allocated under capture belongs to the graph's pool; the workspace outlives graphs.
-            raise RuntimeError("stream_gemm: run one call of this size before capturing it")
-        if ws is not None:
-            _RETIRED.append(ws)
-        ws = _STREAM_WS[device] = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-    return ws
-
-
-def stream_gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """``x [m, k] @ w[n, k]^T`` (bf16, fp32 accumulation) for decode-tick row counts
-    (``m <= STREAM_GEMM_MAX_ROWS``): the weight streams through every SM (hb_stream_gemm),
-    results independent of timing."""
-    _need(x, BF16, "x")
-    _need(w, BF16, "w")
-    m, k = x.shape
-    n = w.shape[0]
-    if w.shape[1] != k:
-        raise ValueError("w must be [n, k] matching x")
-    if out is None:
-        out = torch.empty((m, n), dtype=BF16, device=x.device)
-    if m == 0:
-        return out
-    nbytes = int(lib().hb_stream_gemm_workspace_bytes(m, n, k))
-    if nbytes == 0:
-        raise ValueError(f"stream_gemm does not support m={m}, n={n}, k={k}: {_native.last_error()}")
-    ws = stream_gemm_workspace(x.device, nbytes)
-    rc = lib().hb_stream_gemm(x.data_ptr(), m, k, w.data_ptr(), n, out.data_ptr(), ws.data_ptr(), ws.numel(),
-                              _stream(x.device))
-    _native.check(rc, "hb_stream_gemm")
-    return out
-
-
-_ARGMAX_KEYS: dict[torch.device, torch.Tensor] = {}  # grown like the stream GEMM workspace
+_ARGMAX_KEYS: dict[torch.device, torch.Tensor] = {}
 
 
 def lm_head_argmax(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -194,21 +194,6 @@ HB_API int hb_paged_attention_static_workspace(const void* q, const void* key_po
                                                int32_t head_dim, float scale, void* out, cudaStream_t stream);
 
 /*
- * Weight-streaming GEMM for decode ticks: out[m][n] = x[m][k] * w[n][k]^T, bf16 in and out,
- * fp32 accumulation, for 1 <= m <= 256 token rows (n % 128 == 0, k % 64 == 0). Replaces the
- * nn.Linear projections of GroupedQueryAttention.forward (q|k|v and output,
- * src/helios/runtime/qwen3/layers.py:131-146, :163-164) and FeedForward.forward (gate|up,
- * down, layers.py:26-27) at decode-tick sizes. The (weight tile, K step) work is split in
- * equal ranges over the SMs; weight tiles split between SMs have their fp32 parts added in a
- * fixed order, so results do not depend on timing. workspace: hb_stream_gemm_workspace_bytes
- * bytes (256-byte aligned) whose first part holds per-tile counters that must be zero before
- * the first call and that every call leaves zero; the size depends on the device's SM count.
- */
-HB_API size_t hb_stream_gemm_workspace_bytes(int32_t m, int32_t n, int32_t k);
-HB_API int hb_stream_gemm(const void* x, int32_t m, int32_t k, const void* w, int32_t n, void* out, void* workspace,
-                          size_t workspace_bytes, cudaStream_t stream);
-
-/*
  * Hidden-size RMSNorm (RMSNorm.forward, src/helios/runtime/qwen3/layers.py:36-40).
  * With row_index (int64 [rows]) the rows are gathered first, as the logit-row
  * index_select before the final norm (src/helios/runtime/qwen3/model.py:108-110).
