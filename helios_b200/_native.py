@@ -61,9 +61,6 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "hb_prefix_index_remove": (c_int, [P, I32, P, I32, P]),
     "hb_prefix_index_lookup": (c_int, [P, I32, P, P, P, I32, P, P, P]),
     "hb_lm_head_argmax": (c_int, [P, I32, I32, P, I32, P, P, P]),
-    "hb_rope_gather": (c_int, [P, P, I64, I32, P, I32, I32, P, P, P]),
-    "hb_gemm_qkv_norm_rope_append": (c_int, [P, I32, I32, P, I32, I32, I32, P, P, F32, P, P, I32, I64, P, P, P, P,
-                                             P, I64, P]),
     "hb_embedding": (c_int, [P, P, I64, P, I64, I32, P]),
     "hb_page_copy": (c_int, [P, I64, I32, I64, I64, P, P, I32, P]),
     "hb_sample": (c_int, [P, I64, I32, I32, P, P, P, P, P]),

@@ -4,7 +4,7 @@
 // Persistent CTAs, one per SM (192 threads). A tile is 128 rows of A against 256 rows of the
 // weight B [N_total, K], taken as two 128-row boxes whose first rows the epilogue names
 // (b_row(tile_n, 0 / 1)): the gate|up GEMM stacks 128 gate rows over the matching 128 up
-// rows, the q|k|v GEMM takes two consecutive heads.
+// rows, the greedy lm_head takes 256 consecutive vocabulary rows.
 //   warp 0     TMA producer: per 64-wide K step, the [128 x 64] A tile and the two
 //              [128 x 64] B boxes into a 4-stage ring of 48 KB stages (128B swizzle; rows
 //              past M read as zeros);

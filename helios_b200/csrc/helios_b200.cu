@@ -15,7 +15,6 @@
 #include "../../include/helios_b200.h"
 #include "attention_decode.cuh"
 #include "attention_prefill.cuh"
-#include "gemm_qkv.cuh"
 #include "gemm_swiglu.cuh"
 #include "hb_common.cuh"
 #include "lm_head_argmax.cuh"
@@ -121,7 +120,7 @@ int ensure_smem(K kernel, int bytes, bool (&done)[64]) {
   return HB_OK;
 }
 
-bool g_dec_smem[4][64], g_decp_smem[4][64], g_pre_smem[4][64], g_tick_smem[64], g_gemm_smem[64], g_qkv_smem[64], g_argmax_smem[64];
+bool g_dec_smem[4][64], g_decp_smem[4][64], g_pre_smem[4][64], g_tick_smem[64], g_gemm_smem[64], g_argmax_smem[64];
 
 constexpr int kDefaultOverlapDecodeSms = 100;
 
@@ -732,55 +731,6 @@ int hb_prefix_index_lookup(const uint32_t* table, int32_t slots, const uint8_t* 
   return check_launch("prefix_lookup_kernel");
 }
 
-int hb_rope_gather(const float* cos, const float* sin, int64_t rope_rows, int32_t head_dim, const int64_t* positions,
-                   int32_t tokens, int32_t width, float* out_cos, float* out_sin, cudaStream_t stream) {
-  if (head_dim != hb::kQkvHeadDim || (width != head_dim && width != head_dim / 2) || tokens < 0 || rope_rows < 1)
-    return fail(HB_ERR_INVALID, "rope gather needs head_dim %d, width head_dim or head_dim / 2 and non-empty tables",
-                hb::kQkvHeadDim);
-  if (tokens == 0) return HB_OK;
-  if (cos == nullptr || sin == nullptr || positions == nullptr || out_cos == nullptr || out_sin == nullptr ||
-      !aligned(cos, 16) || !aligned(sin, 16) || !aligned(out_cos, 16) || !aligned(out_sin, 16))
-    return fail(HB_ERR_INVALID, "rope gather pointers must be non-null and 16-byte aligned");
-  hb::RopeGatherParams p{cos, sin, rope_rows, positions, tokens, width, out_cos, out_sin};
-  const int64_t threads = static_cast<int64_t>(width / 4) * tokens;
-  hb::rope_gather_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(p);
-  return check_launch("rope_gather_kernel");
-}
-
-int hb_gemm_qkv_norm_rope_append(const void* x, int32_t m, int32_t k, const void* w_qkv, int32_t heads,
-                                 int32_t kv_heads, int32_t head_dim, const float* q_scale, const float* k_scale,
-                                 float eps, const float* rope_cos, const float* rope_sin, int32_t rope_width,
-                                 int64_t rope_rows, const int64_t* positions, const int64_t* write_slots, void* q_out,
-                                 void* key_pool, void* value_pool, int64_t pool_slots, cudaStream_t stream) {
-  if (m < 0 || k < 1 || heads < 1 || kv_heads < 1 || heads % kv_heads) return fail(HB_ERR_INVALID, "bad q|k|v sizes");
-  if (head_dim != hb::kQkvHeadDim || k % hb::kGemmTileK != 0 || (heads + 2 * kv_heads) % 2 != 0)
-    return fail(HB_ERR_UNSUPPORTED,
-                "fused q|k|v GEMM needs head_dim %d, K %% %d == 0 and an even head-row count (got %d, %d, %d)",
-                hb::kQkvHeadDim, hb::kGemmTileK, head_dim, k, heads + 2 * kv_heads);
-  if ((rope_cos == nullptr) != (rope_sin == nullptr) ||
-      (rope_cos != nullptr && (positions == nullptr || rope_rows < 1 || (rope_width != head_dim && rope_width != head_dim / 2))))
-    return fail(HB_ERR_INVALID, "gathered rope rows need both tables, positions, rope_rows and width 64 or 128");
-  if (m == 0) return HB_OK;
-  if (x == nullptr || w_qkv == nullptr || q_out == nullptr || key_pool == nullptr || value_pool == nullptr ||
-      write_slots == nullptr)
-    return fail(HB_ERR_INVALID, "null q|k|v GEMM pointer");
-  if (!aligned(x, 16) || !aligned(w_qkv, 16) || !aligned(q_out, 16) || !aligned(key_pool, 16) ||
-      !aligned(value_pool, 16) || (q_scale && !aligned(q_scale, 16)) || (k_scale && !aligned(k_scale, 16)) ||
-      (rope_cos && !aligned(rope_cos, 16)) || (rope_sin && !aligned(rope_sin, 16)))
-    return fail(HB_ERR_INVALID, "q|k|v GEMM operands, pools, scales and rope rows must be 16-byte aligned");
-  CUtensorMap amap, bmap;
-  const uint64_t row_bytes = static_cast<uint64_t>(k) * 2;
-  const int head_rows = heads + 2 * kv_heads;
-  if (int rc = encode_2d(&amap, x, k, m, row_bytes, hb::kGemmTileK, hb::kGemmTileM)) return rc;
-  if (int rc = encode_2d(&bmap, w_qkv, k, static_cast<uint64_t>(head_rows) * head_dim, row_bytes, hb::kGemmTileK,
-                         hb::kGemmTileN))
-    return rc;
-  hb::GemmQkvParams p{m, k, (m + hb::kGemmTileM - 1) / hb::kGemmTileM, head_rows / 2, heads, kv_heads, q_scale,
-                      k_scale, eps, rope_cos, rope_sin, rope_width, rope_rows, positions, write_slots,
-                      static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(key_pool),
-                      static_cast<__nv_bfloat16*>(value_pool), pool_slots};
-  return launch_fused_gemm<hb::QkvEpilogue>(p, amap, bmap, g_qkv_smem, stream, "fused_gemm_kernel<qkv>");
-}
 
 int hb_verify_drafts(const int64_t* tokens, const int32_t* cu_seq_q, const int32_t* logit_offsets,
                      const int64_t* predictions, int32_t rows, int32_t* accepted, int64_t* emitted,

@@ -1,7 +1,7 @@
 """Kernel microbenchmarks at the BASELINE config-3 tick shapes, timed from CUDA-graph replays.
 
     python -m helios_b200.microbench [norm_rope] [swiglu] [add_rmsnorm] [prefill] [decode] [mixed[:N]] [prefix_decode] [sample]
-                                     [gate_up_fused] [gate_up_cublas] [qkv_fused] [qkv_fused_full_tables] [qkv_cublas]
+                                     [gate_up_fused] [gate_up_cublas] [qkv_cublas]
                                      [lm_head_argmax33|128] [lm_head_cublas33|128] [prefix_hash]
 
 Each case captures 24 calls of one entry point into a CUDA graph, cycling over input sets
@@ -112,16 +112,13 @@ def _gate_up(dev, g, fused: bool):
     return [make() for _ in range(2)], flops
 
 
-def _qkv(dev, g, fused: bool, half_tables: bool = True):
-    """The attention input side: q|k|v projection + per-head norm, RoPE and KV append, fused
-    (tcgen05, epilogue) or cuBLAS + the norm/RoPE/append kernel. Rope tables repeat their
-    first half in the second (as the model's do) unless half_tables is False."""
+def _qkv(dev, g):
+    """The attention input side as the model runs it: the q|k|v projection on cuBLAS, then the
+    per-head norm, RoPE and KV append kernel (b)."""
     import torch.nn.functional as F
 
     w = (torch.randn((H + 2 * HKV) * D, HIDDEN, device=dev, generator=g) / HIDDEN ** 0.5).to(torch.bfloat16)
     cos, sin = torch.randn(40960, D, device=dev), torch.randn(40960, D, device=dev)
-    if half_tables:
-        cos[:, D // 2:], sin[:, D // 2:] = cos[:, :D // 2], sin[:, :D // 2]
     qs, ks = torch.rand(D, device=dev) + 0.5, torch.rand(D, device=dev) + 0.5
     pages = 600
 
@@ -132,19 +129,14 @@ def _qkv(dev, g, fused: bool, half_tables: bool = True):
         slots = torch.randperm(pages * 256, device=dev, generator=g)[:T].long()
         pos = torch.randint(0, 4096, (T,), device=dev, generator=g).long()
         qo = torch.empty(T, H, D, dtype=torch.bfloat16, device=dev)
-        if fused:
-            return lambda: ops.gemm_qkv_norm_rope_append(x, w, heads=H, kv_heads=HKV, q_scale=qs, k_scale=ks,
-                                                         eps=1e-6, cos=cos, sin=sin, positions=pos, write_slots=slots,
-                                                         q_out=qo, key_pool=kp, value_pool=vp,
-                                                         rope_half_tables=half_tables)
 
-        def unfused():
+        def call():
             qkv = F.linear(x, w)
             ops.qk_norm_rope_append(qkv[:, :H * D].view(T, H, D), qkv[:, H * D:(H + HKV) * D].view(T, HKV, D),
                                     qkv[:, (H + HKV) * D:].view(T, HKV, D), q_scale=qs, k_scale=ks, eps=1e-6,
                                     cos=cos, sin=sin, positions=pos, write_slots=slots, q_out=qo, key_pool=kp,
                                     value_pool=vp)
-        return unfused
+        return call
 
     flops = 2 * T * HIDDEN * (H + 2 * HKV) * D
     return [make() for _ in range(2)], flops
@@ -299,9 +291,7 @@ def main(argv: list[str]) -> None:
         "sample": lambda: _sample(dev, g),
         "gate_up_fused": lambda: _gate_up(dev, g, True),
         "gate_up_cublas": lambda: _gate_up(dev, g, False),
-        "qkv_fused": lambda: _qkv(dev, g, True),
-        "qkv_fused_full_tables": lambda: _qkv(dev, g, True, half_tables=False),
-        "qkv_cublas": lambda: _qkv(dev, g, False),
+        "qkv_cublas": lambda: _qkv(dev, g),
         "prefix_hash": lambda: _prefix_hash(dev),
         "lm_head_argmax33": lambda: _lm_head(dev, g, 33, True),
         "lm_head_cublas33": lambda: _lm_head(dev, g, 33, False),

@@ -68,11 +68,6 @@ def rope_parameters(config: Qwen3Config) -> tuple[torch.Tensor, torch.Tensor]:
 # 128 and 1280 rows, trails it between (39 vs 30 us at 256, 87 vs 82 us at 1024) and leads
 # from 1536 rows (120 vs 126 us; 156 vs 182 us at the 2080-row tick).
 FUSED_GATE_UP_MIN_ROWS = 1280
-# Token rows from which the fused tcgen05 q|k|v + norm/RoPE/append kernel would be used. None:
-# not used. At the Qwen3-4B tick shape (2080 rows) it measured 58-62 us against 56 us for cuBLAS
-# plus the norm/RoPE/append kernel: its one-SM main loop is TMA-latency-bound (~24k cycles per
-# 128 x 256 tile) and the last tile's epilogue (norm, RoPE, scattered row writes) stays exposed.
-FUSED_QKV_MIN_ROWS: int | None = None
 # Decode-tick projections (a few to 256 token rows) stay on cuBLAS: measured at the Qwen3-4B
 # shapes with 128 rows, q|k|v 8.9 us, output 8.5, gate|up 22.4, down 16.4 (56 us per layer,
 # 0.55 of the copy peak over the 202 MB of weights), ahead of a stream-K weight-streaming tcgen05
@@ -149,19 +144,12 @@ class GroupedQueryAttention(nn.Module):
         self._qkv = _Fused(self.query, self.key, self.value)
 
     def forward(self, x: torch.Tensor, cache: PagedBatchCache, layer_index: int, cos: torch.Tensor,
-                sin: torch.Tensor, rope_half_tables: bool = False) -> torch.Tensor:
-        """``x [T, hidden]`` (already input-normed) -> attention block output ``[T, hidden]``.
-        ``rope_half_tables``: every cos/sin row's second half repeats its first."""
-        if (FUSED_QKV_MIN_ROWS is not None and x.shape[0] >= FUSED_QKV_MIN_ROWS and self.head_dim == 128
-                and x.shape[1] % 64 == 0
-                and (self.n_heads + 2 * self.n_kv_heads) % 2 == 0):
-            # One tcgen05 GEMM whose epilogue does the q/k norm, RoPE and KV append.
-            context = cache.attend_projected(layer_index, x.contiguous(), self._qkv.get(), self.q_norm.scale,
-                                             self.k_norm.scale, self.q_norm.eps, cos, sin, rope_half_tables)
-        else:
-            qkv = F.linear(x, self._qkv.get())
-            context = cache.attend_fused(layer_index, qkv, self.q_norm.scale, self.k_norm.scale, self.q_norm.eps,
-                                         cos, sin)
+                sin: torch.Tensor) -> torch.Tensor:
+        """``x [T, hidden]`` (already input-normed) -> attention block output ``[T, hidden]``:
+        one cuBLAS GEMM for q|k|v, kernel (b) (norm, RoPE, KV append), kernel (c), o-proj."""
+        qkv = F.linear(x, self._qkv.get())
+        context = cache.attend_fused(layer_index, qkv, self.q_norm.scale, self.k_norm.scale, self.q_norm.eps,
+                                     cos, sin)
         return F.linear(context.view(x.shape[0], -1), self.output.weight)
 
 
@@ -184,10 +172,6 @@ class Qwen3Model(nn.Module):
         self.output = nn.Linear(config.hidden_size, config.vocab_size, bias=False, dtype=config.dtype)
         self.output.weight = self.token_embedding.weight
         cos, sin = rope_parameters(config)
-        # Each row's second half repeats its first (duplicated angles): the fused q|k|v
-        # kernel may then read half of every row. Checked on the host tables once.
-        half = config.head_dim // 2
-        self.rope_half_tables = bool(torch.equal(cos[:, :half], cos[:, half:]) and torch.equal(sin[:, :half], sin[:, half:]))
         device = self.token_embedding.weight.device  # the device the module is being built on
         self.register_buffer("cos", cos.to(device), persistent=False)
         self.register_buffer("sin", sin.to(device), persistent=False)
@@ -287,7 +271,7 @@ class Qwen3Model(nn.Module):
         h = torch.empty_like(x)
         normed2 = torch.empty_like(x)
         for index, block in enumerate(self.blocks):
-            attn = block.attention(normed, cache, index, self.cos, self.sin, rope_half_tables=self.rope_half_tables)
+            attn = block.attention(normed, cache, index, self.cos, self.sin)
             ops.add_rmsnorm(x, attn, block.post_attention_norm.scale, eps, h, normed2)
             mlp = block.feed_forward(normed2)
             nxt = self.blocks[index + 1].input_norm.scale if index + 1 < len(self.blocks) else self.final_norm.scale

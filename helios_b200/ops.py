@@ -202,63 +202,6 @@ def lm_head_argmax(x: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | No
     return out
 
 
-def rope_gather(cos: torch.Tensor, sin: torch.Tensor, positions: torch.Tensor, *,
-                half_tables: bool) -> tuple[torch.Tensor, torch.Tensor]:
-    """Per-token rope rows for :func:`gemm_qkv_norm_rope_append`: ``[w / 4, T, 4]`` fp32 tables
-    holding ``cos[positions[t], 4g:4g+4]`` (zeros for positions outside the tables), with
-    ``w = d / 2`` when ``half_tables`` (every row's second half repeats its first), else ``d``."""
-    _need(cos, torch.float32, "cos")
-    _need(sin, torch.float32, "sin")
-    if positions.dtype != torch.long or not positions.is_cuda:
-        raise ValueError("positions must be a CUDA int64 tensor")
-    tokens, dim = positions.numel(), cos.shape[1]
-    width = dim // 2 if half_tables else dim
-    out_cos = torch.empty((width // 4, tokens, 4), dtype=torch.float32, device=cos.device)
-    out_sin = torch.empty_like(out_cos)
-    rc = lib().hb_rope_gather(cos.data_ptr(), sin.data_ptr(), cos.shape[0], dim, positions.data_ptr(), tokens, width,
-                              out_cos.data_ptr(), out_sin.data_ptr(), _stream(cos.device))
-    _native.check(rc, "hb_rope_gather")
-    return out_cos, out_sin
-
-
-def gemm_qkv_norm_rope_append(x: torch.Tensor, w_qkv: torch.Tensor, *, heads: int, kv_heads: int, q_scale, k_scale,
-                              eps: float, cos, sin, positions, write_slots: torch.Tensor, q_out: torch.Tensor,
-                              key_pool: torch.Tensor, value_pool: torch.Tensor, rope_half_tables: bool = False,
-                              gathered: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
-    """The q|k|v projection ``x [T, hidden] @ w_qkv^T`` (``w_qkv`` = [Wq; Wk; Wv]) fused with
-    kernel (b): writes the normed, rotated queries to ``q_out [T, heads, 128]`` and appends
-    the normed, rotated keys and the values to one layer's pools ``[P, page, Hkv, 128]`` at
-    ``write_slots``. Same results as ``F.linear`` followed by :func:`qk_norm_rope_append`.
-    ``gathered`` is :func:`rope_gather` of these tokens (made here when not given);
-    ``rope_half_tables`` states that each cos/sin row's second half repeats its first (as
-    :func:`helios_b200.model.rope_parameters` builds them)."""
-    _need(x, BF16, "x")
-    _need(w_qkv, BF16, "w_qkv")
-    _need(q_out, BF16, "q_out")
-    _need(key_pool, BF16, "key_pool")
-    _need(value_pool, BF16, "value_pool")
-    tokens, hidden = x.shape
-    dim = q_out.shape[-1]
-    if w_qkv.shape != ((heads + 2 * kv_heads) * dim, hidden):
-        raise ValueError("w_qkv must be [(heads + 2 kv_heads) head_dim, hidden] matching x")
-    if write_slots.dtype != torch.long:
-        raise ValueError("write_slots must be int64")
-    if cos is not None and gathered is None:
-        gathered = rope_gather(cos, sin, positions, half_tables=rope_half_tables)
-    rope_cos, rope_sin = gathered if cos is not None else (None, None)
-    width = rope_cos.shape[0] * 4 if rope_cos is not None else 0
-    if rope_cos is not None and rope_cos.shape[1] != tokens:
-        raise ValueError("gathered rope rows do not match the tokens")
-    pool_slots = key_pool.shape[0] * key_pool.shape[1]
-    rc = lib().hb_gemm_qkv_norm_rope_append(
-        x.data_ptr(), tokens, hidden, w_qkv.data_ptr(), heads, kv_heads, dim, _ptr(q_scale), _ptr(k_scale), float(eps),
-        _ptr(rope_cos), _ptr(rope_sin), width, cos.shape[0] if cos is not None else 0, _ptr(positions),
-        write_slots.data_ptr(), q_out.data_ptr(), key_pool.data_ptr(), value_pool.data_ptr(), pool_slots,
-        _stream(x.device))
-    _native.check(rc, "hb_gemm_qkv_norm_rope_append")
-    return q_out
-
-
 def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     if ids.dtype != torch.long or not ids.is_cuda or not ids.is_contiguous():
         raise ValueError("token ids must be a contiguous CUDA int64 tensor")

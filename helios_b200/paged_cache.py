@@ -498,7 +498,6 @@ class PagedBatchCache:
         self.prefill_items = out["prefill_items"]
         self.attention_counts = out["counts"] if self.capacity_mode else None
         self.total_tokens = total
-        self._rope_rows = None  # this tick's gathered rope rows, made by the first fused layer
 
     def _outputs(self, rows: int, width: int, tokens: int, logits: int) -> dict:
         """Views of two reusable device buffers sized for this tick."""
@@ -562,29 +561,6 @@ class PagedBatchCache:
         ops.qk_norm_rope_append(q, k, v, q_scale=q_scale, k_scale=k_scale, eps=eps, cos=cos, sin=sin,
                                 positions=self.token_positions, write_slots=self.write_slots, q_out=q_rot,
                                 key_pool=pool.keys[layer], value_pool=pool.values[layer])
-        out = torch.empty_like(q_rot)
-        return ops.paged_attention(q_rot, pool.keys[layer], pool.values[layer], self, out)
-
-    def attend_projected(self, layer: int, x: torch.Tensor, w_qkv: torch.Tensor, q_scale: torch.Tensor,
-                         k_scale: torch.Tensor, eps: float, cos: torch.Tensor, sin: torch.Tensor,
-                         rope_half_tables: bool = False) -> torch.Tensor:
-        """As :meth:`attend_fused`, from the normed hidden rows ``x [T, hidden]`` and the fused
-        ``[Wq; Wk; Wv]`` weight: the projection and kernel (b) run as one tcgen05 GEMM whose
-        epilogue writes the rotated queries and the pool pages. Returns ``[T, H, d]``."""
-        config, pool = self.pool.config, self.pool
-        tokens = x.shape[0]
-        if tokens != self.total_tokens:
-            raise ValueError("Packed attention expects one flattened token dimension.")
-        q_rot = torch.empty((tokens, config.n_heads, config.head_dim), dtype=x.dtype, device=x.device)
-        key = (cos.data_ptr(), sin.data_ptr(), bool(rope_half_tables))
-        if getattr(self, "_rope_rows", None) is None or self._rope_rows[0] != key:
-            # Once per tick: every layer rotates the same tokens by the same tables.
-            self._rope_rows = (key, ops.rope_gather(cos, sin, self.token_positions, half_tables=rope_half_tables))
-        ops.gemm_qkv_norm_rope_append(x, w_qkv, heads=config.n_heads, kv_heads=config.n_kv_heads, q_scale=q_scale,
-                                      k_scale=k_scale, eps=eps, cos=cos, sin=sin, positions=self.token_positions,
-                                      write_slots=self.write_slots, q_out=q_rot, key_pool=pool.keys[layer],
-                                      value_pool=pool.values[layer], rope_half_tables=rope_half_tables,
-                                      gathered=self._rope_rows[1])
         out = torch.empty_like(q_rot)
         return ops.paged_attention(q_rot, pool.keys[layer], pool.values[layer], self, out)
 

@@ -264,37 +264,6 @@ HB_API int hb_prefix_index_lookup(const uint32_t* table, int32_t slots, const ui
                                   const int64_t* block_offsets, const int32_t* full_blocks, int32_t prompts,
                                   int32_t* matched, int32_t* values, cudaStream_t stream);
 
-/*
- * Per-token rope rows for hb_gemm_qkv_norm_rope_append: out[g][t][0..3] = table[positions[t]][4g ..
- * 4g + 3] (fp32, zeros where the position is outside [0, rope_rows)) for g < width / 4, for the
- * cos and sin tables [rope_rows][head_dim] of apply_rope (src/helios/runtime/qwen3/layers.py:
- * 43-72). width = head_dim / 2 when every row's second half repeats its first (the tables of
- * layers.py:43-51 are built that way), else head_dim. out_cos / out_sin hold width * tokens
- * floats each. Needs head_dim == 128.
- */
-HB_API int hb_rope_gather(const float* cos, const float* sin, int64_t rope_rows, int32_t head_dim,
-                          const int64_t* positions, int32_t tokens, int32_t width, float* out_cos, float* out_sin,
-                          cudaStream_t stream);
-
-/*
- * q|k|v projection fused with kernel (b) on tcgen05 tensor cores. Replaces, per decoder layer,
- * query(x), key(x), value(x) (GroupedQueryAttention.forward, src/helios/runtime/qwen3/
- * layers.py:132-146) followed by hb_qk_norm_rope_append's q/k RMSNorm, RoPE and KV append,
- * for x bf16 [m][k] (rows contiguous) and the fused weight w_qkv bf16 [(heads + 2 kv_heads)
- * head_dim][k] (query rows, then key rows, then value rows). rope_cos / rope_sin are the
- * hb_rope_gather rows of these m tokens (width rope_width), or null for no rotation; positions
- * and rope_rows are still checked per token. The other arguments and the results are those of
- * hb_qk_norm_rope_append with q_out bf16 [m][heads][head_dim] (required) and the pools
- * [pool_slots][kv_heads][head_dim]; the projection output is never written. Needs
- * head_dim == 128, k % 64 == 0 and heads + 2 kv_heads even.
- */
-HB_API int hb_gemm_qkv_norm_rope_append(const void* x, int32_t m, int32_t k, const void* w_qkv, int32_t heads,
-                                        int32_t kv_heads, int32_t head_dim, const float* q_scale,
-                                        const float* k_scale, float eps, const float* rope_cos,
-                                        const float* rope_sin, int32_t rope_width, int64_t rope_rows,
-                                        const int64_t* positions, const int64_t* write_slots, void* q_out,
-                                        void* key_pool, void* value_pool, int64_t pool_slots, cudaStream_t stream);
-
 /* Token-embedding gather (Qwen3Model._forward_packed, src/helios/runtime/qwen3/model.py:97). */
 HB_API int hb_embedding(const int64_t* ids, const void* table, int64_t vocab, void* out, int64_t tokens,
                         int32_t hidden, cudaStream_t stream);
