@@ -175,9 +175,16 @@ int launch_fused_gemm(const typename Epi::Params& p, const CUtensorMap& amap, co
   return check_launch(what);
 }
 
-// RMSNorm launch: warp per row up to hidden 4096, CTA per row beyond.
+// RMSNorm launch: a CTA per row for few rows or hidden beyond 4096, else a warp per row.
 int launch_rmsnorm(const hb::RowNormParams& p, cudaStream_t stream, const char* what) {
   const int nvec = p.hidden / 8;
+  // Few rows (a decode tick's): a CTA per row, so each row's loads, sum and stores are spread
+  // over 256 threads instead of one warp's long dependent chain (the launch is latency-bound).
+  const int sms = sm_count();
+  if (sms > 0 && p.rows <= 2 * sms) {
+    hb::rmsnorm_kernel<<<p.rows, hb::kRowThreads, 0, stream>>>(p);
+    return check_launch(what);
+  }
   const unsigned warp_blocks = static_cast<unsigned>((p.rows + hb::kNormWarps - 1) / hb::kNormWarps);
   if (nvec <= 32 * 4)
     hb::rmsnorm_warp_kernel<4><<<warp_blocks, hb::kNormWarps * 32, 0, stream>>>(p);

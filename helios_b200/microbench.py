@@ -52,7 +52,7 @@ def graph_time(calls, reps: int = 24, replays: int = 5) -> float:
     return sorted(times)[len(times) // 2]
 
 
-def _norm_rope(dev, g):
+def _norm_rope(dev, g, T=T):
     cos, sin = torch.randn(40960, D, device=dev), torch.randn(40960, D, device=dev)
     qs, ks = torch.rand(D, device=dev) + 0.5, torch.rand(D, device=dev) + 0.5
     pages = 600
@@ -74,7 +74,7 @@ def _norm_rope(dev, g):
     return [make() for _ in range(4)], T * (H + 2 * HKV) * D * 2 * 2
 
 
-def _swiglu(dev, g):
+def _swiglu(dev, g, T=T):
     def make():
         gu = torch.randn(T, 2 * INTER, device=dev, generator=g).to(torch.bfloat16)
         out = torch.empty(T, INTER, dtype=torch.bfloat16, device=dev)
@@ -83,7 +83,7 @@ def _swiglu(dev, g):
     return [make() for _ in range(4)], T * INTER * 3 * 2
 
 
-def _add_rmsnorm(dev, g):
+def _add_rmsnorm(dev, g, T=T):
     scale = torch.rand(HIDDEN, device=dev) + 0.5
 
     def make():
@@ -281,6 +281,10 @@ def main(argv: list[str]) -> None:
         "norm_rope": lambda: _norm_rope(dev, g),
         "swiglu": lambda: _swiglu(dev, g),
         "add_rmsnorm": lambda: _add_rmsnorm(dev, g),
+        # the same row kernels at a decode tick's 128 rows: latency-bound
+        "norm_rope128": lambda: _norm_rope(dev, g, 128),
+        "swiglu128": lambda: _swiglu(dev, g, 128),
+        "add_rmsnorm128": lambda: _add_rmsnorm(dev, g, 128),
         "prefill": lambda: _attention(dev, [0], [2048], 1),
         **{f"proj_{name}{m}": (lambda m=m, n=n, k=k: _projection(dev, g, m, n, k))
            for name, n, k in (("qkv", 6144, 2560), ("o", 2560, 4096), ("gateup", 19456, 2560), ("down", 2560, 9728))
