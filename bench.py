@@ -671,6 +671,8 @@ def run_b200(args) -> None:
     rank, size, local = replicas.world()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if size > 1:  # N replicas share the host's cores (their engines' host work in config 5)
+        torch.set_num_threads(max(1, (os.cpu_count() or 1) // size))
     # Rank 0 alone runs the rooflines and configs 4 and the reference's GPU path while the
     # others wait at a barrier, so the group's timeout leaves room for those stages.
     replicas.init("nccl" if size > 1 else "gloo", timeout_s=600.0)
