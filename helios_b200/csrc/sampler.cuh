@@ -33,6 +33,10 @@ constexpr int kSampleUnroll = 4;  // groups a lane loads before using any (loads
 // 2^-23 of the partition function, the rounding of its own fp32 sum, so the cut is the
 // one the full sums give; the kept mass and the draw still sum every kept token.
 constexpr float kNegligibleWeight = 9.094947e-13f;  // 2^-40
+// Top-p rows: tokens whose weight can matter (logit >= x_floor, a superset of the weights
+// above kNegligibleWeight) are collected in one pass; when at most this many, the cut and the
+// draw run on that list in shared memory instead of over the whole row again.
+constexpr int kSampleCand = 4096;
 
 struct SampleParams {
   const __nv_bfloat16* logits;  // [rows, row_stride]
@@ -158,8 +162,125 @@ __device__ __forceinline__ int warp_find_cut(const double* hist, double base, do
   return __shfl_sync(0xffffffffu, found, src);
 }
 
+// Exclusive prefix of one value per thread over the block in thread order; also the total.
+template <typename T>
+__device__ __forceinline__ T block_exclusive_scan(T v, T* red, T* total) {
+  const T incl = warp_inclusive_scan(v);
+  const T warp_total = __shfl_sync(0xffffffffu, incl, 31);
+  const T before = warps_exclusive_scan(warp_total, red, total);
+  return before + incl - v;
+}
+
+// Ascending bitonic sort of n (<= kSampleCand) entries in shared memory, padded to a power of
+// two with entries that sort last; called by every thread of the block.
+__device__ void block_sort(unsigned long long* a, int n) {
+  int n2 = 2;
+  while (n2 < n) n2 <<= 1;
+  for (int i = n + static_cast<int>(threadIdx.x); i < n2; i += kSampleThreads) a[i] = ~0ull;
+  __syncthreads();
+  for (int k = 2; k <= n2; k <<= 1)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < n2; i += kSampleThreads) {
+        const int x = i ^ j;
+        if (x > i) {
+          const unsigned long long u = a[i], v = a[x];
+          if ((u > v) == ((i & k) == 0)) {
+            a[i] = v;
+            a[x] = u;
+          }
+        }
+      }
+      __syncthreads();
+    }
+}
+
+__device__ __forceinline__ uint32_t key_to_bits(uint32_t key) {
+  return (key & 0x8000u) ? (key & 0x7FFFu) : (~key & 0xFFFFu);
+}
+
+// The cut and the draw of a top-p row from its candidate list (every token whose weight can
+// matter; see kSampleCand), with the rules of the whole-row passes: only weights above
+// kNegligibleWeight count toward the masses; in descending probability order (ties by
+// ascending index) a token is kept when the mass before it is at most top_p * Z (the first
+// always); the kept tokens are visited in index order and the first whose running mass exceeds
+// u * kept mass is drawn (the last kept one when rounding leaves none). The list is sorted by
+// (key descending, index ascending) for the cut, then its kept prefix by index for the draw.
+// Every thread of the block calls it. Returns false, with nothing written, when the cut keeps
+// every candidate: tokens outside the list may then be kept too, which the whole-row passes
+// decide.
+__device__ bool sample_candidates(const SampleParams& p, int row, int nc, unsigned long long* cand, float top_p,
+                                  float T, float m, int* ired, double* dred, int* chosen) {
+  const int tid = threadIdx.x;
+  auto weight = [&](uint32_t bits) { return expf(__fdiv_rn(bits_to_float(bits), T) - m); };
+
+  // Descending key, ascending index: (0xFFFF - key) << 32 | index, ascending.
+  for (int i = tid; i < nc; i += kSampleThreads) {
+    const unsigned long long c = cand[i];
+    const uint32_t key = bf16_key_bits(static_cast<uint32_t>(c & 0xFFFFu));
+    cand[i] = (static_cast<unsigned long long>(0xFFFFu - key) << 32) | (c >> 16);
+  }
+  __syncthreads();
+  block_sort(cand, nc);
+
+  // Exclusive mass before each entry in that order, over a contiguous slice per thread.
+  const int per = (nc + kSampleThreads - 1) / kSampleThreads;
+  const int lo = min(nc, tid * per), hi = min(nc, lo + per);
+  double mass = 0.0;
+  for (int i = lo; i < hi; ++i) {
+    const float w = weight(key_to_bits(0xFFFFu - static_cast<uint32_t>(cand[i] >> 32)));
+    if (w > kNegligibleWeight) mass += static_cast<double>(w);
+  }
+  double Z;
+  double before = block_exclusive_scan(mass, dred, &Z);
+  const double t = static_cast<double>(top_p) * Z;
+  // Kept entries form a prefix: the count is the number with mass-before <= t (at least 1).
+  int keep = 0;
+  for (int i = lo; i < hi; ++i) {
+    const float w = weight(key_to_bits(0xFFFFu - static_cast<uint32_t>(cand[i] >> 32)));
+    if (before <= t || i == 0) ++keep;
+    if (w > kNegligibleWeight) before += static_cast<double>(w);
+  }
+  const int n_keep = block_reduce(keep, [](int a, int b) { return a + b; }, ired);
+  if (n_keep >= nc) return false;
+
+  // The kept prefix back to (index << 16 | bits), sorted by index.
+  for (int i = tid; i < n_keep; i += kSampleThreads) {
+    const unsigned long long c = cand[i];
+    const uint32_t bits = key_to_bits(0xFFFFu - static_cast<uint32_t>(c >> 32));
+    cand[i] = ((c & 0xFFFFFFFFull) << 16) | bits;
+  }
+  __syncthreads();
+  block_sort(cand, n_keep);
+  const int per2 = (n_keep + kSampleThreads - 1) / kSampleThreads;
+  const int lo2 = min(n_keep, tid * per2), hi2 = min(n_keep, lo2 + per2);
+  double kept_mass = 0.0;
+  for (int i = lo2; i < hi2; ++i) kept_mass += static_cast<double>(weight(static_cast<uint32_t>(cand[i] & 0xFFFFu)));
+  double kept_total;
+  const double kept_before = block_exclusive_scan(kept_mass, dred, &kept_total);
+  const double draw = static_cast<double>(p.uniforms[row]) * kept_total;
+  if (tid == 0) *chosen = static_cast<int>(cand[n_keep - 1] >> 16);  // the last kept (rounding)
+  __syncthreads();
+  if (kept_mass > 0.0 && kept_before <= draw && draw < kept_before + kept_mass) {
+    double run = kept_before;
+    for (int i = lo2; i < hi2; ++i) {
+      run += static_cast<double>(weight(static_cast<uint32_t>(cand[i] & 0xFFFFu)));
+      if (run > draw) {
+        atomicMin(chosen, static_cast<int>(cand[i] >> 16));
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) p.out[row] = *chosen;
+  return true;
+}
+
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) {
-  __shared__ float whist[kSampleWarps][256];  // per-warp mass histograms
+  __shared__ union {
+    float whist[kSampleWarps][256];         // per-warp mass histograms (whole-row passes)
+    unsigned long long cand[kSampleCand];   // candidates: token index << 16 | logit bits
+  } sh;
+  float (*whist)[256] = sh.whist;
   __shared__ double hist[256];                // their sum over the warps
   __shared__ float fred[32];
   __shared__ int ired[32];
@@ -168,6 +289,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) 
   __shared__ double cut_mass_above, cut_target;
   __shared__ int cut_found;
   __shared__ int chosen;
+  __shared__ int ncand;
 
   const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const __nv_bfloat16* lg = p.logits + static_cast<int64_t>(row) * p.row_stride;
@@ -177,7 +299,9 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) 
   const int gpw = (groups + kSampleWarps - 1) / kSampleWarps;  // groups per warp segment
   const int g_begin = min(groups, warp * gpw), g_end = min(groups, g_begin + gpw);
 
-  // Pass 1: max and its first index.
+  const float T = p.temperature[row];
+  const bool greedy = !(T > 0.f);
+  // Pass 1: max (and, for a greedy row, its first index).
   float mx = -INFINITY;
   int arg = INT_MAX;
   for (int base = g_begin; base < g_end; base += 32 * kSampleUnroll) {
@@ -185,18 +309,29 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) 
     int n[kSampleUnroll];
     load_groups(lg, base, g_end, V, vec_ok, b, n);
 #pragma unroll
-    for (int u = 0; u < kSampleUnroll; ++u)
+    for (int u = 0; u < kSampleUnroll; ++u) {
+      if (greedy) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float v = bits_to_float(b[u][e]);
-        if (e < n[u] && v > mx) { mx = v; arg = 8 * (base + 32 * u + lane) + e; }  // indices visited in order
+        for (int e = 0; e < 8; ++e) {
+          const float v = bits_to_float(b[u][e]);
+          if (e < n[u] && v > mx) { mx = v; arg = 8 * (base + 32 * u + lane) + e; }  // indices visited in order
+        }
+      } else if (n[u] == 8) {
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = bits_to_float(b[u][e]);
+        mx = fmaxf(mx, fmaxf(fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3])), fmaxf(fmaxf(v[4], v[5]), fmaxf(v[6], v[7]))));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (e < n[u]) mx = fmaxf(mx, bits_to_float(b[u][e]));
       }
+    }
   }
   const float gmax = block_reduce(mx, [](float a, float b) { return fmaxf(a, b); }, fred);
   if (mx != gmax) arg = INT_MAX;
   const int garg = block_reduce(arg, [](int a, int b) { return min(a, b); }, ired);
-  const float T = p.temperature[row];
-  if (!(T > 0.f)) {
+  if (greedy) {
     if (tid == 0) p.out[row] = garg;
     return;
   }
@@ -206,6 +341,35 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) 
   // Logits below x_floor have weight < e^-28 < kNegligibleWeight (x / T - m < -28 up to the
   // rounding of the division), so the histogram passes skip them without computing it.
   const float x_floor = T * (m - 28.f);
+
+  if (top_p < 1.f) {
+    // Candidate pass: every token with logit >= x_floor (warp-aggregated appends).
+    if (tid == 0) ncand = 0;
+    __syncthreads();
+    for (int base = g_begin; base < g_end; base += 32 * kSampleUnroll) {
+      uint32_t b[kSampleUnroll][8];
+      int n[kSampleUnroll];
+      load_groups(lg, base, g_end, V, vec_ok, b, n);
+#pragma unroll
+      for (int u = 0; u < kSampleUnroll; ++u)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const bool c = e < n[u] && bits_to_float(b[u][e]) >= x_floor;
+          const unsigned mask = __ballot_sync(0xffffffffu, c);
+          if (mask == 0u) continue;  // warp-uniform
+          const int leader = __ffs(mask) - 1;
+          int slot = 0;
+          if (lane == leader) slot = atomicAdd(&ncand, __popc(mask));
+          slot = __shfl_sync(0xffffffffu, slot, leader) + __popc(mask & ((1u << lane) - 1u));
+          if (c && slot < kSampleCand)
+            sh.cand[slot] = (static_cast<unsigned long long>(8 * (base + 32 * u + lane) + e) << 16) | b[u][e];
+        }
+    }
+    __syncthreads();
+    const int nc = ncand;
+    if (nc <= kSampleCand && sample_candidates(p, row, nc, sh.cand, top_p, T, m, ired, dred, &chosen)) return;
+    __syncthreads();  // the candidate list's memory holds the histograms from here on
+  }
 
   uint32_t key_star = 0;  // tokens with key > key_star are kept
   int n_tie_keep = 0;     // how many tokens with key == key_star are kept (lowest indices)
