@@ -51,13 +51,23 @@ def _flatten(token_lists: Sequence[Sequence[int]], block_size: int):
     block_offsets = np.zeros(len(lengths) + 1, dtype=np.int64)
     np.cumsum(blocks, out=block_offsets[1:])
     full = np.array([n // block_size for n in lengths], dtype=np.int32)
-    parts = [np.asarray(tokens, dtype=np.int64).reshape(-1) if isinstance(tokens, (np.ndarray, torch.Tensor))
-             else np.fromiter(tokens, dtype=np.int64, count=n) for tokens, n in zip(token_lists, lengths)]
-    flat = np.concatenate(parts) if parts else np.zeros(0, dtype=np.int64)
-    if flat.size and (flat.min() < 0 or flat.max() > _MAX_TOKEN):
-        raise ValueError("Token IDs must be non-negative integers." if flat.min() < 0
-                         else "Token IDs above 2^31 - 1 are not supported.")
-    return flat.astype(np.int32), offsets, block_offsets, full
+    flat = np.empty(int(offsets[-1]), dtype=np.int32)
+    for tokens, lo, n in zip(token_lists, offsets[:-1].tolist(), lengths):
+        if not n:
+            continue
+        if isinstance(tokens, (np.ndarray, torch.Tensor)):
+            part = np.asarray(tokens).reshape(-1)
+            if part.dtype.kind not in "iu":
+                raise ValueError("Token IDs must be non-negative integers.")
+        else:
+            part = np.fromiter(tokens, dtype=np.int64, count=n)
+        if np.iinfo(part.dtype).max > _MAX_TOKEN and part.max() > _MAX_TOKEN:
+            raise ValueError("Token IDs must be non-negative integers." if part.min() < 0
+                             else "Token IDs above 2^31 - 1 are not supported.")
+        flat[lo:lo + n] = part  # every value now fits int32 unchanged
+    if flat.size and flat.min() < 0:
+        raise ValueError("Token IDs must be non-negative integers.")
+    return flat, offsets, block_offsets, full
 
 
 class _PinnedStaging:
@@ -103,20 +113,26 @@ def _upload(arrays: Sequence[np.ndarray], device: torch.device) -> list[torch.Te
     return out
 
 
-def _hash(token_lists, block_size, device):
+def _hash(token_lists, block_size, device, words_per_block: int = 0, words: int = 0):
+    """Digests of every block. They lead a device buffer (returned last) with room after them
+    for ``words_per_block`` int32 per block plus ``words`` more, which the caller fills, so a
+    single download brings everything back."""
     tokens, offsets, block_offsets, full = _flatten(token_lists, block_size)
     d_tokens, d_offsets, d_boffs, d_full = _upload([tokens, offsets, block_offsets, full], device)
     blocks = int(block_offsets[-1])
-    digests = torch.empty((blocks, 32), dtype=torch.uint8, device=device)
+    buffer = torch.empty(blocks * 32 + 4 * (words_per_block * blocks + words), dtype=torch.uint8, device=device)
+    digests = buffer[:blocks * 32].view(blocks, 32)
     if blocks:  # no tokens at all: nothing to key (and empty buffers have no address)
         rc = _lib().hb_hash_token_blocks(d_tokens.data_ptr(), d_offsets.data_ptr(), len(token_lists), block_size,
                                          d_boffs.data_ptr(), digests.data_ptr(), _stream(device))
         _native.check(rc, "hb_hash_token_blocks")
-    return digests, d_boffs, d_full, block_offsets, full
+    return digests, d_boffs, d_full, block_offsets, full, buffer
 
 
 def _hex_rows(digests: np.ndarray, lo: int, hi: int) -> list[str]:
-    return [bytes(row).hex() for row in digests[lo:hi]]
+    """Hex keys of digest rows lo..hi of a [blocks, 32] uint8 array."""
+    text = digests[lo:hi].tobytes().hex()
+    return [text[64 * i:64 * (i + 1)] for i in range(hi - lo)]
 
 
 def hash_token_blocks(token_lists: Sequence[Sequence[int]], block_size: int,
@@ -124,7 +140,7 @@ def hash_token_blocks(token_lists: Sequence[Sequence[int]], block_size: int,
     """Hex keys of every block of every prompt (partial last blocks included), equal to
     ``[b.hash for b in build_token_blocks(tokens, block_size)]`` of the reference."""
     device = device or torch.device("cuda", torch.cuda.current_device())
-    digests, _, _, block_offsets, _ = _hash(token_lists, block_size, device)
+    digests, _, _, block_offsets, _, _ = _hash(token_lists, block_size, device)
     host = digests.cpu().numpy()
     return [_hex_rows(host, int(block_offsets[p]), int(block_offsets[p + 1])) for p in range(len(token_lists))]
 
@@ -187,22 +203,22 @@ class DevicePrefixIndex:
     def lookup(self, token_lists: Sequence[Sequence[int]]) -> list[tuple[list[str], list[int]]]:
         """Per prompt, the keys and values of its leading full blocks that are stored, up to the
         first that is not (``PrefixCache.longest_prefix``'s walk)."""
-        digests, d_boffs, d_full, block_offsets, full = _hash(token_lists, self.block_size, self.device)
         prompts = len(token_lists)
-        matched = torch.zeros(max(prompts, 1), dtype=torch.int32, device=self.device)
-        values = torch.empty(max(int(block_offsets[-1]), 1), dtype=torch.int32, device=self.device)
-        if int(block_offsets[-1]) == 0:
+        # Digests, values and match counts side by side, so one download brings all three back.
+        digests, d_boffs, d_full, block_offsets, full, out = _hash(token_lists, self.block_size, self.device,
+                                                                   words_per_block=1, words=prompts)
+        blocks = int(block_offsets[-1])
+        if blocks == 0:
             return [([], []) for _ in range(prompts)]
+        values = out[blocks * 32:blocks * 36].view(torch.int32)
+        matched = out[blocks * 36:].view(torch.int32)  # every entry written by the kernel
         rc = _lib().hb_prefix_index_lookup(self.table.data_ptr(), self.slots, digests.data_ptr(), d_boffs.data_ptr(),
                                            d_full.data_ptr(), prompts, matched.data_ptr(), values.data_ptr(),
                                            _stream(self.device))
         _native.check(rc, "hb_prefix_index_lookup")
-        counts = matched[:prompts].cpu().numpy()
-        vals = values.cpu().numpy()
-        host = digests.cpu().numpy()
-        out = []
-        for p in range(prompts):
-            lo = int(block_offsets[p])
-            n = int(counts[p])
-            out.append((_hex_rows(host, lo, lo + n), vals[lo:lo + n].tolist()))
-        return out
+        raw = out.cpu().numpy()
+        host = raw[:blocks * 32].reshape(blocks, 32)
+        vals = raw[blocks * 32:blocks * 36].view(np.int32)
+        counts = raw[blocks * 36:].view(np.int32).tolist()
+        starts = block_offsets[:-1].tolist()
+        return [(_hex_rows(host, lo, lo + n), vals[lo:lo + n].tolist()) for lo, n in zip(starts, counts)]

@@ -117,7 +117,7 @@ def config4(steps: int = 128, share: bool = True, device: torch.device | None = 
             # The prompts as a tokenizer hands them over (int32 arrays): the lookup then needs
             # no per-token conversion of Python ints on the host.
             arrays = [np.asarray(p, dtype=np.int32) for p in prompts]
-            index.lookup(arrays[:2])  # first call: pinned staging and kernel set-up, untimed
+            index.lookup(arrays)  # first call: sizes the reused pinned staging, loads the kernels; untimed
             torch.cuda.synchronize(device)
             # Admission: one device lookup for all 128 prompts, then aliasing restores.
             start, end = _cuda_timer(device)
