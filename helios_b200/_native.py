@@ -42,15 +42,15 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "hb_last_error": (ctypes.c_char_p, []),
     "hb_device_status": (c_int, [ctypes.POINTER(c_uint32), c_int]),
     "hb_selftest_wait_timeout": (c_int, [I64, P, P]),
-    "hb_tick_pack": (c_int, [P, I32, P, I32, P, I32, I32, I32, I32, I32, I32, I32, I32, I32,
-                             P, P, P, P, P, P, P, P, I32, P, I32, P, I32, P, P, P]),
+    "hb_tick_pack": (c_int, [P, I32, P, I32, P, I32, I32, I32, I32, I32, I32, I32, I32, I32, I32,
+                             P, P, P, P, P, P, P, P, I32, P, I32, P, I32, P, I32, P, P, P]),
     "hb_qk_norm_rope_append": (c_int, [P, I64, I64, P, I64, I64, P, I64, I64, P, P, F32, P, P, I64, P, P,
                                        P, P, P, I64, I32, I32, I32, I32, P]),
     "hb_attention_workspace_bytes": (c_size_t, [I32, I32, I32]),
-    "hb_paged_attention": (c_int, [P, P, P, I64, I32, P, I32, P, P, I32, P, P, I32, P, I32, P, I32, I32, I32, I32,
-                                   I32, I32, F32, P, c_size_t, P, P]),
+    "hb_paged_attention": (c_int, [P, P, P, I64, I32, P, I32, P, P, I32, P, P, I32, P, I32, P, I32, P, I32, I32,
+                                   I32, I32, I32, I32, F32, P, c_size_t, P, P]),
     "hb_paged_attention_static_workspace": (c_int, [P, P, P, I64, I32, P, I32, P, P, I32, P, P, I32, P, I32, P, I32,
-                                                    I32, I32, I32, I32, I32, F32, P, P]),
+                                                    P, I32, I32, I32, I32, I32, I32, F32, P, P]),
     "hb_rmsnorm": (c_int, [P, I64, P, P, F32, P, I32, I32, P]),
     "hb_add_rmsnorm": (c_int, [P, P, P, F32, P, P, I32, I32, P]),
     "hb_swiglu": (c_int, [P, P, I64, I64, P]),

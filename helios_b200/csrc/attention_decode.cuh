@@ -5,8 +5,9 @@
 // window_size=(-1, 0), num_splits=1), src/helios/runtime/qwen3/paged_cache.py:501-520;
 // PagedBatchCache.attend, :301-333). The reference runs with num_splits=1, which
 // leaves most SMs idle when a tick holds few long decode rows; here the work unit is
-// (row, split of split_keys keys, KV head), or (group of rows sharing a prefix, split of the
-// prefix keys, KV head): see the decode item layout in tick_pack.cuh.
+// (row, split of split_keys keys, KV head): see the decode item layout in tick_pack.cuh. Keys
+// that rows share through restored pages run as prefix items on the tensor cores instead
+// (attention_prefill.cuh); their records join the rows' own splits in the combine.
 //
 // Semantics (bottom-right causal, as the reference's window_size=(-1, 0)): query
 // i of a row with `count` queries and `end = seqused_k` keys sits at key position
@@ -34,8 +35,6 @@
 //                             tensor-bound).
 #pragma once
 
-#include <climits>
-
 #include "hb_common.cuh"
 
 namespace hb {
@@ -46,20 +45,27 @@ struct AttentionParams {
   const int32_t* block_table;  // [B, W]
   const int32_t* cu_seq_q;     // [B+1]
   const int32_t* seqused_k;    // [B]
-  const int32_t* decode_items;   // [n][6] row, first key, end key, record or prefix split, splits, group rows
+  const int32_t* decode_items;   // [n][6] row, first key, end key, record base, splits of the row, 0
   const int32_t* row_records;    // [rows+1] first partial record of each row
   int32_t num_rows;
   int32_t record_capacity;       // partial records the workspace holds
   const int32_t* prefill_items;  // [n][3] row, query start of tile 2i, of tile 2i+1 or -1
-  // Optional device counts {decode items, prefill pairs, partial records} written by the
-  // tick-pack kernel: when set, grids are sized to capacities and CTAs past a count exit
-  // (a launch that stays valid, e.g. in a CUDA graph, while the work list changes).
+  // [n][5] first row, rows, first key, end key, prefix split index: query tiles of the single
+  // tokens of consecutive rows sharing a prefix, against one split of the shared keys
+  const int32_t* prefix_items;
+  // Optional device counts {decode items, prefill pairs, partial records, prefix items}
+  // written by the tick-pack kernel: when set, grids are sized to capacities and CTAs past a
+  // count exit (a launch that stays valid, e.g. in a CUDA graph, while the work list changes).
   const int32_t* counts;
   // Set when the prefill kernel is launched right behind the decode kernel (programmatic
   // dependent launch): it then reads q, K and V without waiting (the decode kernel waited
   // for them before triggering), and one of its CTAs waits for the decode grid before
   // exiting, so the prefill grid completes after the decode grid.
   int32_t prefill_after_decode;
+  // Set when the (per-unit) decode grid is launched right behind the prefix grid: it reads q,
+  // K and V without waiting (the prefix grid waited for them before triggering), and its last
+  // CTA waits for the prefix grid, so the decode grid completes after it.
+  int32_t decode_after_prefix;
   int32_t num_decode;   // decode items (without counts)
   int32_t decode_ctas;  // decode CTAs that stay when prefill work runs beside the decode grid
   // The next unclaimed decode unit: zero before the decode grid, reset to zero by the
@@ -69,6 +75,7 @@ struct AttentionParams {
   float* ws_lse;   // [records, H]
   int32_t width, num_pages, page_size, heads, kv_heads, split_keys, tokens;
   int32_t num_prefill;  // prefill items (the kernel walks them from the last, heaviest, first)
+  int32_t num_prefix;   // prefix items (without counts)
   float scale_log2;  // softmax scale * log2(e)
 };
 
@@ -88,18 +95,16 @@ constexpr int kMergeStride = 132;  // floats per row of the split merge scratch 
 // The key-split merge writes the accumulators of at most 3 warps into one stage.
 static_assert((kDecConsumerWarps - 1) * 16 * kMergeStride * 4 <= kDecStageBytes, "merge scratch fits a stage");
 
-// What a consumer warp needs to know about its unit. A group unit (group > 0) holds the
-// single query token of rows row .. row + group - 1 against their shared prefix keys: no
-// causal mask inside the prefix, and query row j writes record row_records[row + j / GROUP]
-// + split (the prefix split index).
+// What a consumer warp needs to know about its unit.
 struct DecodeUnit {
-  int h, row, q0, count, end, kb, ke, n_tiles, rec, nsplit, group;
+  int h, row, q0, count, end, kb, ke, n_tiles, rec, nsplit;
   int qrows, key_split, kpw, mt, kpart;
 };
 
 constexpr int kDecodeItemInts = 6;
+constexpr int kPrefixItemInts = 5;
 
-// From decode item `it` (the tick-pack layout), q0 / count / end of its row or group.
+// From decode item `it` (the tick-pack layout), q0 / count / end of its row.
 template <int GROUP>
 __device__ __forceinline__ DecodeUnit decode_unit(const AttentionParams& p, int h, const int4& ia, const int2& ib,
                                                   int q0, int count, int end, int consumer_warp) {
@@ -110,7 +115,6 @@ __device__ __forceinline__ DecodeUnit decode_unit(const AttentionParams& p, int 
   u.ke = ia.z;
   u.rec = ia.w;
   u.nsplit = ib.x;
-  u.group = ib.y;
   u.q0 = q0;
   u.count = count;
   u.end = end;
@@ -124,30 +128,22 @@ __device__ __forceinline__ DecodeUnit decode_unit(const AttentionParams& p, int 
   return u;
 }
 
-// The decode item as two vectors plus its row's (or group's) query range and key end.
+// The decode item as two vectors plus its row's query range and key end.
 __device__ __forceinline__ void decode_item(const AttentionParams& p, int index, int4& ia, int2& ib, int& q0,
                                             int& count, int& end) {
   const int32_t* it = p.decode_items + kDecodeItemInts * index;
   ia = make_int4(it[0], it[1], it[2], it[3]);
   ib = make_int2(it[4], it[5]);
   q0 = p.cu_seq_q[ia.x];
-  count = ib.y > 0 ? ib.y : p.cu_seq_q[ia.x + 1] - q0;
-  end = ib.y > 0 ? ia.z : p.seqused_k[ia.x];
-  if (ib.y > 0) {  // a group's rows and their single tokens must exist
-    const int limit = max(0, min(p.num_rows - ia.x, p.tokens - q0));
-    if (count > limit) {
-      raise_status(kStatusBadRow);
-      count = limit;
-      ib.y = limit;
-    }
-  }
+  count = p.cu_seq_q[ia.x + 1] - q0;
+  end = p.seqused_k[ia.x];
 }
 
-// Key position limit of query row j (bottom-right causal); group units see every key.
+// Key position limit of query row j (bottom-right causal).
 template <int GROUP>
 __device__ __forceinline__ int decode_qpos(const DecodeUnit& u, int j) {
   if (j >= u.qrows) return -1;
-  return u.group > 0 ? INT_MAX : u.end - u.count + j / GROUP;
+  return u.end - u.count + j / GROUP;
 }
 
 // Query A-fragments for rows mt*16 + g4 and +8 of the unit: 8 k-steps of 16 dims.
@@ -344,21 +340,7 @@ __device__ __forceinline__ void decode_store(const AttentionParams& p, const Dec
     const float m = half ? m_b : m_a, l = half ? l_b : l_a;
     const float inv = l > 0.f ? 1.f / l : 0.f;
     const int tq = j / GROUP, head = u.h * GROUP + j % GROUP;
-    if (u.group > 0) {  // member row u.row + tq, prefix split u.rec
-      const int r = p.row_records[u.row + tq] + u.rec;
-      if (r < 0 || r >= p.record_capacity) {
-        raise_status(kStatusBadRow);
-        continue;
-      }
-      const int64_t rec = static_cast<int64_t>(r) * p.heads + head;
-      float* o = p.ws_out + rec * D;
-#pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        const int col = n * 8 + 2 * c4;
-        *reinterpret_cast<float2*>(o + col) = make_float2(acc[n][2 * half] * inv, acc[n][2 * half + 1] * inv);
-      }
-      if (c4 == 0) p.ws_lse[rec] = l > 0.f ? m + log2f(l) : -INFINITY;
-    } else if (u.nsplit == 1) {
+    if (u.nsplit == 1) {
       __nv_bfloat16* o = p.out + (static_cast<int64_t>(u.q0 + tq) * p.heads + head) * D;
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
@@ -415,7 +397,9 @@ __global__ void __launch_bounds__(kDecSubThreads, 2) decode_attention_kernel(Att
   __shared__ int abort_flag;
   __shared__ float merge_ml[kDecConsumerWarps][16][2];
 
-  pdl_wait();     // q, K and V from the norm/RoPE/append kernel ahead of this one
+  // q, K and V from the norm/RoPE/append kernel ahead of this one (or, behind the prefix grid,
+  // already complete: see decode_after_prefix).
+  if (!p.decode_after_prefix || blockIdx.x == gridDim.x - 1) pdl_wait();
   pdl_trigger();  // the prefill kernel (or the split combine) may launch behind this grid
   // KV heads fastest: the CTAs of one item's heads run together and read the same pool rows
   // (each its own 256 bytes of every 2 KB token row).
@@ -507,13 +491,14 @@ __global__ void __launch_bounds__(kDecPersistentThreads, 1) decode_persistent_ke
   __shared__ int abort_flag;
   __shared__ float merge_ml[kDecSubs][kDecConsumerWarps][16][2];
   // The unit whose first tile a stage holds, with its metadata: {unit, row, first key, end
-  // key}, {record, splits, group rows, first query}, {queries, keys}; unit -1: no more units.
+  // key}, {record, splits, unused, first query}, {queries, keys}; unit -1: no more units.
   __shared__ int4 unit_meta[kDecSubs][kDecStages][3];
 
   pdl_wait();     // q, K and V from the norm/RoPE/append kernel ahead of this one
   pdl_trigger();  // the prefill kernel (or the split combine) may launch behind this grid
   const int n_items = p.counts != nullptr ? p.counts[0] : p.num_decode;
-  const bool beside_prefill = (p.counts != nullptr ? p.counts[1] : p.num_prefill) > 0;
+  const bool beside_prefill =
+      (p.counts != nullptr ? p.counts[1] + p.counts[3] : p.num_prefill + p.num_prefix) > 0;
   const int active = beside_prefill ? min(static_cast<int>(gridDim.x), p.decode_ctas) : static_cast<int>(gridDim.x);
   if (static_cast<int>(blockIdx.x) >= active) return;  // the SM is left to the prefill grid
   const int units = n_items * p.kv_heads;

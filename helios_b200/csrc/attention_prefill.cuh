@@ -86,7 +86,13 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return r;
 }
 
-template <int GROUP>
+// PREFIX = false: prefill items, causal over each row's keys, bf16 output.
+// PREFIX = true: prefix items (see AttentionParams::prefix_items): the query tiles hold the
+// single tokens of consecutive rows that share their leading pages, every key of the item's
+// split of those pages is visible to all of them (they sit past the shared keys), and each
+// query row's (normalised output, log2-sum-exp) goes to its row's split record for the
+// combine, beside the row's own decode splits.
+template <int GROUP, bool PREFIX>
 __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(AttentionParams p,
                                                                           const __grid_constant__ CUtensorMap qmap,
                                                                           const __grid_constant__ CUtensorMap kmap,
@@ -108,33 +114,66 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_flag;
 
-  // Programmatic dependent launch. Right behind the decode kernel, this grid starts while
-  // decode CTAs still run: q, K and V are complete (the decode kernel waited for them before
-  // triggering) and this kernel does not read decode output; one CTA (the last launched)
-  // waits for the decode grid before it exits, so this grid completes after it. Behind the
-  // norm/RoPE/append kernel instead, every CTA waits first.
+  // Programmatic dependent launch. Right behind the decode (or prefix) grid, this grid starts
+  // while that grid's CTAs still run: q, K and V are complete (that grid waited for them before
+  // triggering) and this kernel does not read its output; one CTA (the last launched) waits for
+  // it before it exits, so this grid completes after it. Behind the norm/RoPE/append kernel
+  // instead, every CTA waits first.
   if (!p.prefill_after_decode) pdl_wait();
   pdl_trigger();
   const bool joins_decode = blockIdx.x == 0 && blockIdx.y == gridDim.y - 1;
-  // KV head fastest, items last to first: the longest query tiles of every head launch first.
-  const int n_items = p.counts != nullptr ? p.counts[1] : p.num_prefill;
+  // KV head fastest; prefill items last to first: the longest query tiles of every head
+  // launch first.
+  const int n_items = PREFIX ? (p.counts != nullptr ? p.counts[3] : p.num_prefix)
+                             : (p.counts != nullptr ? p.counts[1] : p.num_prefill);
   if (static_cast<int>(blockIdx.y) >= n_items) {  // past this tick's items (capacity grid)
     if (joins_decode) pdl_wait();
     return;
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x;
-  const int32_t* item = p.prefill_items + 3 * (n_items - 1 - static_cast<int>(blockIdx.y));
-  const int row = item[0];
-  const int q0 = p.cu_seq_q[row];
-  const int count = p.cu_seq_q[row + 1] - q0;
-  const int end = p.seqused_k[row];
-  // Tile 0 starts at item[1]; tile 1 (if any) at item[2] > item[1], so nk0 <= nk1.
-  const int qs0 = item[1], qs1 = item[2];
-  const int tc0 = min(kTileTokens, count - qs0);
+  // Keys [key_base, end) of the row's block table; query tiles at qs0 and qs1 (or none) of
+  // the count queries from token q0.
+  int row, q0, count, end, qs0, qs1, key_base = 0, split = 0;
+  if constexpr (PREFIX) {
+    const int32_t* item = p.prefix_items + kPrefixItemInts * static_cast<int>(blockIdx.y);
+    row = item[0];
+    count = item[1];
+    key_base = item[2];
+    end = item[3];
+    split = item[4];
+    const bool row_ok = row >= 0 && row < p.num_rows;
+    q0 = row_ok ? p.cu_seq_q[row] : 0;
+    // The members and their single tokens must exist, and the keys lie on the row's pages.
+    const int limit = row_ok ? max(0, min(p.num_rows - row, p.tokens - q0)) : 0;
+    if (count < 0 || count > limit || key_base < 0 || end < key_base || end > p.width * p.page_size) {
+      if (threadIdx.x == 0) raise_status(kStatusBadRow);
+      count = 0;
+      end = key_base;
+    }
+    qs0 = 0;
+    qs1 = count > kTileTokens ? kTileTokens : -1;
+  } else {
+    const int32_t* item = p.prefill_items + 3 * (n_items - 1 - static_cast<int>(blockIdx.y));
+    row = item[0];
+    q0 = p.cu_seq_q[row];
+    count = p.cu_seq_q[row + 1] - q0;
+    end = p.seqused_k[row];
+    // Tile 0 starts at item[1]; tile 1 (if any) at item[2] > item[1], so nk0 <= nk1.
+    qs0 = item[1];
+    qs1 = item[2];
+  }
+  const int tc0 = max(0, min(kTileTokens, count - qs0));
   const int tc1 = qs1 >= 0 ? min(kTileTokens, count - qs1) : 0;
-  const int nk0 = (min(end, end - count + qs0 + tc0) + kPreKeys - 1) / kPreKeys;
-  const int nk1 = tc1 > 0 ? (min(end, end - count + qs1 + tc1) + kPreKeys - 1) / kPreKeys : 0;
+  int nk0, nk1;
+  if constexpr (PREFIX) {
+    const int n = (end - key_base + kPreKeys - 1) / kPreKeys;
+    nk0 = tc0 > 0 ? n : 0;
+    nk1 = tc1 > 0 ? n : 0;
+  } else {
+    nk0 = (min(end, end - count + qs0 + tc0) + kPreKeys - 1) / kPreKeys;
+    nk1 = tc1 > 0 ? (min(end, end - count + qs1 + tc1) + kPreKeys - 1) / kPreKeys : 0;
+  }
   const int n_all = max(nk0, nk1);
 
   if (threadIdx.x == 0) {
@@ -187,7 +226,7 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
         bool bad = false;
 #pragma unroll
         for (int hb = 0; hb < 2; ++hb) {
-          const int key = j * kPreKeys + hb * kPreBoxKeys;
+          const int key = key_base + j * kPreKeys + hb * kPreBoxKeys;
           if (hb == 1 && key >= end) { tok[1] = tok[0]; continue; }
           const int pidx = key / p.page_size;
           if (pidx != cached_pidx) {  // one block-table read per page
@@ -324,7 +363,8 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
     const int tok = r / GROUP;
     const int qs = t ? qs1 : qs0;
     const bool row_valid = tok < (t ? tc1 : tc0);
-    const int qpos = row_valid ? end - count + qs + tok : -1;
+    // Key position limit of this query row: bottom-right causal, or every key of a prefix item.
+    const int qpos = !row_valid ? -1 : (PREFIX ? (1 << 30) : end - count + qs + tok);
     const int n = t ? nk1 : nk0;
     float m_used = -INFINITY, l = 0.f;  // running max (log2 units) the exponents are taken against
     bool ok = true;
@@ -339,7 +379,7 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
         tmem_ld32(tSP + half * 64 + 32, *reinterpret_cast<float(*)[32]>(s1));
         tmem_wait_ld();
       }
-      const int key0 = j * kPreKeys + half * 64;
+      const int key0 = key_base + j * kPreKeys + half * 64;
       if (!(key0 + 63 <= qpos && key0 + 64 <= end)) {  // edge of the causal or sequence range: mask
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
@@ -405,7 +445,7 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
       // query tile that uses key tile j (the MMA warp issues tile 1's P V of a key tile
       // after tile 0's), so both products read the zeros. Each warp of a row pair clears
       // its 64-column d-half of key row r.
-      const int vkey0 = j * kPreKeys;
+      const int vkey0 = key_base + j * kPreKeys;
       const bool zeroer = t == 0 || j >= nk0;
       if (zeroer && vkey0 + kPreKeys > end && vkey0 + r >= end) {
         // V_j must have landed first, or its TMA write would land over the zeros.
@@ -426,13 +466,34 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
         const float total = l + xsum[t][half ^ 1][r];
         tc_fence_after();
         const float inv = total > 0.f ? 1.f / total : 0.f;
-        __nv_bfloat16* o = row_valid ? p.out + (static_cast<int64_t>(q0 + qs + tok) * p.heads + h * GROUP + r % GROUP) * D + half * 64
-                                     : nullptr;
+        __nv_bfloat16* o = nullptr;
+        float* po = nullptr;  // prefix items: the member row's split record
+        if constexpr (PREFIX) {
+          if (row_valid) {
+            const int member = row + qs + tok;
+            const int rec_idx = p.row_records[member] + split;
+            if (rec_idx < 0 || rec_idx >= p.record_capacity) {
+              raise_status(kStatusBadRow);
+            } else {
+              const int64_t rec = static_cast<int64_t>(rec_idx) * p.heads + h * GROUP + r % GROUP;
+              po = p.ws_out + rec * D + half * 64;
+              if (half == 0) p.ws_lse[rec] = total > 0.f ? m_used + log2f(total) : -INFINITY;
+            }
+          }
+        } else if (row_valid) {
+          o = p.out + (static_cast<int64_t>(q0 + qs + tok) * p.heads + h * GROUP + r % GROUP) * D + half * 64;
+        }
 #pragma unroll 1
         for (int cc = 0; cc < 4; ++cc) {
           float v[16];
           tmem_ld16(tO + cc * 16, v);
           tmem_wait_ld();
+          if (po != nullptr) {
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4)
+              *reinterpret_cast<float4*>(po + cc * 16 + c4 * 4) =
+                  make_float4(v[c4 * 4] * inv, v[c4 * 4 + 1] * inv, v[c4 * 4 + 2] * inv, v[c4 * 4 + 3] * inv);
+          }
           if (o != nullptr) {
 #pragma unroll
             for (int c8 = 0; c8 < 2; ++c8) {

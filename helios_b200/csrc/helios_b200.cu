@@ -120,7 +120,7 @@ int ensure_smem(K kernel, int bytes, bool (&done)[64]) {
   return HB_OK;
 }
 
-bool g_dec_smem[4][64], g_decp_smem[4][64], g_pre_smem[4][64], g_tick_smem[64], g_gemm_smem[64], g_argmax_smem[64];
+bool g_dec_smem[4][64], g_decp_smem[4][64], g_pre_smem[4][64], g_prx_smem[4][64], g_tick_smem[64], g_gemm_smem[64], g_argmax_smem[64];
 
 constexpr int kDefaultOverlapDecodeSms = 100;
 
@@ -251,10 +251,11 @@ int hb_selftest_wait_timeout(int64_t limit_cycles, int32_t* result, cudaStream_t
 
 int hb_tick_pack(const int32_t* rows, int32_t num_rows, const int32_t* updates, int32_t num_updates, int32_t* arena,
                  int32_t arena_slots, int32_t arena_width, int32_t page_size, int32_t width, int32_t num_pages,
-                 int32_t decode_max_tokens, int32_t split_keys, int32_t prefill_tile_tokens, int32_t total_tokens,
-                 int32_t* block_table, int32_t* cu_seq_q, int32_t* cu_seq_k, int32_t* seqused_k, int64_t* positions,
-                 int64_t* write_slots, int32_t* token_row, int64_t* logit_indices, int32_t logit_capacity,
-                 int32_t* decode_items, int32_t decode_capacity, int32_t* prefill_items, int32_t prefill_capacity,
+                 int32_t decode_max_tokens, int32_t split_keys, int32_t prefill_tile_tokens,
+                 int32_t prefix_split_keys, int32_t total_tokens, int32_t* block_table, int32_t* cu_seq_q,
+                 int32_t* cu_seq_k, int32_t* seqused_k, int64_t* positions, int64_t* write_slots, int32_t* token_row,
+                 int64_t* logit_indices, int32_t logit_capacity, int32_t* decode_items, int32_t decode_capacity,
+                 int32_t* prefill_items, int32_t prefill_capacity, int32_t* prefix_items, int32_t prefix_capacity,
                  int32_t* counts, int32_t* row_records, cudaStream_t stream) {
   if (num_rows < 1 || num_rows > HB_MAX_TICK_ROWS)
     return fail(HB_ERR_INVALID, "num_rows %d outside [1, %d]", num_rows, HB_MAX_TICK_ROWS);
@@ -263,20 +264,22 @@ int hb_tick_pack(const int32_t* rows, int32_t num_rows, const int32_t* updates, 
     return fail(HB_ERR_INVALID, "null metadata pointer");
   if (num_updates < 0 || (num_updates > 0 && updates == nullptr)) return fail(HB_ERR_INVALID, "bad page updates");
   if (page_size < 1 || width < 1 || arena_width < 1 || arena_slots < 1 || num_pages < 1 || split_keys < page_size ||
-      split_keys % page_size != 0 || prefill_tile_tokens < 1 || total_tokens < 0)
+      split_keys % page_size != 0 || prefill_tile_tokens < 1 || total_tokens < 0 || prefix_split_keys < page_size ||
+      prefix_split_keys % page_size != 0)
     return fail(HB_ERR_INVALID, "bad tick sizes");
   if (total_tokens > 0 && (positions == nullptr || write_slots == nullptr || token_row == nullptr))
     return fail(HB_ERR_INVALID, "null per-token output");
   if ((logit_capacity > 0 && logit_indices == nullptr) || (decode_capacity > 0 && decode_items == nullptr) ||
-      (prefill_capacity > 0 && prefill_items == nullptr) || logit_capacity < 0 || decode_capacity < 0 ||
-      prefill_capacity < 0)
+      (prefill_capacity > 0 && prefill_items == nullptr) || (prefix_capacity > 0 && prefix_items == nullptr) ||
+      logit_capacity < 0 || decode_capacity < 0 || prefill_capacity < 0 || prefix_capacity < 0)
     return fail(HB_ERR_INVALID, "bad output capacities");
   hb::TickPackParams p{rows, updates, arena, num_rows, num_updates, arena_width, arena_slots, page_size, width,
-                       num_pages, decode_max_tokens, split_keys, prefill_tile_tokens, block_table, cu_seq_q, cu_seq_k,
-                       seqused_k, positions, write_slots, token_row, logit_indices, decode_items, prefill_items,
-                       total_tokens, logit_capacity, decode_capacity, prefill_capacity, counts, row_records};
-  const int smem = 6 * (num_rows + 1) * static_cast<int>(sizeof(int32_t));
-  if (int rc = ensure_smem(hb::tick_pack_kernel, 6 * (HB_MAX_TICK_ROWS + 1) * 4, g_tick_smem)) return rc;
+                       num_pages, decode_max_tokens, split_keys, prefill_tile_tokens, prefix_split_keys, block_table,
+                       cu_seq_q, cu_seq_k, seqused_k, positions, write_slots, token_row, logit_indices, decode_items,
+                       prefill_items, total_tokens, logit_capacity, decode_capacity, prefill_capacity, counts,
+                       row_records, prefix_items, prefix_capacity};
+  const int smem = 7 * (num_rows + 1) * static_cast<int>(sizeof(int32_t));
+  if (int rc = ensure_smem(hb::tick_pack_kernel, 7 * (HB_MAX_TICK_ROWS + 1) * 4, g_tick_smem)) return rc;
   hb::tick_pack_kernel<<<1, hb::kTickThreads, smem, stream>>>(p);
   return check_launch("tick_pack_kernel");
 }
@@ -333,10 +336,10 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
                        int32_t page_size, const int32_t* block_table, int32_t width, const int32_t* cu_seq_q,
                        const int32_t* seqused_k, int32_t num_rows, const int32_t* row_records,
                        const int32_t* decode_items, int32_t num_decode_items,
-                       const int32_t* prefill_items, int32_t num_prefill_items, const int32_t* counts,
-                       int32_t partial_records, int32_t split_keys, int32_t total_tokens, int32_t heads,
-                       int32_t kv_heads, int32_t head_dim, float scale, void* workspace, size_t workspace_bytes,
-                       void* out, cudaStream_t stream) {
+                       const int32_t* prefill_items, int32_t num_prefill_items, const int32_t* prefix_items,
+                       int32_t num_prefix_items, const int32_t* counts, int32_t partial_records,
+                       int32_t split_keys, int32_t total_tokens, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                       float scale, void* workspace, size_t workspace_bytes, void* out, cudaStream_t stream) {
   if (head_dim != 128) return fail(HB_ERR_UNSUPPORTED, "paged attention supports head_dim 128, got %d", head_dim);
   if (heads < 1 || kv_heads < 1 || heads % kv_heads) return fail(HB_ERR_INVALID, "bad head counts");
   const int group = heads / kv_heads;
@@ -344,10 +347,15 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
     return fail(HB_ERR_UNSUPPORTED, "query heads per KV head must be 1, 2, 4 or 8 (got %d)", group);
   if (page_size % hb::kDecTileKeys != 0 || split_keys % page_size != 0 || split_keys < page_size)
     return fail(HB_ERR_INVALID, "page_size must be a multiple of 64 and split_keys of page_size");
-  if (num_decode_items < 0 || num_prefill_items < 0 || total_tokens < 0 || num_pages < 1 || width < 1 ||
-      partial_records < 0 || num_rows < 1 || num_rows > HB_MAX_TICK_ROWS)
+  if (num_decode_items < 0 || num_prefill_items < 0 || num_prefix_items < 0 || total_tokens < 0 || num_pages < 1 ||
+      width < 1 || partial_records < 0 || num_rows < 1 || num_rows > HB_MAX_TICK_ROWS)
     return fail(HB_ERR_INVALID, "bad work sizes");
-  if (num_decode_items > 0 && row_records == nullptr) return fail(HB_ERR_INVALID, "null row records");
+  if ((num_decode_items > 0 || num_prefix_items > 0) && row_records == nullptr)
+    return fail(HB_ERR_INVALID, "null row records");
+  // Prefix items add their splits to rows that also have decode items: the combine behind the
+  // decode grid merges them.
+  if (num_prefix_items > 0 && num_decode_items == 0)
+    return fail(HB_ERR_INVALID, "prefix items without decode items");
   if (num_pages * page_size > (int64_t(1) << 31)) return fail(HB_ERR_UNSUPPORTED, "pool exceeds 2^31 tokens");
   if (q == nullptr || key_pool == nullptr || value_pool == nullptr || out == nullptr || block_table == nullptr ||
       cu_seq_q == nullptr || seqused_k == nullptr)
@@ -370,6 +378,7 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
   p.num_rows = num_rows;
   p.record_capacity = partial_records;
   p.prefill_items = prefill_items;
+  p.prefix_items = prefix_items;
   p.work_counter = static_cast<int32_t*>(workspace);
   p.ws_out = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWorkspaceHeader);
   p.ws_lse = p.ws_out + static_cast<size_t>(partial_records > 0 ? partial_records : 0) * heads * head_dim;
@@ -381,6 +390,7 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
   p.split_keys = split_keys;
   p.tokens = total_tokens;
   p.num_prefill = num_prefill_items;
+  p.num_prefix = num_prefix_items;
   p.counts = counts;
   p.scale_log2 = scale * 1.4426950408889634f;
 
@@ -398,17 +408,23 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
   if (static_cast<int64_t>(num_decode_items) * kv_heads > INT32_MAX)
     return fail(HB_ERR_UNSUPPORTED, "decode items x KV heads exceed 2^31");
   if (num_prefill_items > 0 && prefill_items == nullptr) return fail(HB_ERR_INVALID, "null prefill items");
+  if (num_prefix_items > 0 && prefix_items == nullptr) return fail(HB_ERR_INVALID, "null prefix items");
 
-  // Launch order decode -> prefill -> split combine on the caller's stream, each behind the
-  // previous one with programmatic dependent launch; completions are ordered through
-  // grid-dependency waits (the prefill grid completes after the decode grid, see
-  // prefill_after_decode, and the combine after both). Decode alone: one CTA per unit, two
-  // per SM. Decode with prefill work: the persistent decode grid, whose CTAs past
-  // decode_ctas exit at once so that the prefill tiles start on those SMs while the decode
-  // CTAs stream K/V (decode is HBM-bound, prefill tensor-bound).
-  if (num_prefill_items > 65535) return fail(HB_ERR_UNSUPPORTED, "more than 65535 prefill tile pairs in one call");
+  // Launch order on the caller's stream, each grid behind the previous one with programmatic
+  // dependent launch; completions are ordered through grid-dependency waits (each grid that
+  // skips its initial wait has one CTA wait for the grid ahead before it exits, see
+  // prefill_after_decode / decode_after_prefix, and the combine waits last).
+  //   Without prefill items: prefix -> decode -> combine. The decode grid runs one CTA per
+  //   unit, two per SM; its CTAs fill the SMs the prefix tiles leave and take the rest as
+  //   they finish.
+  //   With prefill items: decode -> prefix -> prefill -> combine, the decode grid persistent:
+  //   its CTAs past decode_ctas exit at once so that the tensor-core tiles start on those SMs
+  //   while the decode CTAs stream K/V (decode is HBM-bound, the tiles tensor-bound).
+  if (num_prefill_items > 65535 || num_prefix_items > 65535)
+    return fail(HB_ERR_UNSUPPORTED, "more than 65535 prefill tile pairs or prefix items in one call");
   const int overlap_sms = g_overlap_decode_sms.load();
   const bool beside = num_decode_items > 0 && num_prefill_items > 0 && overlap_sms > 0;
+  const bool prefix_first = num_prefix_items > 0 && !beside;
   int decode_grid = 0;
   if (beside) {
     const int sms = sm_count();
@@ -423,13 +439,18 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
   // opt-ins) is done first, so an early return never leaves the decode grid queued without
   // the combine that resets its work ticket.
   CUtensorMap qmap;
-  if (num_prefill_items > 0) {
+  if (num_prefill_items > 0 || num_prefix_items > 0) {
 #define HB_PREFILL_PREP(G)                                                                                      \
   do {                                                                                                          \
     if (int rc = encode_3d(&qmap, q, head_dim, heads, total_tokens, head_dim * 2,                               \
                            static_cast<uint64_t>(heads) * head_dim * 2, 64, G, hb::kPreRows / G))               \
       return rc;                                                                                                \
-    if (int rc = ensure_smem(hb::prefill_attention_kernel<G>, hb::kPreSmemBytes, g_pre_smem[gs])) return rc;     \
+    if (num_prefill_items > 0)                                                                                  \
+      if (int rc = ensure_smem(hb::prefill_attention_kernel<G, false>, hb::kPreSmemBytes, g_pre_smem[gs]))      \
+        return rc;                                                                                              \
+    if (num_prefix_items > 0)                                                                                   \
+      if (int rc = ensure_smem(hb::prefill_attention_kernel<G, true>, hb::kPreSmemBytes, g_prx_smem[gs]))       \
+        return rc;                                                                                              \
   } while (0)
     switch (group) {
       case 1: HB_PREFILL_PREP(1); break;
@@ -466,6 +487,29 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
     if (ticket_queued) cudaMemsetAsync(workspace, 0, sizeof(int32_t), stream);
     return rc;
   };
+  auto launch_prefix = [&]() -> int {
+#define HB_PREFIX(G)                                                                                            \
+  do {                                                                                                          \
+    const cudaError_t e = launch_pdl(hb::prefill_attention_kernel<G, true>, dim3(kv_heads, num_prefix_items),   \
+                                     dim3(hb::kPreThreads), hb::kPreSmemBytes, stream, p, qmap, kmap, vmap);     \
+    if (e != cudaSuccess)                                                                                       \
+      return fail_after_decode(fail(HB_ERR_CUDA, "prefill_attention_kernel<prefix>: %s", cudaGetErrorString(e))); \
+  } while (0)
+    switch (group) {
+      case 1: HB_PREFIX(1); break;
+      case 2: HB_PREFIX(2); break;
+      case 4: HB_PREFIX(4); break;
+      default: HB_PREFIX(8); break;
+    }
+#undef HB_PREFIX
+    return HB_OK;
+  };
+  if (prefix_first) {  // first behind the norm/RoPE/append kernel: every prefix CTA waits for it
+    p.prefill_after_decode = 0;
+    if (int rc = launch_prefix()) return rc;
+    p.decode_after_prefix = 1;
+  }
+  p.prefill_after_decode = num_decode_items > 0 ? 1 : 0;
   if (num_decode_items > 0) {
 #define HB_DECODE(G)                                                                                            \
   do {                                                                                                          \
@@ -488,11 +532,14 @@ int hb_paged_attention(const void* q, const void* key_pool, const void* value_po
 #undef HB_DECODE
     ticket_queued = beside;
   }
+  if (num_prefix_items > 0 && !prefix_first) {
+    if (int rc = launch_prefix()) return rc;
+  }
   if (num_prefill_items > 0) {
     const dim3 grid(kv_heads, num_prefill_items);
 #define HB_PREFILL(G)                                                                                           \
   do {                                                                                                          \
-    const cudaError_t e = launch_pdl(hb::prefill_attention_kernel<G>, grid, dim3(hb::kPreThreads),              \
+    const cudaError_t e = launch_pdl(hb::prefill_attention_kernel<G, false>, grid, dim3(hb::kPreThreads),       \
                                      hb::kPreSmemBytes, stream, p, qmap, kmap, vmap);                           \
     if (e != cudaSuccess)                                                                                       \
       return fail_after_decode(fail(HB_ERR_CUDA, "prefill_attention_kernel: %s", cudaGetErrorString(e)));      \
@@ -536,6 +583,7 @@ int hb_paged_attention_static_workspace(const void* q, const void* key_pool, con
                                        int32_t num_rows, const int32_t* row_records,
                                        const int32_t* decode_items, int32_t num_decode_items,
                                        const int32_t* prefill_items, int32_t num_prefill_items,
+                                       const int32_t* prefix_items, int32_t num_prefix_items,
                                        const int32_t* counts, int32_t partial_records, int32_t split_keys,
                                        int32_t total_tokens, int32_t heads, int32_t kv_heads, int32_t head_dim,
                                        float scale, void* out, cudaStream_t stream) {
@@ -562,7 +610,7 @@ int hb_paged_attention_static_workspace(const void* q, const void* key_pool, con
   }
   return hb_paged_attention(q, key_pool, value_pool, num_pages, page_size, block_table, width, cu_seq_q, seqused_k,
                             num_rows, row_records, decode_items, num_decode_items, prefill_items, num_prefill_items,
-                            counts, partial_records,
+                            prefix_items, num_prefix_items, counts, partial_records,
                             split_keys, total_tokens, heads, kv_heads, head_dim, scale, ws, HB_STATIC_WORKSPACE_BYTES,
                             out, stream);
 }

@@ -21,15 +21,17 @@
 //     tiles differ by at most two key tiles;
 //   * shared-prefix groups: consecutive single-token decode rows whose block tables
 //     start with the same shared_len keys (pages restored by aliasing) form a group. The
-//     group's first row carries group_rows = n. Its keys [0, shared_len) are split once
-//     for all n rows (items with group_rows = n, every query of the group against the
-//     same pages); each row's own items cover only [shared_len, end). The row's partial
-//     records are the prefix splits, then its tail splits, merged by the split combine.
+//     group's first row carries group_rows = n. Its keys [0, shared_len) are split every
+//     prefix_split_keys keys once for all n rows: prefix items, each up to two query tiles
+//     (2 x prefill_tile_tokens consecutive rows of the group, one token each) against one
+//     split of the shared pages, run on the tensor cores by the prefill kernel; each row's
+//     own decode items cover only [shared_len, end). The row's partial records are the
+//     prefix splits, then its tail splits, merged by the split combine.
 //
-// Decode item (6 int32): row, first key, end key, then
-//   group_rows == 0: record base of the item (row record base + split * count), splits of the row
-//   group_rows  > 0: the prefix split index s (member i's record: row_records[row + i] + s), unused
-// then group_rows.
+// Decode item (6 int32): row, first key, end key, record base of the item (row record base
+// + split * count), splits of the row, 0.
+// Prefix item (5 int32): first row, rows (<= 2 x prefill_tile_tokens), first key, end key,
+// prefix split index s (member i's record: row_records[first row + i] + s).
 // Every output write is bounded by the capacity the host sized it for; an entry
 // that would fall outside is skipped and reported in the status word.
 #pragma once
@@ -46,7 +48,7 @@ struct TickPackParams {
   const int32_t* updates;  // [U][3] slot, page position, page index
   int32_t* arena;          // [slots][arena_width]
   int32_t num_rows, num_updates, arena_width, arena_slots, page_size, width, num_pages;
-  int32_t decode_max_tokens, split_keys, prefill_tile_tokens;
+  int32_t decode_max_tokens, split_keys, prefill_tile_tokens, prefix_split_keys;
   int32_t* block_table;    // [B][width]
   int32_t* cu_seq_q;       // [B+1]
   int32_t* cu_seq_k;       // [B+1]
@@ -58,28 +60,32 @@ struct TickPackParams {
   int32_t* decode_items;   // [decode_capacity][kDecodeItemInts] (above)
   int32_t* prefill_items;  // [prefill_capacity][3] row, first tile start, second tile start or -1
   int32_t total_tokens, logit_capacity, decode_capacity, prefill_capacity;
-  int32_t* counts;         // optional [3]: decode items, prefill pairs, partial records (capped)
+  int32_t* counts;         // optional [4]: decode items, prefill pairs, partial records, prefix items (capped)
   int32_t* row_records;    // [B+1] first partial record of each row (exclusive prefix)
+  int32_t* prefix_items;   // [prefix_capacity][kPrefixItemInts] (above)
+  int32_t prefix_capacity;
 };
 
 constexpr int kTickThreads = 1024;
 
 __device__ __forceinline__ int row_splits(int end, int split_keys) { return (end + split_keys - 1) / split_keys; }
 
-// Decode items and partial records of row r (see the header).
+// Decode items, prefix items and partial records of row r (see the header).
 struct RowWork {
-  int items, records, prefix_splits, tail_splits;
+  int items, records, prefix_splits, tail_splits, prefix_items;
 };
 __device__ __forceinline__ RowWork row_work(const TickPackParams& p, int r) {
   const int32_t* row = p.rows + kTickRowFields * r;
   const int32_t end = row[1] + row[2], cnt = row[2], shared = row[5], group = row[6];
-  RowWork w{0, 0, 0, 0};
+  RowWork w{0, 0, 0, 0, 0};
   if (cnt > p.decode_max_tokens) return w;
   if (shared > 0) {
-    w.prefix_splits = row_splits(shared, p.split_keys);
+    const int pair_rows = 2 * p.prefill_tile_tokens;
+    w.prefix_splits = row_splits(shared, p.prefix_split_keys);
     w.tail_splits = row_splits(end - shared, p.split_keys);
-    w.items = w.tail_splits + (group > 0 ? w.prefix_splits : 0);
+    w.items = w.tail_splits;
     w.records = (w.prefix_splits + w.tail_splits) * cnt;
+    w.prefix_items = group > 0 ? ((group + pair_rows - 1) / pair_rows) * w.prefix_splits : 0;
   } else {
     w.tail_splits = row_splits(end, p.split_keys);
     w.items = w.tail_splits;
@@ -101,7 +107,8 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
   int32_t* d_off = l_off + (B + 1);
   int32_t* r_off = d_off + (B + 1);
   int32_t* f_off = r_off + (B + 1);
-  __shared__ int32_t warp_tot[32][6];
+  int32_t* x_off = f_off + (B + 1);  // prefix items
+  __shared__ int32_t warp_tot[32][7];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
   // 1. Page-arena updates (pages acquired or restored since the last tick).
@@ -117,7 +124,7 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
   // 2. Block scan over rows. Each thread owns a contiguous chunk of rows.
   const int per = (B + kTickThreads - 1) / kTickThreads;
   const int r0 = min(B, tid * per), r1 = min(B, r0 + per);
-  int32_t s[6] = {0, 0, 0, 0, 0, 0};
+  int32_t s[7] = {0, 0, 0, 0, 0, 0, 0};
   for (int r = r0; r < r1; ++r) {
     const int32_t len = p.rows[kTickRowFields * r + 1], cnt = p.rows[kTickRowFields * r + 2];
     const int32_t lc = p.rows[kTickRowFields * r + 3];
@@ -129,13 +136,14 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
       const RowWork w = row_work(p, r);
       s[3] += w.items;
       s[4] += w.records;
+      s[6] += w.prefix_items;
     } else {
       s[5] += row_prefill_items(cnt, p.prefill_tile_tokens);
     }
   }
-  int32_t incl[6];
+  int32_t incl[7];
 #pragma unroll
-  for (int f = 0; f < 6; ++f) {
+  for (int f = 0; f < 7; ++f) {
     int32_t v = s[f];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -148,7 +156,7 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
   __syncthreads();
   if (warp == 0) {
 #pragma unroll
-    for (int f = 0; f < 6; ++f) {
+    for (int f = 0; f < 7; ++f) {
       int32_t v = warp_tot[lane][f];
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -159,9 +167,9 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
     }
   }
   __syncthreads();
-  int32_t base[6];
+  int32_t base[7];
 #pragma unroll
-  for (int f = 0; f < 6; ++f) base[f] = (warp ? warp_tot[warp - 1][f] : 0) + incl[f] - s[f];
+  for (int f = 0; f < 7; ++f) base[f] = (warp ? warp_tot[warp - 1][f] : 0) + incl[f] - s[f];
   for (int r = r0; r < r1; ++r) {
     const int32_t len = p.rows[kTickRowFields * r + 1], cnt = p.rows[kTickRowFields * r + 2];
     const int32_t lc = p.rows[kTickRowFields * r + 3];
@@ -172,6 +180,7 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
     d_off[r] = base[3];
     r_off[r] = base[4];
     f_off[r] = base[5];
+    x_off[r] = base[6];
     base[0] += cnt;
     base[1] += end;
     base[2] += lc;
@@ -179,6 +188,7 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
       const RowWork w = row_work(p, r);
       base[3] += w.items;
       base[4] += w.records;
+      base[6] += w.prefix_items;
     } else {
       base[5] += row_prefill_items(cnt, p.prefill_tile_tokens);
     }
@@ -190,10 +200,12 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
     d_off[B] = base[3];
     r_off[B] = base[4];
     f_off[B] = base[5];
+    x_off[B] = base[6];
     if (p.counts != nullptr) {  // work-list sizes for launches sized to capacities
       p.counts[0] = min(base[3], p.decode_capacity);
       p.counts[1] = min(base[5], p.prefill_capacity);
       p.counts[2] = base[4];
+      p.counts[3] = min(base[6], p.prefix_capacity);
     }
   }
   __syncthreads();
@@ -230,15 +242,18 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
         it[5] = 0;
       }
       if (group > 0) {  // the group's shared keys [0, shared), once for its `group` rows
-        for (int k = 0; k < w.prefix_splits; ++k, ++at) {
-          if (at >= p.decode_capacity) { raise_status(kStatusBadRow); break; }
-          int32_t* it = p.decode_items + kDecodeItemInts * at;
-          it[0] = r;
-          it[1] = k * p.split_keys;
-          it[2] = min(shared, (k + 1) * p.split_keys);
-          it[3] = k;
-          it[4] = 0;
-          it[5] = group;
+        const int pair_rows = 2 * p.prefill_tile_tokens;
+        int px = x_off[r];
+        for (int k = 0; k < w.prefix_splits; ++k) {
+          for (int i = 0; i < group; i += pair_rows, ++px) {
+            if (px >= p.prefix_capacity) { raise_status(kStatusBadRow); break; }
+            int32_t* it = p.prefix_items + kPrefixItemInts * px;
+            it[0] = r + i;
+            it[1] = min(pair_rows, group - i);
+            it[2] = k * p.prefix_split_keys;
+            it[3] = min(shared, (k + 1) * p.prefix_split_keys);
+            it[4] = k;
+          }
         }
       }
     } else {

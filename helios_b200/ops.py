@@ -15,7 +15,8 @@ from helios_b200 import _native
 
 BF16 = torch.bfloat16
 TICK_ROW_FIELDS = 7  # slot, length, count, logit count, pages, shared prefix keys, group rows
-DECODE_ITEM_INTS = 6  # row, first key, end key, record base or prefix split, splits, group rows
+DECODE_ITEM_INTS = 6  # row, first key, end key, record base, splits of the row, 0
+PREFIX_ITEM_INTS = 5  # first row, rows, first key, end key, prefix split index
 
 
 def _ptr(t: torch.Tensor | None) -> int | None:
@@ -41,19 +42,22 @@ def lib():
 
 def tick_pack(rows_dev: torch.Tensor, num_rows: int, updates_dev: torch.Tensor | None, num_updates: int,
               arena: torch.Tensor, page_size: int, width: int, num_pages: int, decode_max_tokens: int,
-              split_keys: int, prefill_tile_tokens: int, total_tokens: int, out: dict) -> None:
+              split_keys: int, prefill_tile_tokens: int, total_tokens: int, out: dict, *,
+              prefix_split_keys: int | None = None) -> None:
     """Kernel (a): expand row descriptors into the tick's metadata (``out`` holds the buffers)."""
     _need(rows_dev, torch.int32, "rows")
     _need(arena, torch.int32, "arena")
     rc = lib().hb_tick_pack(
         rows_dev.data_ptr(), num_rows, _ptr(updates_dev) if num_updates else None, num_updates, arena.data_ptr(),
         arena.shape[0], arena.shape[1], page_size, width, num_pages, decode_max_tokens, split_keys,
-        prefill_tile_tokens, total_tokens,
+        prefill_tile_tokens, split_keys if prefix_split_keys is None else prefix_split_keys, total_tokens,
         out["block_table"].data_ptr(), out["cu_seq_q"].data_ptr(), out["cu_seq_k"].data_ptr(),
         out["seqused_k"].data_ptr(), out["positions"].data_ptr(), out["write_slots"].data_ptr(),
         out["token_row"].data_ptr(), out["logit_store"].data_ptr(), out["logit_store"].numel(),
         out["decode_items"].data_ptr(), out["decode_items"].numel() // DECODE_ITEM_INTS,
-        out["prefill_items"].data_ptr(), out["prefill_items"].numel() // 3, _ptr(out.get("counts")),
+        out["prefill_items"].data_ptr(), out["prefill_items"].numel() // 3,
+        _ptr(out.get("prefix_items")), out["prefix_items"].numel() // PREFIX_ITEM_INTS if "prefix_items" in out else 0,
+        _ptr(out.get("counts")),
         _ptr(out.get("row_records")), _stream(rows_dev.device))
     _native.check(rc, "hb_tick_pack")
 
@@ -107,7 +111,8 @@ def paged_attention(q: torch.Tensor, key_pool: torch.Tensor, value_pool: torch.T
         meta.block_table.data_ptr(), meta.block_table.shape[1], meta.cu_seq_q.data_ptr(), meta.seqused_k.data_ptr(),
         meta.batch_size, meta.row_records.data_ptr(),
         meta.decode_items.data_ptr(), meta.launch_decode_items, meta.prefill_items.data_ptr(),
-        meta.launch_prefill_items, _ptr(meta.attention_counts), meta.launch_partial_records, meta.split_keys, tokens,
+        meta.launch_prefill_items, meta.prefix_items.data_ptr(), meta.launch_prefix_items,
+        _ptr(meta.attention_counts), meta.launch_partial_records, meta.split_keys, tokens,
         heads, kv_heads, dim, float(scale),
         _ptr(ws), ws.numel() if ws is not None else 0, out.data_ptr(), _stream(q.device))
     _native.check(rc, "hb_paged_attention")

@@ -39,6 +39,9 @@ from helios_b200.config import Qwen3Config
 
 DECODE_QUERY_ROWS = 64      # query rows (tokens x group heads) one decode CTA holds
 MIN_SHARED_PAGES = 4        # common leading pages from which single-token decode rows share one prefix pass
+PREFIX_GROUP_MAX_ROWS = 512  # rows of one shared-prefix group (its prefix items take 2 tiles of rows each)
+PREFIX_MIN_SPLIT_KEYS = 512  # shortest split of the shared keys one prefix item covers
+PREFIX_SM_SHARE = 4          # the prefix tiles aim at 1/PREFIX_SM_SHARE of the SMs; the decode grid takes the rest
 PREFILL_TILE_ROWS = 128     # query rows of one tcgen05 prefill tile (a CTA takes a pair of tiles)
 NUM_SMS_B200 = 148
 
@@ -249,6 +252,18 @@ def choose_split_keys(decode_keys_x_heads: int, page_size: int, num_sms: int = N
     return min(split, 64 * page_size)
 
 
+def choose_prefix_split_keys(pairs_x_heads: int, max_shared: int, page_size: int, num_sms: int = NUM_SMS_B200) -> int:
+    """Keys per split of the shared prefixes. The prefix tiles (one CTA per pair of query tiles,
+    split and KV head) run first and the decode grid fills the SMs they leave, so the splits are
+    sized for about num_sms / PREFIX_SM_SHARE of those CTAs: few enough that most SMs stream the
+    rows' own keys meanwhile, and the tensor-core work of the shared keys ends with them (measured
+    at BASELINE config 4, 128 rows on 16 shared pages: 89 / 78 / 74 us for splits of 512 / 1024 /
+    2048 keys). At least PREFIX_MIN_SPLIT_KEYS keys, a multiple of the page size."""
+    splits = max(1, round(num_sms / PREFIX_SM_SHARE / max(1, pairs_x_heads)))
+    split = max(PREFIX_MIN_SPLIT_KEYS, math.ceil(max(1, max_shared) / splits))
+    return math.ceil(split / page_size) * page_size
+
+
 class PagedBatchCache:
     def __init__(self, caches: Sequence[PagedKVCache]) -> None:
         if not caches:
@@ -273,9 +288,10 @@ class PagedBatchCache:
         # tick's real work counts from the device, so launch arguments and buffer
         # addresses stay the same from tick to tick.
         self.capacity_mode = False
-        self.work_capacity: tuple[int, int] | None = None
+        self.work_capacity: tuple[int, int, int] | None = None
         self.attention_counts: torch.Tensor | None = None
         self.launch_decode_items = self.launch_prefill_items = self.launch_partial_records = 0
+        self.launch_prefix_items = self.num_prefix_items = 0
 
     @property
     def length(self) -> int:
@@ -377,34 +393,39 @@ class PagedBatchCache:
         group = config.n_heads // config.n_kv_heads
         decode_max = DECODE_QUERY_ROWS // group
         tile_tokens = PREFILL_TILE_ROWS // group
-        self._share_prefixes(rows, decode_max)
+        pair_rows = 2 * tile_tokens
+        self._share_prefixes(rows, PREFIX_GROUP_MAX_ROWS)
         ends = rows[:, 1].astype(np.int64) + rows[:, 2]
         cnts = rows[:, 2].astype(np.int64)
         shared = rows[:, 5].astype(np.int64)
-        heads = rows[:, 6] > 0
+        group_rows = rows[:, 6].astype(np.int64)
+        heads = group_rows > 0
         is_decode = cnts <= decode_max
-        # Keys the decode work reads: each row's own keys, each shared prefix once.
-        read = ends - shared + np.where(heads, shared, 0)
-        split = choose_split_keys(int(read[is_decode].sum()) * config.n_kv_heads, page_size)
-        prefix_splits = (shared + split - 1) // split
+        # The decode items read each row's own keys; the prefix items each group's shared keys,
+        # once per pair of query tiles.
+        split = choose_split_keys(int((ends - shared)[is_decode].sum()) * config.n_kv_heads, page_size)
+        pairs = (group_rows + pair_rows - 1) // pair_rows
+        prefix_split = choose_prefix_split_keys(int(pairs[heads].sum()) * config.n_kv_heads,
+                                                int(shared[heads].max(initial=0)), page_size)
+        prefix_splits = (shared + prefix_split - 1) // prefix_split
         tail_splits = (ends - shared + split - 1) // split
-        items = tail_splits + np.where(heads, prefix_splits, 0)
         records = (prefix_splits + tail_splits) * cnts
         return {
             "rows": rows, "updates": np.asarray(updates, dtype=np.int32), "decode_max": decode_max,
-            "tile_tokens": tile_tokens, "split_keys": split, "num_decode_items": int(items[is_decode].sum()),
-            "partial_records": int(records[is_decode].sum()),
+            "tile_tokens": tile_tokens, "split_keys": split, "num_decode_items": int(tail_splits[is_decode].sum()),
+            "prefix_split_keys": prefix_split, "num_prefix_items": int((pairs * prefix_splits)[heads].sum()),
+            "pair_rows": pair_rows, "partial_records": int(records[is_decode].sum()),
             "num_prefill_items": int(((((cnts[~is_decode] + tile_tokens - 1) // tile_tokens) + 1) // 2).sum()),
             "total_tokens": int(cnts.sum()), "num_logits": int(rows[:, 3].sum()),
             "width": _pages_for(max(cache.capacity for cache in self.caches), page_size),
         }
 
-    def _share_prefixes(self, rows: np.ndarray, decode_max: int) -> None:
-        """Fill the shared-prefix columns of ``rows``: runs of up to ``decode_max`` consecutive
+    def _share_prefixes(self, rows: np.ndarray, max_rows: int) -> None:
+        """Fill the shared-prefix columns of ``rows``: runs of up to ``max_rows`` consecutive
         single-token decode rows whose page lists start with the same MIN_SHARED_PAGES or more
         pages (restored by aliasing) form a group; every member gets the group's common full
         pages as shared prefix keys and the first member the group size. Their attention reads
-        those pages once for the whole group."""
+        those pages once per pair of tensor-core query tiles (2 x 128 query rows)."""
         page_size = self.pool.page_size
         caches = self.caches
         # Committed pages a row may share: single-token rows only.
@@ -421,7 +442,7 @@ class PagedBatchCache:
             head = caches[r].pages
             common, j = lead, r + 1
             shared = head[:common]  # the group's common pages so far, sliced once per change
-            while j < count and j - r < decode_max:
+            while j < count and j - r < max_rows:
                 fj = full[j]
                 limit = common if fj >= common else fj
                 pages = caches[j].pages
@@ -454,21 +475,28 @@ class PagedBatchCache:
             raise ValueError("The B200 paged cache needs its pool on a CUDA device.")
         desc = self._host_descriptor(counts, logit_counts)
         self.split_keys = desc["split_keys"]
+        self.prefix_split_keys = desc["prefix_split_keys"]
         self.num_decode_items = desc["num_decode_items"]
         self.partial_records = desc["partial_records"]
         self.num_prefill_items = desc["num_prefill_items"]
+        self.num_prefix_items = desc["num_prefix_items"]
         if self.capacity_mode:
             cap = self.work_capacity
-            if cap is None or self.num_decode_items > cap[0] or self.num_prefill_items > cap[1]:
-                # Headroom of one more split and one more tile pair per row; no prefill capacity for a
-                # decode-only tick, so its attention runs the decode grid alone (all SMs).
+            if (cap is None or self.num_decode_items > cap[0] or self.num_prefill_items > cap[1]
+                    or self.num_prefix_items > cap[2]):
+                # Headroom of one more split and one more tile pair per row and twice the prefix
+                # items; no prefill or prefix capacity for a tick without them, so its attention
+                # runs the decode grid alone (all SMs).
                 cap = (self.num_decode_items + self.batch_size,
-                       self.num_prefill_items + self.batch_size if self.num_prefill_items else 0)
+                       self.num_prefill_items + self.batch_size if self.num_prefill_items else 0,
+                       2 * self.num_prefix_items)
                 self.work_capacity = cap
-            self.launch_decode_items, self.launch_prefill_items = cap
-            self.launch_partial_records = cap[0] * desc["decode_max"]  # each item has <= decode_max rows
+            self.launch_decode_items, self.launch_prefill_items, self.launch_prefix_items = cap
+            # Each decode item has <= decode_max rows, each prefix item <= pair_rows, one record each.
+            self.launch_partial_records = cap[0] * desc["decode_max"] + cap[2] * desc["pair_rows"]
         else:
             self.launch_decode_items, self.launch_prefill_items = self.num_decode_items, self.num_prefill_items
+            self.launch_prefix_items = self.num_prefix_items
             self.launch_partial_records = self.partial_records
         rows, updates = desc["rows"], desc["updates"]
         total, width = desc["total_tokens"], desc["width"]
@@ -479,7 +507,7 @@ class PagedBatchCache:
         out = self._outputs(self.batch_size, width, total, desc["num_logits"])
         ops.tick_pack(dev[: rows.size], self.batch_size, dev[rows.size:], updates.size // 3, pool.arena,
                       pool.page_size, width, pool.num_pages, desc["decode_max"], desc["split_keys"],
-                      desc["tile_tokens"], total, out)
+                      desc["tile_tokens"], total, out, prefix_split_keys=desc["prefix_split_keys"])
         need = ops.workspace_bytes(self.launch_partial_records, config.n_heads, config.head_dim)
         if need and (self.workspace is None or self.workspace.numel() < need):
             # Zeroed: its header holds the decode work ticket, which every call leaves at zero.
@@ -496,6 +524,7 @@ class PagedBatchCache:
         self.decode_items = out["decode_items"]
         self.row_records = out["row_records"]
         self.prefill_items = out["prefill_items"]
+        self.prefix_items = out["prefix_items"]
         self.attention_counts = out["counts"] if self.capacity_mode else None
         self.total_tokens = total
 
@@ -503,8 +532,9 @@ class PagedBatchCache:
         """Views of two reusable device buffers sized for this tick."""
         n_dec = max(1, self.launch_decode_items)
         n_pre = max(1, self.launch_prefill_items)
+        n_pfx = max(1, self.launch_prefix_items)
         sizes32 = [rows * width, rows + 1, rows + 1, rows, max(tokens, 1), ops.DECODE_ITEM_INTS * n_dec, 3 * n_pre, 4,
-                   rows + 1]
+                   rows + 1, ops.PREFIX_ITEM_INTS * n_pfx]
         sizes64 = [max(tokens, 1), max(tokens, 1), max(logits, 1)]
         dev = self.pool.device
         if self._i32 is None or self._i32.numel() < sum(sizes32):
@@ -517,8 +547,8 @@ class PagedBatchCache:
         v64 = [self._i64[o64[i]:o64[i + 1]] for i in range(len(sizes64))]
         return {
             "block_table": v32[0].view(rows, width), "cu_seq_q": v32[1], "cu_seq_k": v32[2], "seqused_k": v32[3],
-            "token_row": v32[4][:tokens], "decode_items": v32[5], "prefill_items": v32[6], "counts": v32[7][:3],
-            "row_records": v32[8],
+            "token_row": v32[4][:tokens], "decode_items": v32[5], "prefill_items": v32[6], "counts": v32[7],
+            "row_records": v32[8], "prefix_items": v32[9],
             "positions": v64[0][:tokens], "write_slots": v64[1][:tokens], "logit_store": v64[2],
             "logit_indices": v64[2][:logits],
         }

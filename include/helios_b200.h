@@ -82,26 +82,30 @@ HB_API int hb_selftest_wait_timeout(int64_t limit_cycles, int32_t* result, cudaS
  * cu_seq_q/cu_seq_k int32 [num_rows+1], seqused_k int32 [num_rows], positions,
  * write_slots int64 [total_tokens], token_row int32 [total_tokens], logit_indices
  * int64 [logit_capacity], decode_items int32 [decode_capacity][6] for rows with count <=
- * decode_max_tokens, split every split_keys keys: (row, first key, end key, record base,
- * splits of the row, 0), and for each group (first row, first key, end key of a split of
- * the shared keys, its split index, 0, n), run once for the group's n rows.
+ * decode_max_tokens, split every split_keys keys of the row's own keys (after its shared
+ * prefix keys): (row, first key, end key, record base, splits of the row, 0).
+ * prefix_items int32 [prefix_capacity][5]: for each group, its shared keys split every
+ * prefix_split_keys keys (a multiple of page_size), and its rows taken 2 x prefill_tile_tokens
+ * at a time: (first row, rows, first key, end key, split index), each run once for those rows.
  * row_records int32 [num_rows+1] (device, may be null when there are no decode rows) gets
  * each row's first partial record: a decode row's records are its shared-prefix splits, then
  * its own splits, each with one record per query token. prefill_items int32
  * [prefill_capacity][3] (row, start of query
  * tile 2i, start of tile 2i+1 or -1) pairing adjacent tiles of prefill_tile_tokens
- * queries of a row. Entries past a capacity are not written. counts (device int32[3],
+ * queries of a row. Entries past a capacity are not written. counts (device int32[4],
  * may be null) receives the number of decode items and prefill pairs written (capped at
- * their capacities) and the partial records the decode items need.
+ * their capacities), the partial records the decode and prefix items need, and the number
+ * of prefix items written (capped).
  */
 HB_API int hb_tick_pack(const int32_t* rows, int32_t num_rows, const int32_t* updates, int32_t num_updates,
                         int32_t* arena, int32_t arena_slots, int32_t arena_width, int32_t page_size, int32_t width,
                         int32_t num_pages, int32_t decode_max_tokens, int32_t split_keys, int32_t prefill_tile_tokens,
-                        int32_t total_tokens, int32_t* block_table, int32_t* cu_seq_q, int32_t* cu_seq_k,
-                        int32_t* seqused_k, int64_t* positions, int64_t* write_slots, int32_t* token_row,
-                        int64_t* logit_indices, int32_t logit_capacity, int32_t* decode_items,
+                        int32_t prefix_split_keys, int32_t total_tokens, int32_t* block_table, int32_t* cu_seq_q,
+                        int32_t* cu_seq_k, int32_t* seqused_k, int64_t* positions, int64_t* write_slots,
+                        int32_t* token_row, int64_t* logit_indices, int32_t logit_capacity, int32_t* decode_items,
                         int32_t decode_capacity, int32_t* prefill_items, int32_t prefill_capacity,
-                        int32_t* counts, int32_t* row_records, cudaStream_t stream);
+                        int32_t* prefix_items, int32_t prefix_capacity, int32_t* counts, int32_t* row_records,
+                        cudaStream_t stream);
 
 /*
  * (b) Fused per-head q/k RMSNorm + RoPE + paged KV append. Replaces, in
@@ -134,13 +138,17 @@ HB_API size_t hb_attention_workspace_bytes(int32_t partial_records, int32_t head
  * paged_cache.py:521-546. q and out are [total_tokens][heads][head_dim]; the
  * pools [num_pages][page_size][kv_heads][head_dim]. Work items come from
  * hb_tick_pack: decode items run split-K (partials in `workspace`, merged by a
- * combine launch), prefill items run on tcgen05 tensor cores. With counts null the
- * launch covers exactly num_decode_items / num_prefill_items. With counts (device, the
- * array hb_tick_pack filled) those two arguments and partial_records are capacities: the
- * grids are sized to them and the kernels read the real numbers from counts, so one
- * launch (for instance inside a CUDA graph) serves every tick within the capacities.
- * The decode grid is persistent (at most one CTA per SM); with prefill items in the same call the
- * prefill grid runs beside it on the SMs it leaves (hb_attention_set_overlap), all on `stream`.
+ * combine launch), prefill items run on tcgen05 tensor cores, and so do prefix items (rows
+ * sharing restored pages: their tokens against each split of the shared keys, once for
+ * all of them), whose partials the same combine merges into each row's own splits. With
+ * counts null the launch covers exactly num_decode_items / num_prefill_items /
+ * num_prefix_items. With counts (device, the array hb_tick_pack filled) those arguments and
+ * partial_records are capacities: the grids are sized to them and the kernels read the real
+ * numbers from counts, so one launch (for instance inside a CUDA graph) serves every tick
+ * within the capacities. Prefix items need decode items in the same call (their rows' own
+ * keys). With prefill or prefix items in the same call the decode grid is persistent (at
+ * most one CTA per SM) and the tensor-core grids run beside it on the SMs it leaves
+ * (hb_attention_set_overlap), all on `stream`.
  * The workspace's first 256 bytes hold a work ticket: they must be zero before the first call
  * with a workspace, and every call leaves them zero.
  */
@@ -148,7 +156,8 @@ HB_API int hb_paged_attention(const void* q, const void* key_pool, const void* v
                               int32_t page_size, const int32_t* block_table, int32_t width, const int32_t* cu_seq_q,
                               const int32_t* seqused_k, int32_t num_rows, const int32_t* row_records,
                               const int32_t* decode_items, int32_t num_decode_items,
-                              const int32_t* prefill_items, int32_t num_prefill_items, const int32_t* counts,
+                              const int32_t* prefill_items, int32_t num_prefill_items,
+                              const int32_t* prefix_items, int32_t num_prefix_items, const int32_t* counts,
                               int32_t partial_records, int32_t split_keys, int32_t total_tokens, int32_t heads,
                               int32_t kv_heads, int32_t head_dim, float scale, void* workspace,
                               size_t workspace_bytes, void* out, cudaStream_t stream);
@@ -189,6 +198,7 @@ HB_API int hb_paged_attention_static_workspace(const void* q, const void* key_po
                                                int32_t num_rows, const int32_t* row_records,
                                                const int32_t* decode_items, int32_t num_decode_items,
                                                const int32_t* prefill_items, int32_t num_prefill_items,
+                                               const int32_t* prefix_items, int32_t num_prefix_items,
                                                const int32_t* counts, int32_t partial_records, int32_t split_keys,
                                                int32_t total_tokens, int32_t heads, int32_t kv_heads,
                                                int32_t head_dim, float scale, void* out, cudaStream_t stream);

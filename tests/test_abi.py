@@ -39,14 +39,14 @@ def test_version_and_workspace_arithmetic(lib):
 def test_invalid_arguments_are_rejected_before_any_launch(lib):
     rc = lib.hb_rmsnorm(None, 0, None, None, ctypes.c_float(1e-6), None, 4, 7, None)
     assert rc == _native.HB_ERR_UNSUPPORTED and "multiple of 8" in _native.last_error()
-    rc = lib.hb_paged_attention(None, None, None, 1, 256, None, 1, None, None, 1, None, None, 0, None, 0, None, 0, 256,
-                                1, 32, 8, 64, ctypes.c_float(1.0), None, 0, None, None)
+    rc = lib.hb_paged_attention(None, None, None, 1, 256, None, 1, None, None, 1, None, None, 0, None, 0, None, 0, None,
+                                0, 256, 1, 32, 8, 64, ctypes.c_float(1.0), None, 0, None, None)
     assert rc == _native.HB_ERR_UNSUPPORTED and "head_dim 128" in _native.last_error()
-    rc = lib.hb_paged_attention(None, None, None, 1, 256, None, 1, None, None, 1, None, None, 0, None, 0, None, 0, 256,
-                                1, 32, 5, 128, ctypes.c_float(1.0), None, 0, None, None)
+    rc = lib.hb_paged_attention(None, None, None, 1, 256, None, 1, None, None, 1, None, None, 0, None, 0, None, 0, None,
+                                0, 256, 1, 32, 5, 128, ctypes.c_float(1.0), None, 0, None, None)
     assert rc == _native.HB_ERR_INVALID
-    rc = lib.hb_tick_pack(None, 0, None, 0, None, 1, 1, 256, 1, 1, 16, 256, 32, 0, None, None, None, None, None, None,
-                          None, None, 0, None, 0, None, 0, None, None, None)
+    rc = lib.hb_tick_pack(None, 0, None, 0, None, 1, 1, 256, 1, 1, 16, 256, 32, 256, 0, None, None, None, None, None,
+                          None, None, None, 0, None, 0, None, 0, None, 0, None, None, None)
     assert rc == _native.HB_ERR_INVALID
     with pytest.raises(ValueError, match="hb_swiglu"):
         _native.check(lib.hb_swiglu(None, None, 4, 7, None), "hb_swiglu")

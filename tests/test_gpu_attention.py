@@ -235,18 +235,20 @@ def _shared_prefix_batch(tails, prefix_pages, extra_counts=(), seed=7, heads=32,
     return pool, batch, prefix
 
 
-@pytest.mark.parametrize("tails,prefix_pages,extra", [
-    ([10, 300, 700, 5, 256, 1000], 16, ()),                  # decode alone: one grid per unit
-    ([40] * 20, 6, ()),                                      # 20 rows: groups of 16 and 4
-    ([3, 500, 77, 1200, 64], 9, (700,)),                    # beside a prefill row: the persistent grid
+@pytest.mark.parametrize("tails,prefix_pages,extra,heads", [
+    ([10, 300, 700, 5, 256, 1000], 16, (), 32),              # decode grid per unit, then the prefix tiles
+    ([40] * 20, 6, (), 32),                                  # 20 rows: one pair of query tiles
+    ([3, 500, 77, 1200, 64], 9, (700,), 32),                # beside a prefill row: the persistent grid
+    ([(7 * i) % 1000 + 1 for i in range(130)], 16, (), 32),  # 130 rows: 3 pairs, several prefix splits
+    ([(11 * i) % 500 + 1 for i in range(70)], 8, (), 8),     # 1 query head per KV head: 128-token tiles
+    ([(13 * i) % 300 + 1 for i in range(40)], 5, (300,), 64),  # 8 query heads per KV head: 16-token tiles
 ])
-def test_rows_sharing_a_prefix_match_the_oracle(tails, prefix_pages, extra):
-    pool, batch, prefix = _shared_prefix_batch(tails, prefix_pages, extra)
-    dec = batch.decode_items[: 6 * batch.num_decode_items].view(-1, 6)
-    assert (dec[:, 5] > 0).any()  # the prefix is read once per group
+def test_rows_sharing_a_prefix_match_the_oracle(tails, prefix_pages, extra, heads):
+    pool, batch, prefix = _shared_prefix_batch(tails, prefix_pages, extra, heads=heads)
+    assert batch.num_prefix_items > 0  # the prefix is read once per pair of query tiles
     g = torch.Generator().manual_seed(99)
     T = batch.total_tokens
-    q = torch.randn(1, 32, T, 128, generator=g).to(torch.bfloat16)
+    q = torch.randn(1, heads, T, 128, generator=g).to(torch.bfloat16)
     k = (torch.randn(1, 8, T, 128, generator=g) / 3).to(torch.bfloat16)
     v = torch.randn(1, 8, T, 128, generator=g).to(torch.bfloat16)
     kp_cpu, vp_cpu = pool.keys[0].cpu(), pool.values[0].cpu()

@@ -75,3 +75,45 @@ def test_graph_ticks_match_eager_ticks():
         last = a.argmax(-1).tolist()
     assert runner.replays > before
     assert _native.device_status() == 0
+
+
+def test_graph_ticks_with_a_shared_prefix_match_eager_ticks():
+    """Decode rows that restored the same prefix pages (page aliasing) run their shared keys as
+    prefix items on the tensor cores: replayed graphs read the prefix items' count from the
+    device like the other work counts and must agree with eager ticks."""
+    torch.manual_seed(0)
+    model = Qwen3Model(Qwen3Config(**SHAPE)).to(DEV).eval()
+    model.enable_cuda_graphs()
+    runner = model._graphs
+    eager, graphed = Decoder(model), Decoder(model)
+    pools = [KVPagePool(model.config, 64, device=DEV) for _ in range(2)]
+    eager.page_pool, graphed.page_pool = pools
+    g = torch.Generator().manual_seed(2)
+    prompt = torch.randint(0, 4096, (1100,), generator=g).tolist()
+    bases = [PagedKVCache(pool, 1200) for pool in pools]
+    model._graphs = None
+    for dec, base in zip((eager, graphed), bases):
+        dec.packed_caches([base], [prompt])
+    blocks = [base.snapshot_block(0, 4 * 256) for base in bases]
+    tails = [torch.randint(0, 4096, (n,), generator=g).tolist() for n in (5, 90, 260, 31, 140)]
+    rows = [[], []]
+    for side in range(2):
+        for tail in tails:
+            cache = PagedKVCache(pools[side], 1024 + len(tail) + 40)
+            cache.restore_blocks([blocks[side]])
+            rows[side].append(cache)
+    a = eager.packed_caches(rows[0], tails).clone()
+    b = graphed.packed_caches(rows[1], tails).clone()
+    _close(b, a)
+    last = a.argmax(-1).tolist()
+    for _ in range(12):
+        chunks = [[t] for t in last]
+        model._graphs = None
+        a = eager.packed_caches(rows[0], chunks).clone()
+        model._graphs = runner
+        b = graphed.packed_caches(rows[1], chunks).clone()
+        assert graphed._packed_batch.num_prefix_items > 0  # the 5 rows share 4 pages
+        _close(b, a)
+        last = a.argmax(-1).tolist()
+    assert runner.replays >= 10
+    assert _native.device_status() == 0

@@ -123,8 +123,9 @@ def test_second_tick_uploads_only_new_pages_and_restore_resyncs():
 
 def test_rows_sharing_restored_pages_form_one_prefix_pass():
     """Single-token decode rows whose page lists start with the same restored pages: the group's
-    prefix keys get items once for all its rows, each row keeps items for its own keys only,
-    and its records are the prefix splits, then its own."""
+    prefix keys get prefix items once for all its rows (one per split of the shared keys), each
+    row keeps decode items for its own keys only, and its records are the prefix splits, then
+    its own."""
     pool = KVPagePool(attn_config(heads=32, kv_heads=8), 120, device=DEV)
     prefix = PagedKVCache(pool, 2048)
     prefix.pages.extend(pool.acquire(6))
@@ -143,16 +144,17 @@ def test_rows_sharing_restored_pages_form_one_prefix_pass():
     other.length = 2000
     batch = PackedBatchCache(caches + [other])
     batch.prepare_packed([1] * 6)
-    sk = batch.split_keys
+    sk, psk = batch.split_keys, batch.prefix_split_keys
     dec = batch.decode_items[: 6 * batch.num_decode_items].view(-1, 6).tolist()
+    pfx = batch.prefix_items[: 5 * batch.num_prefix_items].view(-1, 5).tolist()
     rec = batch.row_records.tolist()
     shared = 6 * 256
-    groups = [it for it in dec if it[5] > 0]
-    n_prefix = math.ceil(shared / sk)
-    assert groups == [[0, s * sk, min(shared, (s + 1) * sk), s, 0, 5] for s in range(n_prefix)]
+    n_prefix = math.ceil(shared / psk)
+    assert pfx == [[0, 5, s * psk, min(shared, (s + 1) * psk), s] for s in range(n_prefix)]
+    assert all(it[5] == 0 for it in dec)
     for row, tail in enumerate(tails):
         end = shared + tail + 1
-        own = [it for it in dec if it[0] == row and it[5] == 0]
+        own = [it for it in dec if it[0] == row]
         n_own = math.ceil((end - shared) / sk)
         assert [(kb, ke) for _, kb, ke, _, _, _ in own] == [(shared + k * sk, min(end, shared + (k + 1) * sk))
                                                            for k in range(n_own)]
@@ -160,6 +162,6 @@ def test_rows_sharing_restored_pages_form_one_prefix_pass():
         assert all(n == n_prefix + n_own for _, _, _, _, n, _ in own)
         assert rec[row + 1] - rec[row] == n_prefix + n_own
     own = [it for it in dec if it[0] == 5]
-    assert all(it[5] == 0 and it[1] % sk == 0 for it in own)  # the unshared row: plain splits from key 0
+    assert all(it[1] % sk == 0 for it in own)  # the unshared row: plain splits from key 0
     assert rec[6] == batch.partial_records
     assert _native.device_status() == 0

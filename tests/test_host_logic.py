@@ -18,6 +18,7 @@ from helios_b200.paged_cache import (
     PackedBatchCache,
     PagedBatchCache,
     PagedKVCache,
+    choose_prefix_split_keys,
     choose_split_keys,
 )
 
@@ -178,13 +179,47 @@ def test_rows_restoring_one_prefix_are_grouped():
     rows = d["rows"]
     assert rows[:, 5].tolist() == [5 * 256, 5 * 256, 5 * 256, 0, 0, 0]  # the third row shares 5 pages
     assert rows[:, 6].tolist() == [3, 0, 0, 0, 0, 0]  # row 4 is alone: row 5 has two tokens
-    split = d["split_keys"]
+    split, prefix_split = d["split_keys"], d["prefix_split_keys"]
     ends = [c.length + n for c, n in zip(caches, counts)]
     shared = 5 * 256
-    prefix_splits = math.ceil(shared / split)
+    # The group's shared keys: one prefix item per split (its 3 rows fit one pair of query
+    # tiles); each row's own keys: decode items.
+    prefix_splits = math.ceil(shared / prefix_split)
+    assert prefix_split % 256 == 0 and prefix_split >= 512
     own = [math.ceil((e - shared) / split) for e in ends[:3]] + [math.ceil(e / split) for e in ends[3:]]
-    assert d["num_decode_items"] == prefix_splits + sum(own)
+    assert d["num_decode_items"] == sum(own)
+    assert d["num_prefix_items"] == prefix_splits
     assert d["partial_records"] == 3 * prefix_splits + sum(o * n for o, n in zip(own, counts))
+
+
+def test_prefix_groups_take_pairs_of_query_tiles():
+    """A group of more rows than a pair of tensor-core query tiles holds (2 x 32 tokens at 4
+    query heads per KV head) gets one prefix item per pair and split; groups stop at
+    PREFIX_GROUP_MAX_ROWS rows."""
+    cfg = tiny(n_heads=32, n_kv_heads=8, context_length=8192)
+    pool = KVPagePool(cfg, 4096, device=CPU)
+    prefix = PagedKVCache(pool, 4096)
+    prefix.pages.extend(pool.acquire(16))
+    prefix.length = 16 * 256
+    block = prefix.snapshot_block(0, prefix.length)
+    caches = []
+    for tail in range(1, 131):
+        c = PagedKVCache(pool, 8192)
+        c.restore_blocks([block])
+        c.pages.extend(pool.acquire(math.ceil((prefix.length + tail) / 256) - len(c.pages)))
+        c.length = prefix.length + tail
+        caches.append(c)
+    d = PackedBatchCache(caches)._host_descriptor([1] * 130, [1] * 130)
+    rows = d["rows"]
+    assert rows[:, 6].tolist() == [130] + [0] * 129 and set(rows[:, 5].tolist()) == {4096}
+    assert d["pair_rows"] == 64
+    splits = math.ceil(4096 / d["prefix_split_keys"])
+    assert d["num_prefix_items"] == math.ceil(130 / 64) * splits
+    # About a quarter of the SMs run the prefix tiles: 3 pairs x 8 KV heads x 2 splits.
+    assert d["prefix_split_keys"] == choose_prefix_split_keys(3 * 8, 4096, 256) == 2048
+    # Few rows: more splits of the shared keys; never below PREFIX_MIN_SPLIT_KEYS.
+    assert choose_prefix_split_keys(8, 4096, 256) == 1024
+    assert choose_prefix_split_keys(1, 1024, 256) == 512
 
 
 def test_split_policy():

@@ -41,7 +41,8 @@ def _static_attention(q, key_pool, value_pool, batch, out):
         batch.block_table.data_ptr(), batch.block_table.shape[1], batch.cu_seq_q.data_ptr(),
         batch.seqused_k.data_ptr(), batch.batch_size, batch.row_records.data_ptr(),
         batch.decode_items.data_ptr(), batch.num_decode_items,
-        batch.prefill_items.data_ptr(), batch.num_prefill_items, None, batch.partial_records, batch.split_keys,
+        batch.prefill_items.data_ptr(), batch.num_prefill_items, batch.prefix_items.data_ptr(), batch.num_prefix_items,
+        None, batch.partial_records, batch.split_keys,
         q.shape[0], q.shape[1], key_pool.shape[2], q.shape[2], ctypes.c_float(q.shape[2] ** -0.5),
         out.data_ptr(), torch.cuda.current_stream().cuda_stream)
 
@@ -130,7 +131,8 @@ def test_static_workspace_rejects_partials_beyond_its_size():
         batch.block_table.data_ptr(), batch.block_table.shape[1], batch.cu_seq_q.data_ptr(),
         batch.seqused_k.data_ptr(), batch.batch_size, batch.row_records.data_ptr(),
         batch.decode_items.data_ptr(), batch.num_decode_items,
-        batch.prefill_items.data_ptr(), batch.num_prefill_items, None, too_many, batch.split_keys, tokens, 32, 8, 128,
+        batch.prefill_items.data_ptr(), batch.num_prefill_items, batch.prefix_items.data_ptr(), batch.num_prefix_items,
+        None, too_many, batch.split_keys, tokens, 32, 8, 128,
         ctypes.c_float(0.0883883), out.data_ptr(), torch.cuda.current_stream().cuda_stream)
     assert rc == _native.HB_ERR_INVALID
     assert "built-in" in _native.last_error()
