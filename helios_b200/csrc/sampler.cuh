@@ -17,6 +17,14 @@
 // histograms are per warp (no cross-warp atomics on the few bins a peaked distribution
 // fills), index-ordered counts and sums are warp scans plus one block scan over the warps,
 // and the last pass walks only the warp whose segment holds the draw.
+//
+// A top-p row first takes the short path: after the max pass (packed bf16 maxima), one pass
+// collects the candidates (tokens whose weight can matter: logit >= x_floor), testing each
+// 16-byte group by its maximum first since few groups hold one, each warp staging its own run
+// of the list with its count in a register. The cut is then a single mass histogram over the
+// candidates' keys (by distance below their top key, fixed-point masses, so the sums are exact
+// and order-free), and only the kept tokens are sorted, by index, for the draw. Rows with more
+// candidates than the list holds, or whose cut keeps every candidate, take the whole-row passes.
 #pragma once
 
 #include <climits>
@@ -130,6 +138,66 @@ __device__ __forceinline__ void load_groups(const __nv_bfloat16* lg, int base, i
   }
 }
 
+constexpr int kSampleRawUnroll = 8;  // raw groups a lane loads before using any (max pass)
+
+// The 8 logits of group g as four packed bf16 pairs (-inf past the row end); returns how many
+// are in the row.
+__device__ __forceinline__ int load_raw(const __nv_bfloat16* lg, int g, int V, bool vec_ok, uint4& r) {
+  const int i0 = 8 * g;
+  const int n = min(8, V - i0);
+  if (vec_ok && n == 8) {
+    r = *reinterpret_cast<const uint4*>(lg + i0);
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t lo = 2 * k < n ? __bfloat16_as_ushort(lg[i0 + 2 * k]) : 0xFF80u;
+      const uint32_t hi = 2 * k + 1 < n ? __bfloat16_as_ushort(lg[i0 + 2 * k + 1]) : 0xFF80u;
+      w[k] = lo | (hi << 16);
+    }
+    r = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  return n;
+}
+
+// Largest of a group's 8 logits (packed bf16 maxima, NaN-ignoring as fmaxf), as a float.
+__device__ __forceinline__ float group_max(const uint4& r) {
+  auto h = [](uint32_t w) { return *reinterpret_cast<const __nv_bfloat162*>(&w); };
+  const __nv_bfloat162 m = __hmax2(__hmax2(h(r.x), h(r.y)), __hmax2(h(r.z), h(r.w)));
+  return fmaxf(__low2float(m), __high2float(m));
+}
+
+// Logit bits of element e (0..7, known when compiled) of a raw group.
+__device__ __forceinline__ uint32_t raw_bits(const uint4& r, int e) {
+  const uint32_t w = e < 2 ? r.x : e < 4 ? r.y : e < 6 ? r.z : r.w;
+  return (e & 1) ? (w >> 16) : (w & 0xFFFFu);
+}
+
+// Appends the tokens of group g (its bits b, n of them in the row) whose logit reaches x_floor to
+// list[0 .. cap) as (index << 16 | bits), reserving their slots with one shared-memory atomic
+// per warp; every lane of the warp calls it. Slots past cap are counted but not written.
+__device__ __forceinline__ void append_candidates(const uint32_t (&b)[8], int n, int g, float x_floor, int* count,
+                                                  unsigned long long* list, int cap) {
+  const int lane = threadIdx.x & 31;
+  uint32_t mine = 0;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) mine |= (e < n && bits_to_float(b[e]) >= x_floor) ? (1u << e) : 0u;
+  const int cnt = __popc(mine);
+  const int incl = warp_inclusive_scan(cnt);
+  const int total = __shfl_sync(0xffffffffu, incl, 31);
+  if (total == 0) return;  // warp-uniform
+  int slot0 = 0;
+  if (lane == 31) slot0 = atomicAdd(count, total);
+  int slot = __shfl_sync(0xffffffffu, slot0, 31) + incl - cnt;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    if ((mine >> e) & 1u) {
+      if (slot < cap) list[slot] = (static_cast<unsigned long long>(8 * g + e) << 16) | b[e];
+      ++slot;
+    }
+  }
+}
+
 // The 256 bins of `hist` in descending key order (bin 255 first), by one warp: the first bin
 // k with cum <= target < cum + hist[k] (and hist[k] > 0 when `nonempty`), where cum is `base`
 // plus the mass of the bins above k. Returns the bin (or -1) and its cum; also the total mass.
@@ -198,74 +266,185 @@ __device__ __forceinline__ uint32_t key_to_bits(uint32_t key) {
   return (key & 0x8000u) ? (key & 0x7FFFu) : (~key & 0xFFFFu);
 }
 
+// Masses of candidate tokens in fixed point: a weight in (kNegligibleWeight, 1] times 2^50,
+// rounded to an integer (negligible weights count 0). Sums of at most kSampleCand of them stay
+// below 2^62 and are exact, so every mass below is independent of the order it was summed in.
+constexpr double kMassScale = 1125899906842624.0;  // 2^50
+__device__ __forceinline__ unsigned long long mass_q(float w) {
+  return w > kNegligibleWeight ? __double2ull_rn(static_cast<double>(w) * kMassScale) : 0ull;
+}
+
+// Shared memory the candidate path needs besides the candidate list (which, once read into
+// registers, holds first the mass histogram and then the kept tokens).
+struct CandidateScratch {
+  unsigned long long ull_red[32];
+  uint32_t u32_red[32];
+  int n_kept, n_ties, cut_d, far;
+  unsigned long long cut_cum;
+};
+constexpr int kCandBins = kSampleCand;  // key distances below the row's top key the histogram covers
+
 // The cut and the draw of a top-p row from its candidate list (every token whose weight can
 // matter; see kSampleCand), with the rules of the whole-row passes: only weights above
 // kNegligibleWeight count toward the masses; in descending probability order (ties by
 // ascending index) a token is kept when the mass before it is at most top_p * Z (the first
 // always); the kept tokens are visited in index order and the first whose running mass exceeds
-// u * kept mass is drawn (the last kept one when rounding leaves none). The list is sorted by
-// (key descending, index ascending) for the cut, then its kept prefix by index for the draw.
-// Every thread of the block calls it. Returns false, with nothing written, when the cut keeps
-// every candidate: tokens outside the list may then be kept too, which the whole-row passes
-// decide.
+// u * kept mass is drawn (the last kept one when rounding leaves none). The cut comes from one
+// mass histogram over the order key, binned by distance below the candidates' top key (tokens
+// at one bf16 value share a bin, so few tokens meet in a bin's atomics) and scanned top down;
+// tokens tied at the cut key are kept lowest index first. Only the kept tokens are sorted (by
+// index) for the draw. Every thread of the block calls it. Returns false, with nothing written,
+// when the cut keeps every candidate (tokens outside the list may then be kept too) or the
+// candidates span more than kCandBins keys: the whole-row passes decide those rows.
+// `cand` holds the list on entry and the kept tokens (index << 16 | bits) afterwards.
 __device__ bool sample_candidates(const SampleParams& p, int row, int nc, unsigned long long* cand, float top_p,
-                                  float T, float m, int* ired, double* dred, int* chosen) {
-  const int tid = threadIdx.x;
+                                  float T, float m, CandidateScratch& sc, int* chosen) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int R = kSampleCand / kSampleThreads;  // candidates (and histogram bins) per thread
   auto weight = [&](uint32_t bits) { return expf(__fdiv_rn(bits_to_float(bits), T) - m); };
 
-  // Descending key, ascending index: (0xFFFF - key) << 32 | index, ascending.
-  for (int i = tid; i < nc; i += kSampleThreads) {
-    const unsigned long long c = cand[i];
-    const uint32_t key = bf16_key_bits(static_cast<uint32_t>(c & 0xFFFFu));
-    cand[i] = (static_cast<unsigned long long>(0xFFFFu - key) << 32) | (c >> 16);
+  unsigned long long c[R], q[R];
+  uint32_t key[R];
+  uint32_t kmax = 0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = tid + r * kSampleThreads;
+    c[r] = i < nc ? cand[i] : 0ull;
+    key[r] = i < nc ? bf16_key_bits(static_cast<uint32_t>(c[r] & 0xFFFFu)) : 0u;
+    q[r] = i < nc ? mass_q(weight(static_cast<uint32_t>(c[r] & 0xFFFFu))) : 0ull;
+    kmax = max(kmax, key[r]);
+  }
+  // The top key, and whether every candidate lies within kCandBins keys of it.
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+  if (lane == 0) sc.u32_red[warp] = kmax;
+  if (tid == 0) sc.n_kept = sc.n_ties = sc.far = 0;
+  __syncthreads();  // every candidate is in registers: `cand` is free for the histogram
+  kmax = sc.u32_red[0];
+#pragma unroll
+  for (int w = 1; w < kSampleWarps; ++w) kmax = max(kmax, sc.u32_red[w]);
+  bool far = false;
+#pragma unroll
+  for (int r = 0; r < R; ++r) far |= tid + r * kSampleThreads < nc && kmax - key[r] >= static_cast<uint32_t>(kCandBins);
+  if (__any_sync(0xffffffffu, far) && lane == 0) sc.far = 1;
+  unsigned long long* hist = cand;  // bin d: the mass of the tokens with key kmax - d
+#pragma unroll
+  for (int r = 0; r < R; ++r) hist[tid * R + r] = 0ull;
+  __syncthreads();
+  if (sc.far) return false;
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+    if (q[r]) atomicAdd(&hist[kmax - key[r]], q[r]);
+  __syncthreads();
+  // Scan top down (thread t owns bins R t .. R t + R - 1): Z, then the first bin with
+  // cum <= top_p Z < cum + mass and mass > 0.
+  unsigned long long h[R], local = 0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    h[r] = hist[tid * R + r];
+    local += h[r];
+  }
+  const unsigned long long incl = warp_inclusive_scan(local);
+  if (lane == 31) sc.ull_red[warp] = incl;
+  if (tid == 0) sc.cut_d = -1;
+  __syncthreads();
+  unsigned long long cum = incl - local, Z = 0;
+  for (int w = 0; w < kSampleWarps; ++w) {
+    if (w < warp) cum += sc.ull_red[w];
+    Z += sc.ull_red[w];
+  }
+  const double target = static_cast<double>(top_p) * static_cast<double>(Z);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if (h[r] > 0 && static_cast<double>(cum) <= target && target < static_cast<double>(cum + h[r])) {
+      sc.cut_d = tid * R + r;  // one bin at most meets this
+      sc.cut_cum = cum;
+    }
+    cum += h[r];
   }
   __syncthreads();
-  block_sort(cand, nc);
+  if (sc.cut_d < 0) return false;  // the cut keeps every candidate
+  const uint32_t key_star = kmax - static_cast<uint32_t>(sc.cut_d);
+  // Tokens tied at key_star share one weight: the first n_tie_keep of them (by index) are kept.
+  const unsigned long long e_star = mass_q(weight(key_to_bits(key_star)));
+  if (e_star == 0) return false;
+  const int n_tie_keep =
+      static_cast<int>(floor((target - static_cast<double>(sc.cut_cum)) / static_cast<double>(e_star))) + 1;
+  unsigned long long* kept = cand;  // the histogram is read: the kept tokens go here
+  // Kept tokens above the cut go to the front of `kept`, tokens at the cut to its back.
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = tid + r * kSampleThreads;
+    const bool above = i < nc && key[r] > key_star, tie = i < nc && key[r] == key_star;
+    const unsigned ma = __ballot_sync(0xffffffffu, above), mt = __ballot_sync(0xffffffffu, tie);
+    int base_a = 0, base_t = 0;
+    if (lane == 0) {
+      if (ma) base_a = atomicAdd(&sc.n_kept, __popc(ma));
+      if (mt) base_t = atomicAdd(&sc.n_ties, __popc(mt));
+    }
+    base_a = __shfl_sync(0xffffffffu, base_a, 0);
+    base_t = __shfl_sync(0xffffffffu, base_t, 0);
+    const unsigned below = (1u << lane) - 1u;
+    if (above) kept[base_a + __popc(ma & below)] = c[r];
+    if (tie) kept[kSampleCand - 1 - (base_t + __popc(mt & below))] = c[r];
+  }
+  __syncthreads();
+  const int n_above = sc.n_kept, n_ties = sc.n_ties;
+  const int t_keep = min(n_ties, n_tie_keep);
+  if (n_above + t_keep >= nc) return false;
+  // A tie is kept when fewer than n_tie_keep ties have a lower index (its rank, counted over
+  // the tie list; the ties at one bf16 value are few). All ranks are taken before any write.
+  bool keep_tie[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int i = tid + r * kSampleThreads;
+    keep_tie[r] = false;
+    if (i < nc && key[r] == key_star) {
+      if (n_ties <= n_tie_keep) {
+        keep_tie[r] = true;
+      } else {
+        const unsigned long long idx = c[r] >> 16;
+        int rank = 0;
+        for (int j = 0; j < n_ties; ++j) rank += (kept[kSampleCand - 1 - j] >> 16) < idx;
+        keep_tie[r] = rank < n_tie_keep;
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const unsigned mk = __ballot_sync(0xffffffffu, keep_tie[r]);
+    int base_k = 0;
+    if (lane == 0 && mk) base_k = atomicAdd(&sc.n_kept, __popc(mk));
+    base_k = __shfl_sync(0xffffffffu, base_k, 0);
+    if (keep_tie[r]) kept[base_k + __popc(mk & ((1u << lane) - 1u))] = c[r];
+  }
+  __syncthreads();
+  const int n_keep = sc.n_kept;  // n_above + t_keep
+  block_sort(kept, n_keep);      // by index (the keys lead with it); pads within the list's 4096 entries
 
-  // Exclusive mass before each entry in that order, over a contiguous slice per thread.
-  const int per = (nc + kSampleThreads - 1) / kSampleThreads;
-  const int lo = min(nc, tid * per), hi = min(nc, lo + per);
-  double mass = 0.0;
-  for (int i = lo; i < hi; ++i) {
-    const float w = weight(key_to_bits(0xFFFFu - static_cast<uint32_t>(cand[i] >> 32)));
-    if (w > kNegligibleWeight) mass += static_cast<double>(w);
-  }
-  double Z;
-  double before = block_exclusive_scan(mass, dred, &Z);
-  const double t = static_cast<double>(top_p) * Z;
-  // Kept entries form a prefix: the count is the number with mass-before <= t (at least 1).
-  int keep = 0;
-  for (int i = lo; i < hi; ++i) {
-    const float w = weight(key_to_bits(0xFFFFu - static_cast<uint32_t>(cand[i] >> 32)));
-    if (before <= t || i == 0) ++keep;
-    if (w > kNegligibleWeight) before += static_cast<double>(w);
-  }
-  const int n_keep = block_reduce(keep, [](int a, int b) { return a + b; }, ired);
-  if (n_keep >= nc) return false;
-
-  // The kept prefix back to (index << 16 | bits), sorted by index.
-  for (int i = tid; i < n_keep; i += kSampleThreads) {
-    const unsigned long long c = cand[i];
-    const uint32_t bits = key_to_bits(0xFFFFu - static_cast<uint32_t>(c >> 32));
-    cand[i] = ((c & 0xFFFFFFFFull) << 16) | bits;
-  }
+  // Kept mass in index order over a contiguous slice per thread, then the draw.
+  const int per = (n_keep + kSampleThreads - 1) / kSampleThreads;
+  const int lo = min(n_keep, tid * per), hi2 = min(n_keep, lo + per);
+  unsigned long long kept_mass = 0;
+  for (int i = lo; i < hi2; ++i) kept_mass += mass_q(weight(static_cast<uint32_t>(kept[i] & 0xFFFFu)));
+  const unsigned long long kincl = warp_inclusive_scan(kept_mass);
+  if (lane == 31) sc.ull_red[warp] = kincl;
   __syncthreads();
-  block_sort(cand, n_keep);
-  const int per2 = (n_keep + kSampleThreads - 1) / kSampleThreads;
-  const int lo2 = min(n_keep, tid * per2), hi2 = min(n_keep, lo2 + per2);
-  double kept_mass = 0.0;
-  for (int i = lo2; i < hi2; ++i) kept_mass += static_cast<double>(weight(static_cast<uint32_t>(cand[i] & 0xFFFFu)));
-  double kept_total;
-  const double kept_before = block_exclusive_scan(kept_mass, dred, &kept_total);
-  const double draw = static_cast<double>(p.uniforms[row]) * kept_total;
-  if (tid == 0) *chosen = static_cast<int>(cand[n_keep - 1] >> 16);  // the last kept (rounding)
+  unsigned long long before = kincl - kept_mass, kept_total = 0;
+  for (int w = 0; w < kSampleWarps; ++w) {
+    if (w < warp) before += sc.ull_red[w];
+    kept_total += sc.ull_red[w];
+  }
+  const double draw = static_cast<double>(p.uniforms[row]) * static_cast<double>(kept_total);
+  if (tid == 0) *chosen = static_cast<int>(kept[n_keep - 1] >> 16);  // the last kept (rounding)
   __syncthreads();
-  if (kept_mass > 0.0 && kept_before <= draw && draw < kept_before + kept_mass) {
-    double run = kept_before;
-    for (int i = lo2; i < hi2; ++i) {
-      run += static_cast<double>(weight(static_cast<uint32_t>(cand[i] & 0xFFFFu)));
-      if (run > draw) {
-        atomicMin(chosen, static_cast<int>(cand[i] >> 16));
+  if (kept_mass > 0 && static_cast<double>(before) <= draw && draw < static_cast<double>(before + kept_mass)) {
+    unsigned long long run = before;
+    for (int i = lo; i < hi2; ++i) {
+      run += mass_q(weight(static_cast<uint32_t>(kept[i] & 0xFFFFu)));
+      if (static_cast<double>(run) > draw) {
+        atomicMin(chosen, static_cast<int>(kept[i] >> 16));
         break;
       }
     }
@@ -290,6 +469,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) 
   __shared__ int cut_found;
   __shared__ int chosen;
   __shared__ int ncand;
+  __shared__ CandidateScratch cscratch;
 
   const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const __nv_bfloat16* lg = p.logits + static_cast<int64_t>(row) * p.row_stride;
@@ -304,28 +484,30 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) 
   // Pass 1: max (and, for a greedy row, its first index).
   float mx = -INFINITY;
   int arg = INT_MAX;
-  for (int base = g_begin; base < g_end; base += 32 * kSampleUnroll) {
+  for (int base = g_begin; greedy && base < g_end; base += 32 * kSampleUnroll) {
     uint32_t b[kSampleUnroll][8];
     int n[kSampleUnroll];
     load_groups(lg, base, g_end, V, vec_ok, b, n);
 #pragma unroll
-    for (int u = 0; u < kSampleUnroll; ++u) {
-      if (greedy) {
+    for (int u = 0; u < kSampleUnroll; ++u)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float v = bits_to_float(b[u][e]);
-          if (e < n[u] && v > mx) { mx = v; arg = 8 * (base + 32 * u + lane) + e; }  // indices visited in order
-        }
-      } else if (n[u] == 8) {
-        float v[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = bits_to_float(b[u][e]);
-        mx = fmaxf(mx, fmaxf(fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3])), fmaxf(fmaxf(v[4], v[5]), fmaxf(v[6], v[7]))));
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          if (e < n[u]) mx = fmaxf(mx, bits_to_float(b[u][e]));
+      for (int e = 0; e < 8; ++e) {
+        const float v = bits_to_float(b[u][e]);
+        if (e < n[u] && v > mx) { mx = v; arg = 8 * (base + 32 * u + lane) + e; }  // indices visited in order
       }
+  }
+  if (!greedy) {  // the maximum alone: packed maxima, twice the loads in flight
+    for (int base = g_begin; base < g_end; base += 32 * kSampleRawUnroll) {
+      uint4 r[kSampleRawUnroll];
+      int n[kSampleRawUnroll];
+#pragma unroll
+      for (int u = 0; u < kSampleRawUnroll; ++u) {
+        const int g = base + 32 * u + lane;
+        n[u] = g < g_end ? load_raw(lg, g, V, vec_ok, r[u]) : 0;
+      }
+#pragma unroll
+      for (int u = 0; u < kSampleRawUnroll; ++u)
+        if (n[u] > 0) mx = fmaxf(mx, group_max(r[u]));
     }
   }
   const float gmax = block_reduce(mx, [](float a, float b) { return fmaxf(a, b); }, fred);
@@ -343,31 +525,75 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleParams p) 
   const float x_floor = T * (m - 28.f);
 
   if (top_p < 1.f) {
-    // Candidate pass: every token with logit >= x_floor (warp-aggregated appends).
-    if (tid == 0) ncand = 0;
-    __syncthreads();
+    // Candidate pass: every token with logit >= x_floor. Each warp stages the candidates of its
+    // segment in its own kWarpCand entries of the list, counting in a register (no shared
+    // counter for all warps to meet on), then the warps' runs are packed together in order.
+    constexpr int kWarpCand = kSampleCand / kSampleWarps;
+    int wcount = 0;  // the same in every lane
+    unsigned long long* mine_list = sh.cand + warp * kWarpCand;
     for (int base = g_begin; base < g_end; base += 32 * kSampleUnroll) {
-      uint32_t b[kSampleUnroll][8];
+      uint4 r[kSampleUnroll];
       int n[kSampleUnroll];
-      load_groups(lg, base, g_end, V, vec_ok, b, n);
 #pragma unroll
-      for (int u = 0; u < kSampleUnroll; ++u)
+      for (int u = 0; u < kSampleUnroll; ++u) {
+        const int g = base + 32 * u + lane;
+        n[u] = g < g_end ? load_raw(lg, g, V, vec_ok, r[u]) : 0;
+      }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const bool c = e < n[u] && bits_to_float(b[u][e]) >= x_floor;
-          const unsigned mask = __ballot_sync(0xffffffffu, c);
-          if (mask == 0u) continue;  // warp-uniform
-          const int leader = __ffs(mask) - 1;
-          int slot = 0;
-          if (lane == leader) slot = atomicAdd(&ncand, __popc(mask));
-          slot = __shfl_sync(0xffffffffu, slot, leader) + __popc(mask & ((1u << lane) - 1u));
-          if (c && slot < kSampleCand)
-            sh.cand[slot] = (static_cast<unsigned long long>(8 * (base + 32 * u + lane) + e) << 16) | b[u][e];
+      for (int u = 0; u < kSampleUnroll; ++u) {
+        // Most groups hold no candidate: their packed maximum is below the floor.
+        uint32_t mine = 0;
+        if (n[u] > 0 && group_max(r[u]) >= x_floor) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) mine |= (e < n[u] && bits_to_float(raw_bits(r[u], e)) >= x_floor) ? (1u << e) : 0u;
         }
+        const int cnt = __popc(mine);
+        const int incl = warp_inclusive_scan(cnt);
+        const int total = __shfl_sync(0xffffffffu, incl, 31);
+        if (total == 0) continue;  // warp-uniform
+        int slot = wcount + incl - cnt;
+        const int g = base + 32 * u + lane;
+        while (mine) {
+          const int e = __ffs(mine) - 1;
+          mine &= mine - 1;
+          const uint32_t w = e < 2 ? r[u].x : e < 4 ? r[u].y : e < 6 ? r[u].z : r[u].w;
+          const uint32_t bits = (e & 1) ? (w >> 16) : (w & 0xFFFFu);
+          if (slot < kWarpCand) mine_list[slot] = (static_cast<unsigned long long>(8 * g + e) << 16) | bits;
+          ++slot;
+        }
+        wcount += total;
+      }
     }
-    __syncthreads();
-    const int nc = ncand;
-    if (nc <= kSampleCand && sample_candidates(p, row, nc, sh.cand, top_p, T, m, ired, dred, &chosen)) return;
+    int total_cand;
+    const int woff = warps_exclusive_scan(wcount, ired, &total_cand);  // syncs the block
+    const bool overflow = __syncthreads_or(wcount > kWarpCand);
+    int nc = total_cand;
+    if (!overflow) {
+      // Pack the runs: every warp reads its entries before any is written over.
+      unsigned long long v[kWarpCand / 32];
+#pragma unroll
+      for (int k = 0; k < kWarpCand / 32; ++k) v[k] = lane + 32 * k < wcount ? mine_list[lane + 32 * k] : 0ull;
+      __syncthreads();
+#pragma unroll
+      for (int k = 0; k < kWarpCand / 32; ++k)
+        if (lane + 32 * k < wcount) sh.cand[woff + lane + 32 * k] = v[k];
+      __syncthreads();
+    } else {
+      // A segment held more candidates than its run: collect again through one shared counter.
+      if (tid == 0) ncand = 0;
+      __syncthreads();
+      for (int base = g_begin; base < g_end; base += 32 * kSampleUnroll) {
+        uint32_t b[kSampleUnroll][8];
+        int n[kSampleUnroll];
+        load_groups(lg, base, g_end, V, vec_ok, b, n);
+#pragma unroll
+        for (int u = 0; u < kSampleUnroll; ++u)
+          append_candidates(b[u], n[u], base + 32 * u + lane, x_floor, &ncand, sh.cand, kSampleCand);
+      }
+      __syncthreads();
+      nc = ncand;
+    }
+    if (nc <= kSampleCand && sample_candidates(p, row, nc, sh.cand, top_p, T, m, cscratch, &chosen)) return;
     __syncthreads();  // the candidate list's memory holds the histograms from here on
   }
 

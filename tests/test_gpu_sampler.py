@@ -29,10 +29,11 @@ def _draw(logits, temperature, top_p, uniforms):
 def test_greedy_first_index_and_large_vocab():
     g = torch.Generator().manual_seed(0)
     logits = (torch.randn(33, 151936, generator=g) * 3).to(torch.bfloat16)
-    logits[5, [7, 99, 150000]] = 40.0  # tie at the max: first index wins
+    logits[5, [7, 99, 150000]] = 40.0  # tie at the max: first index wins (across warp segments too)
+    logits[6, [150000, 149999]] = 41.0  # tie inside the last segment
     ids = _draw(logits, 0.0, 1.0, torch.zeros(33))
     assert ids.tolist() == torch.argmax(logits.float(), -1).tolist()
-    assert ids[5].item() == 7
+    assert ids[5].item() == 7 and ids[6].item() == 149999
 
 
 @pytest.mark.parametrize("temperature,top_p", [(0.2, 0.95), (0.7, 0.9), (1.0, 0.5), (1.5, 1.0), (1.0, 0.999)])
@@ -70,3 +71,28 @@ def test_draws_stay_in_reference_kept_set_and_follow_its_distribution(golden_dir
             freq = torch.bincount(ids, minlength=vocab).double() / n
             # Inverse CDF over an evenly spaced sweep: each token's share is within 1/n of its mass.
             assert (freq - probs).abs().max().item() <= 1.0 / n + 1e-6
+
+
+@pytest.mark.parametrize("temperature,top_p,rows", [
+    (0.2, 0.95, "crowded"),  # 400 candidates inside one warp's segment: collected again through one counter
+    (1.0, 0.9, "flat"),      # more candidates than the list holds: the whole-row passes
+    (0.2, 0.95, "few"),      # three tokens above -inf-like logits, two of them tied
+])
+def test_unusual_rows_match_oracle(temperature, top_p, rows):
+    g = torch.Generator().manual_seed(7)
+    vocab = 151936
+    logits = torch.full((4, vocab), -30.0)
+    if rows == "crowded":
+        logits[:, 5000:5400] = torch.randn(4, 400, generator=g)
+    elif rows == "flat":
+        logits = torch.randn(4, vocab, generator=g) * 0.01
+    else:
+        logits[:, [3, 77777, 150001]] = torch.tensor([2.0, 2.5, 2.5])
+    logits = logits.to(torch.bfloat16)
+    uniforms = torch.rand(4, generator=g)
+    got = _draw(logits, temperature, top_p, uniforms)
+    want = osampler.sample(logits.float(), temperature, top_p, uniforms)
+    if not torch.equal(got, want):
+        dist = osampler.boundary_distance(logits.float(), temperature, uniforms, top_p)
+        bad = (got != want).nonzero().reshape(-1)
+        assert (dist[bad] < 1e-5).all(), (bad, dist[bad])
