@@ -256,7 +256,7 @@ class TickRunner:
 
     def _count_launches(self, batch) -> int:
         attention = (batch.num_decode_items > 0) + (batch.num_decode_items > 0 and batch.partial_records > 0) \
-            + (batch.num_prefill_items > 0)
+            + (batch.num_prefill_items > 0) + (batch.num_prefix_items > 0)
         per_layer = 1 + attention + 2 + 1  # norm/rope/append, attention, add_rmsnorm x2, swiglu
         # tick pack, embed, first norm, the layers, the lm_head GEMM with the argmax and its finalize
         return 3 + per_layer * self.model.config.n_layers + 2
