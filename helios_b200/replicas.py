@@ -27,6 +27,10 @@ def init(backend: str, timeout_s: float = 120.0) -> bool:
     if size <= 1:
         return False
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    if backend == "nccl":
+        # NCCL's own log (its version banner at the VERSION and WARN levels) goes to stderr, so
+        # rank 0's stdout carries only what the caller prints.
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     dist.init_process_group(backend=backend, rank=rank, world_size=size, timeout=timedelta(seconds=timeout_s))
     return True
 
