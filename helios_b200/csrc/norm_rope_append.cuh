@@ -48,6 +48,47 @@ struct NormRopeParams {
 constexpr int kRopeThreads = 256;
 constexpr int kRopeMaxRows = 3;  // rows one thread keeps in flight per pass (48 rows = one pass)
 
+// Two fp32 products / sums / differences in one instruction (sm_100 f32x2), each rounded to
+// nearest as its scalar form is.
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w);
+  return make_float2(__low2float(h), __high2float(h));
+}
+__device__ __forceinline__ uint32_t pack2(float2 f) { return pack_bf16(f.x, f.y); }
+
 __device__ __forceinline__ void unpack4(const uint2& v, float (&f)[4]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
   f[0] = __low2float(h[0]);
@@ -76,10 +117,11 @@ __device__ __forceinline__ void norm_lane(uint2& ylo, uint2& yhi, const float4& 
   for (int o = kLanes / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(row_mask, ss, o);
   // mean = ss / D: D is a power of two, so the product by 1 / D is the exact quotient.
   const float inv = rsqrtf(__fadd_rn(ss * (1.f / static_cast<float>(D)), eps));
-  ylo.x = pack_bf16(__fmul_rn(__fmul_rn(a[0], inv), ga.x), __fmul_rn(__fmul_rn(a[1], inv), ga.y));
-  ylo.y = pack_bf16(__fmul_rn(__fmul_rn(a[2], inv), ga.z), __fmul_rn(__fmul_rn(a[3], inv), ga.w));
-  yhi.x = pack_bf16(__fmul_rn(__fmul_rn(b[0], inv), gb.x), __fmul_rn(__fmul_rn(b[1], inv), gb.y));
-  yhi.y = pack_bf16(__fmul_rn(__fmul_rn(b[2], inv), gb.z), __fmul_rn(__fmul_rn(b[3], inv), gb.w));
+  const float2 inv2 = make_float2(inv, inv);
+  ylo.x = pack2(mul2(mul2(make_float2(a[0], a[1]), inv2), make_float2(ga.x, ga.y)));
+  ylo.y = pack2(mul2(mul2(make_float2(a[2], a[3]), inv2), make_float2(ga.z, ga.w)));
+  yhi.x = pack2(mul2(mul2(make_float2(b[0], b[1]), inv2), make_float2(gb.x, gb.y)));
+  yhi.y = pack2(mul2(mul2(make_float2(b[2], b[3]), inv2), make_float2(gb.z, gb.w)));
 }
 
 // One lane's share of RoPE, y * cos + rot(y) * sin with rot(y) = (-y_hi, y_lo):
@@ -87,16 +129,13 @@ __device__ __forceinline__ void norm_lane(uint2& ylo, uint2& yhi, const float4& 
 // (negation is exact); c_lo/s_lo are the tables at this lane's first-half elements.
 __device__ __forceinline__ void rope_lane(uint2& ylo, uint2& yhi, const float (&c_lo)[4], const float (&c_hi)[4],
                                           const float (&s_lo)[4], const float (&s_hi)[4]) {
-  float a[4], b[4], o[8];
-  unpack4(ylo, a);
-  unpack4(yhi, b);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    o[e] = __fsub_rn(__fmul_rn(a[e], c_lo[e]), __fmul_rn(b[e], s_lo[e]));
-    o[4 + e] = __fadd_rn(__fmul_rn(b[e], c_hi[e]), __fmul_rn(a[e], s_hi[e]));
-  }
-  ylo = make_uint2(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]));
-  yhi = make_uint2(pack_bf16(o[4], o[5]), pack_bf16(o[6], o[7]));
+  const float2 a01 = unpack2(ylo.x), a23 = unpack2(ylo.y), b01 = unpack2(yhi.x), b23 = unpack2(yhi.y);
+  const float2 cl01 = make_float2(c_lo[0], c_lo[1]), cl23 = make_float2(c_lo[2], c_lo[3]);
+  const float2 ch01 = make_float2(c_hi[0], c_hi[1]), ch23 = make_float2(c_hi[2], c_hi[3]);
+  const float2 sl01 = make_float2(s_lo[0], s_lo[1]), sl23 = make_float2(s_lo[2], s_lo[3]);
+  const float2 sh01 = make_float2(s_hi[0], s_hi[1]), sh23 = make_float2(s_hi[2], s_hi[3]);
+  ylo = make_uint2(pack2(sub2(mul2(a01, cl01), mul2(b01, sl01))), pack2(sub2(mul2(a23, cl23), mul2(b23, sl23))));
+  yhi = make_uint2(pack2(add2(mul2(b01, ch01), mul2(a01, sh01))), pack2(add2(mul2(b23, ch23), mul2(a23, sh23))));
 }
 
 // rope_lane with the table values as float4 (the same arithmetic).
