@@ -271,10 +271,12 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the issue loop (waits by every lane, one elected lane issuing each
+    // MMA and commit), so it stays converged and warp-uniform beside the 16 softmax warps.
+    {
       constexpr uint32_t idesc_s = idesc_bf16(kPreRows, kPreKeys, false, false);
       constexpr uint32_t idesc_pv = idesc_bf16(kPreRows, D, false, true);
-      bool ok = mbar_wait(&q_full, 0, &abort_flag);
+      bool ok = mbar_wait_warp(&q_full, 0, &abort_flag);
       // Operand descriptors are built once; per K step and stage only their start-address
       // field (low 14 bits, 16-byte units) moves, by offsets that never carry out of it
       // (shared memory is below 256 KB), so each MMA costs one add per operand.
@@ -289,9 +291,9 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
         for (int kk = 0; kk < D / 16; ++kk) {  // 16 of the 128 head dims per step
           const uint32_t qoff = ((kk >> 2) * (kPreQBytes / 2) + (kk & 3) * 32) >> 4;
           const uint32_t koff = ((kk >> 2) * kPreKVHalf + (kk & 3) * 32) >> 4;
-          mma_ss(d, a + qoff, b + koff, idesc_s, kk > 0);
+          mma_ss_warp(d, a + qoff, b + koff, idesc_s, kk > 0);
         }
-        mma_commit(&s_full[t]);
+        mma_commit_warp(&s_full[t]);
       };
       auto issue_pv = [&](int t, int j) {
         const uint32_t p_tmem = tmem + kPreKeys * t;
@@ -299,8 +301,8 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
         const uint32_t d = tmem + kPreTmemO + t * 128;
 #pragma unroll
         for (int kk = 0; kk < kPreKeys / 16; ++kk)  // 16 keys = 8 columns of P, 16 rows of V per step
-          mma_ts(d, p_tmem + kk * 8, b + ((kk * 2048) >> 4), idesc_pv, (j > 0 || kk > 0));
-        mma_commit(&o_done[t]);
+          mma_ts_warp(d, p_tmem + kk * 8, b + ((kk * 2048) >> 4), idesc_pv, (j > 0 || kk > 0));
+        mma_commit_warp(&o_done[t]);
       };
       // Fixed issue order with blocking waits (a poll of an mbarrier costs about as
       // much as an MMA, so the thread never polls): S of key tile 0 for both tiles,
@@ -313,7 +315,7 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
       int k_have = -1;  // highest key tile whose K stage is known to have landed
       auto need_k = [&](int x) -> bool {
         if (k_have >= x) return true;
-        if (!mbar_wait(&k_full[x % kPreKStages], (x / kPreKStages) & 1, &abort_flag)) return false;
+        if (!mbar_wait_warp(&k_full[x % kPreKStages], (x / kPreKStages) & 1, &abort_flag)) return false;
         k_have = x;
         tc_fence_after();
         return true;
@@ -324,16 +326,16 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
 #pragma unroll
           for (int t = 0; t < kPreTiles; ++t)
             if (nk[t] > 0) issue_s(t, 0);
-          mma_commit(&k_empty[0]);
+          mma_commit_warp(&k_empty[0]);
           issued_any = true;
         }
       }
       for (int j = 0; ok && j < n_all; ++j) {
-        if (!mbar_wait(&v_full[j % kPreVStages], (j / kPreVStages) & 1, &abort_flag)) { ok = false; break; }
+        if (!mbar_wait_warp(&v_full[j % kPreVStages], (j / kPreVStages) & 1, &abort_flag)) { ok = false; break; }
 #pragma unroll
         for (int t = 0; t < kPreTiles; ++t) {
           if (j >= nk[t]) continue;
-          if (!mbar_wait(&p_full[t], j & 1, &abort_flag)) { ok = false; break; }
+          if (!mbar_wait_warp(&p_full[t], j & 1, &abort_flag)) { ok = false; break; }
           tc_fence_after();
           issue_pv(t, j);
           if (j + 1 < nk[t]) {
@@ -342,11 +344,11 @@ __global__ void __launch_bounds__(kPreThreads, 1) prefill_attention_kernel(Atten
           }
         }
         if (!ok) break;
-        mma_commit(&v_empty[j % kPreVStages]);  // V_j is free once these P V complete
-        if (j + 1 < n_all) mma_commit(&k_empty[(j + 1) % kPreKStages]);
+        mma_commit_warp(&v_empty[j % kPreVStages]);  // V_j is free once these P V complete
+        if (j + 1 < n_all) mma_commit_warp(&k_empty[(j + 1) % kPreKStages]);
       }
       if (issued_any) {  // nothing may still write TMEM when it is freed
-        mma_commit(&drain_bar);
+        mma_commit_warp(&drain_bar);
         mbar_drain(&drain_bar, 0);
       }
     }
