@@ -42,6 +42,8 @@ MIN_SHARED_PAGES = 4        # common leading pages from which single-token decod
 PREFIX_GROUP_MAX_ROWS = 512  # rows of one shared-prefix group (its prefix items take 2 tiles of rows each)
 PREFIX_MIN_SPLIT_KEYS = 512  # shortest split of the shared keys one prefix item covers
 PREFIX_SM_SHARE = 4          # the prefix tiles aim at 1/PREFIX_SM_SHARE of the SMs; the decode grid takes the rest
+DECODE_SPLIT_CTAS_PER_SM = 8         # decode units per SM the split size aims at (decode-only calls)
+DECODE_SPLIT_CTAS_PER_SM_MIXED = 3   # the same when prefill tiles run beside the (persistent) decode grid
 PREFILL_TILE_ROWS = 128     # query rows of one tcgen05 prefill tile (a CTA takes a pair of tiles)
 NUM_SMS_B200 = 148
 
@@ -244,9 +246,15 @@ class _Staging:
         return self.dev[:n]
 
 
-def choose_split_keys(decode_keys_x_heads: int, page_size: int, num_sms: int = NUM_SMS_B200) -> int:
-    """Keys per decode split: aim for ~8 CTAs per SM across the decode rows."""
-    target = 8 * num_sms
+def choose_split_keys(decode_keys_x_heads: int, page_size: int, num_sms: int = NUM_SMS_B200,
+                      ctas_per_sm: int = DECODE_SPLIT_CTAS_PER_SM) -> int:
+    """Keys per decode split: aim for ``ctas_per_sm`` decode units per SM across the decode rows.
+    A decode-only call runs one CTA per unit, two per SM, and gains from fine splits that even out
+    the rows' lengths (BASELINE config 2's 64 long rows: 170 us at 8 per SM, 174 at 4, 179 at 3).
+    Beside prefill tiles the decode grid is persistent on fewer SMs and every unit pays its start
+    and merge on those SMs, so fewer, longer units win there (config-3 ticks 18.15 -> 18.03 ms at
+    3 per SM; mixed config-3 attention 106.6 -> 102.3 us)."""
+    target = ctas_per_sm * num_sms
     split = math.ceil(max(1, decode_keys_x_heads) / target)
     split = max(page_size, math.ceil(split / page_size) * page_size)
     return min(split, 64 * page_size)
@@ -403,7 +411,9 @@ class PagedBatchCache:
         is_decode = cnts <= decode_max
         # The decode items read each row's own keys; the prefix items each group's shared keys,
         # once per pair of query tiles.
-        split = choose_split_keys(int((ends - shared)[is_decode].sum()) * config.n_kv_heads, page_size)
+        mixed = bool((~is_decode).any())  # prefill rows: the decode grid runs beside their tiles
+        split = choose_split_keys(int((ends - shared)[is_decode].sum()) * config.n_kv_heads, page_size,
+                                  ctas_per_sm=DECODE_SPLIT_CTAS_PER_SM_MIXED if mixed else DECODE_SPLIT_CTAS_PER_SM)
         pairs = (group_rows + pair_rows - 1) // pair_rows
         prefix_split = choose_prefix_split_keys(int(pairs[heads].sum()) * config.n_kv_heads,
                                                 int(shared[heads].max(initial=0)), page_size)

@@ -20,6 +20,8 @@ from helios_b200.paged_cache import (
     PagedKVCache,
     choose_prefix_split_keys,
     choose_split_keys,
+    DECODE_SPLIT_CTAS_PER_SM,
+    DECODE_SPLIT_CTAS_PER_SM_MIXED,
 )
 
 CPU = torch.device("cpu")
@@ -220,6 +222,27 @@ def test_prefix_groups_take_pairs_of_query_tiles():
     # Few rows: more splits of the shared keys; never below PREFIX_MIN_SPLIT_KEYS.
     assert choose_prefix_split_keys(8, 4096, 256) == 1024
     assert choose_prefix_split_keys(1, 1024, 256) == 512
+
+
+def test_decode_splits_are_longer_beside_prefill():
+    """A tick with prefill rows runs its decode grid beside the prefill tiles (persistent, on fewer
+    SMs): its split aims at DECODE_SPLIT_CTAS_PER_SM_MIXED units per SM instead of
+    DECODE_SPLIT_CTAS_PER_SM, so the same decode rows get splits at least as long."""
+    cfg = tiny(n_heads=32, n_kv_heads=8)
+    pool = KVPagePool(cfg, 512, device=CPU)
+    caches = []
+    for length in [1024 + 90 * i for i in range(32)] + [0]:
+        c = PagedKVCache(pool, 4096)
+        c.pages.extend(pool.acquire(math.ceil(length / 256)))
+        c.length = length
+        caches.append(c)
+    keys_x_heads = sum(c.length + 1 for c in caches[:32]) * 8
+    mixed = PackedBatchCache(caches)._host_descriptor([1] * 32 + [2048], [1] * 33)
+    alone = PackedBatchCache(caches[:32])._host_descriptor([1] * 32, [1] * 32)
+    assert mixed["split_keys"] == choose_split_keys(keys_x_heads, 256, ctas_per_sm=DECODE_SPLIT_CTAS_PER_SM_MIXED)
+    assert alone["split_keys"] == choose_split_keys(keys_x_heads, 256, ctas_per_sm=DECODE_SPLIT_CTAS_PER_SM)
+    assert mixed["split_keys"] > alone["split_keys"]
+    assert mixed["num_decode_items"] < alone["num_decode_items"]
 
 
 def test_split_policy():
