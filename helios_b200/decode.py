@@ -226,19 +226,31 @@ class Decoder:
         if tuple(logits.shape) != expected:
             raise RuntimeError(f"Decoder logits must have shape {expected}; received {tuple(logits.shape)}.")
 
-    def decode_caches(self, caches: list[PagedKVCache], token_ids: list[int]) -> torch.Tensor:
-        """Logits ``[B, V]`` of one decode step of every cache (decode.py:220-258)."""
+    def decode_caches(self, caches: list[PagedKVCache], token_ids: list[int] | torch.Tensor) -> torch.Tensor:
+        """Logits ``[B, V]`` of one decode step of every cache (decode.py:220-258).
+
+        ``token_ids`` may also be a 1-D integer tensor on the pool's device (for instance the
+        previous step's sampled ids): it is copied on the device, so a caller can queue the next
+        step before it reads the previous step's ids back (the host half of a tick then overlaps
+        the device half of the one before)."""
         return self._decode(caches, token_ids, greedy=False)
 
-    def decode_caches_greedy(self, caches: list[PagedKVCache], token_ids: list[int]) -> torch.Tensor:
+    def decode_caches_greedy(self, caches: list[PagedKVCache], token_ids: list[int] | torch.Tensor) -> torch.Tensor:
         """The temperature-0 next token of every cache (int64 ``[B]``): ``decode_caches`` followed
         by the argmax the reference samples greedy rows with (decode.py:458-460), with the argmax
         in the lm_head GEMM's epilogue so the logits are never written."""
         return self._decode(caches, token_ids, greedy=True)
 
-    def _decode(self, caches: list[PagedKVCache], token_ids: list[int], *, greedy: bool) -> torch.Tensor:
+    def _decode(self, caches: list[PagedKVCache], token_ids: list[int] | torch.Tensor, *,
+                greedy: bool) -> torch.Tensor:
         if not caches or len(caches) != len(token_ids):
             raise ValueError("Every request cache needs exactly one pending token.")
+        on_device = isinstance(token_ids, torch.Tensor)
+        pool_device = caches[0].pool.device
+        if on_device and (token_ids.dim() != 1 or token_ids.device.type != pool_device.type
+                          or (pool_device.index is not None and token_ids.device.index != pool_device.index)
+                          or token_ids.dtype not in (torch.int32, torch.int64)):
+            raise ValueError("Device token ids must be a 1-D integer tensor on the pool's device.")
         if any(not isinstance(cache, PagedKVCache) or cache.pool is not caches[0].pool for cache in caches):
             raise ValueError("Paged decode caches must share one pool.")
         if len({id(cache) for cache in caches}) != len(caches):
@@ -252,7 +264,10 @@ class Decoder:
             batch.caches = tuple(caches)
             batch.batch_size = len(caches)
             try:
-                tokens = batch.metadata("token_ids", list(token_ids), torch.long).unsqueeze(1)
+                if on_device:
+                    tokens = token_ids.to(torch.long).unsqueeze(1)
+                else:
+                    tokens = batch.metadata("token_ids", list(token_ids), torch.long).unsqueeze(1)
                 batch.prepare(1)
                 slots = tuple(range(len(caches)))
                 if greedy:

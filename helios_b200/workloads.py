@@ -1,7 +1,7 @@
 """Model-level workloads beyond the bench's mixed tick.
 
-    python -m helios_b200.workloads config4 [--steps N] [--no-share]
-    python -m helios_b200.workloads config4-decode [--ticks N] [--no-share]
+    python -m helios_b200.workloads config4 [--steps N] [--no-share] [--sync]
+    python -m helios_b200.workloads config4-decode [--ticks N] [--no-share] [--sync]
 
 ``config4``: BASELINE config 4 end to end on the Qwen3-4B architecture (random init, bf16,
 seed 3). One request prefills the common 4096-token prefix through packed ticks and its 16
@@ -12,7 +12,8 @@ blocks and ``restore_blocks`` aliases their pages (no K/V bytes move). The tails
 prefilled through packed ticks of at most 2048 tokens (chunked, as the reference engine's
 budget does), and every request then decodes ``steps`` (128) tokens with temperature 0.2
 and top-p 0.95, one decode tick per step (CUDA-graph replay) sampled by kernel d, each
-step's ids read back to the host. Reports the restore cost (lookup + aliasing, and the
+step's ids read back to the host (pipelined: while the GPU runs the next step, which takes
+the ids on the device; ``--sync`` reads them before queueing it). Reports the restore cost (lookup + aliasing, and the
 bytes it uploads), the tail prefill time and the decode tokens/s, each timed with CUDA
 events.
 
@@ -76,8 +77,41 @@ def _cuda_timer(device):
     return start, end
 
 
+def decode_steps(tick, ids, steps: int, pipelined: bool = True) -> list[list[int]]:
+    """Runs ``steps`` decode ticks from ``ids`` (a host list or a device tensor) through
+    ``tick`` (token ids -> sampled ids on the device) and returns every step's sampled ids as
+    read back to the host.
+
+    Synchronous: each tick's ids come back (``.tolist``) before the next tick is queued, as the
+    reference engine's loop does (src/helios/runtime/engine.py:406-530). Pipelined: the next tick
+    takes the sampled ids on the device and is queued first; each step's ids are copied to pinned
+    memory and read while the GPU runs the step after it, so the host half of a tick (page
+    bookkeeping, the descriptor, tick packing) overlaps the device half of the one before. Both
+    sample the same ids."""
+    out: list[list[int]] = []
+    if not pipelined:
+        for _ in range(steps):
+            ids = tick(ids).tolist()
+            out.append(ids)
+        return out
+    host, done = None, [torch.cuda.Event(), torch.cuda.Event()]
+    for step in range(steps):
+        ids = tick(ids)
+        if host is None:
+            host = [torch.empty(ids.numel(), dtype=ids.dtype, pin_memory=True) for _ in range(2)]
+        host[step & 1].copy_(ids, non_blocking=True)
+        done[step & 1].record()
+        if step:
+            done[(step - 1) & 1].synchronize()
+            out.append(host[(step - 1) & 1].tolist())
+    if steps:
+        done[(steps - 1) & 1].synchronize()
+        out.append(host[(steps - 1) & 1].tolist())
+    return out
+
+
 def config4(steps: int = 128, share: bool = True, device: torch.device | None = None, seed: int = 3,
-            warmup: int = 3) -> dict:
+            warmup: int = 3, pipelined: bool = True) -> dict:
     """BASELINE config 4 as specified (see the module docstring); returns its measurements."""
     from helios_b200.prefix_index import DevicePrefixIndex
 
@@ -175,15 +209,14 @@ def config4(steps: int = 128, share: bool = True, device: torch.device | None = 
 
             def tick(token_ids):
                 out = decoder.decode_caches(caches, token_ids)
-                return sample_rows(out, samplings, generator=sample_gen).tolist()
+                return sample_rows(out, samplings, generator=sample_gen)
 
             for _ in range(warmup):  # eager tick, graph capture, first replay
-                ids = tick(ids)
+                ids = tick(ids).tolist()
             torch.cuda.synchronize(device)
             start, end = _cuda_timer(device)
             start.record()
-            for _ in range(steps):
-                ids = tick(ids)
+            decode_steps(tick, ids, steps, pipelined)
             end.record()
             torch.cuda.synchronize(device)
             decode_seconds = start.elapsed_time(end) / 1e3
@@ -204,12 +237,14 @@ def config4(steps: int = 128, share: bool = True, device: torch.device | None = 
                          "tokens_per_s": round(tail_tokens / prefill_seconds, 1)},
         "decode": {"steps": steps, "ms_per_step": round(1e3 * decode_seconds / steps, 3),
                    "tokens_per_s": round(REQUESTS * steps / decode_seconds, 1),
-                   "timing": "CUDA events around the decode steps; each step's sampled ids read back to the host"},
+                   "timing": "CUDA events around the decode steps; each step's sampled ids read back to the host "
+                             + ("while the GPU runs the next step (the next tick takes the ids on the device)"
+                                if pipelined else "before the next step is queued")},
         "shared_prefix_grouping": share,
     }
 
 
-def config4_decode(ticks: int, share: bool, warmup: int = 3) -> dict:
+def config4_decode(ticks: int, share: bool, warmup: int = 3, pipelined: bool = True) -> dict:
     device = torch.device("cuda", 0)
     cfg = qwen3_4b_config()
     torch.manual_seed(3)
@@ -254,11 +289,15 @@ def config4_decode(ticks: int, share: bool, warmup: int = 3) -> dict:
         torch.cuda.synchronize()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
-        out = None
-        for _ in range(ticks):
+
+        def marked(token_ids):
             torch.cuda.nvtx.range_push("tick")  # lets a profiler select exactly the timed ticks
-            out = tick(ids if out is None else out.tolist())
-            torch.cuda.nvtx.range_pop()
+            try:
+                return tick(token_ids)
+            finally:
+                torch.cuda.nvtx.range_pop()
+
+        decode_steps(marked, ids, ticks, pipelined)
         end.record()
         torch.cuda.synchronize()
     finally:
@@ -268,7 +307,8 @@ def config4_decode(ticks: int, share: bool, warmup: int = 3) -> dict:
                         "T=0.2 top-p 0.95", "model": "Qwen3-4B architecture, random init", "dtype": "bf16",
             "shared_prefix_grouping": share, "ticks": ticks, "ms_per_tick": round(ms, 3),
             "tokens_per_s": round(REQUESTS / (ms / 1e3), 1),
-            "timing": "CUDA events around the ticks, each tick's ids read back to the host (.tolist)"}
+            "timing": "CUDA events around the ticks, each tick's ids read back to the host "
+                      + ("while the GPU runs the next tick" if pipelined else "before the next tick is queued")}
 
 
 def main(argv: list[str]) -> None:
@@ -277,13 +317,15 @@ def main(argv: list[str]) -> None:
     parser.add_argument("--ticks", type=int, default=16)
     parser.add_argument("--steps", type=int, default=128)
     parser.add_argument("--no-share", action="store_true")
+    parser.add_argument("--sync", action="store_true",
+                        help="read each step's ids back before queueing the next step (no pipelining)")
     args = parser.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("the workloads need a CUDA device")
     if args.workload == "config4":
-        print(json.dumps(config4(args.steps, not args.no_share)), flush=True)
+        print(json.dumps(config4(args.steps, not args.no_share, pipelined=not args.sync)), flush=True)
     else:
-        print(json.dumps(config4_decode(args.ticks, not args.no_share)), flush=True)
+        print(json.dumps(config4_decode(args.ticks, not args.no_share, pipelined=not args.sync)), flush=True)
 
 
 if __name__ == "__main__":

@@ -117,3 +117,35 @@ def test_graph_ticks_with_a_shared_prefix_match_eager_ticks():
         last = a.argmax(-1).tolist()
     assert runner.replays >= 10
     assert _native.device_status() == 0
+
+
+def test_pipelined_decode_steps_match_synchronous_steps():
+    """``workloads.decode_steps`` pipelined (the next tick takes the sampled ids on the device and
+    is queued before the host reads them back) samples the same ids as the synchronous loop that
+    reads every step's ids before queueing the next, over graph-replayed sampled decode ticks."""
+    from helios_b200.config import Sampling
+    from helios_b200.decode import sample_rows
+    from helios_b200.workloads import decode_steps
+
+    torch.manual_seed(0)
+    model = Qwen3Model(Qwen3Config(**SHAPE)).to(DEV).eval()
+    model.enable_cuda_graphs()
+    g = torch.Generator().manual_seed(4)
+    prompts = [torch.randint(0, 4096, (n,), generator=g).tolist() for n in (120, 300, 45, 260)]
+    samplings = [Sampling(temperature=0.7, top_p=0.9, max_new_tokens=64)] * len(prompts)
+    results = []
+    for pipelined in (False, True):
+        decoder = Decoder(model)
+        decoder.page_pool = KVPagePool(model.config, 48, device=DEV)
+        caches = [PagedKVCache(decoder.page_pool, len(p) + 40) for p in prompts]
+        heads = decoder.packed_caches(caches, prompts).clone()
+        gen = torch.Generator(device=DEV).manual_seed(5)
+        first = sample_rows(heads, samplings, generator=gen).tolist()
+
+        def tick(ids, caches=caches, gen=gen, decoder=decoder):
+            return sample_rows(decoder.decode_caches(caches, ids), samplings, generator=gen)
+
+        results.append([first] + decode_steps(tick, first, 24, pipelined))
+        assert [c.length for c in caches] == [len(p) + 24 for p in prompts]
+    assert results[0] == results[1]
+    assert _native.device_status() == 0
