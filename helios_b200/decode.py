@@ -245,6 +245,8 @@ class Decoder:
                 greedy: bool) -> torch.Tensor:
         if not caches or len(caches) != len(token_ids):
             raise ValueError("Every request cache needs exactly one pending token.")
+        if isinstance(token_ids, torch.Tensor) and token_ids.device.type == "cpu":
+            token_ids = token_ids.tolist()  # host ids take the list path
         on_device = isinstance(token_ids, torch.Tensor)
         pool_device = caches[0].pool.device
         if on_device and (token_ids.dim() != 1 or token_ids.device.type != pool_device.type
