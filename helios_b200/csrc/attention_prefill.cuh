@@ -15,8 +15,9 @@
 //              128B-swizzled [64 keys][64 d] boxes each, each 64-key half from the
 //              page the block table names) into 2-stage K and V rings;
 //   warp 1     owns the TMEM allocation (512 columns: the S/P buffer of tile t at
-//              128 t, its O accumulator at 256 + 128 t); lane 0 issues
-//              S_t = Q_t K^T (both operands in shared memory) and O_t += P_t V (P
+//              128 t, its O accumulator at 256 + 128 t) and runs the issue loop as a
+//              converged warp, one elected lane issuing S_t = Q_t K^T (both
+//              operands in shared memory) and O_t += P_t V (P
 //              read from TMEM, where the softmax wrote it over S_t), in a fixed
 //              order with blocking waits: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1). So
 //              the tensor core computes one tile's P V and next S while the
@@ -26,7 +27,8 @@
 //              row (thread = row, so no shuffles); they swap their half-row maxima
 //              through shared memory (an mbarrier per row pair, so the wait is
 //              bounded) and their row sums once at the end; each warp rescales and
-//              writes its 64 of the 128 output columns.
+//              writes its 64 of the 128 output columns. A quarter of the exponentials
+//              run on the FMA pipe (exp2_fma2) beside the ex2 unit.
 // O is rescaled (in TMEM) only when a row's running max grows by more than 2^8;
 // exponents stay relative to the max in use, so P <= 2^8 and the final O / l is
 // unchanged. Keys at or beyond seqused_k get their V rows zeroed so stale pool
