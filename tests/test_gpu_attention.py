@@ -88,6 +88,8 @@ def _run(lengths, counts, heads=32, kv_heads=8, seed=0, nan_fill=False):
                                batch.cu_seq_q.cpu().tolist(), batch.seqused_k.cpu().tolist())
     assert torch.isfinite(out.float()).all()
     torch.testing.assert_close(out.float(), expected.float(), rtol=2e-2, atol=2e-2)
+    batch.max_abs_err = (out.float() - expected.float()).abs().max().item()
+    batch.mean_abs_err = (out.float() - expected.float()).abs().mean().item()
     return batch
 
 
@@ -109,6 +111,11 @@ def test_drafted_rows():
 def test_prefill_single_row_2048():
     batch = _run([0], [2048])
     assert batch.num_prefill_items == 2048 // 32 // 2  # 64 tiles of 32 tokens, paired
+    print(f"prefill 2048 vs fp32 oracle: max abs {batch.max_abs_err:.3e}, mean abs {batch.mean_abs_err:.3e}")
+    # Tighter than the reference's bound: one bf16 ulp of the output at most (7.8e-3 measured)
+    # and a mean error near bf16 rounding (5.8e-5 measured), so a worse exponential or a dropped
+    # key shows up here before it reaches the 2e-2 parity bound.
+    assert batch.max_abs_err <= 1.6e-2 and batch.mean_abs_err <= 2e-4
 
 
 def test_prefill_partial_tiles_and_continuation():
