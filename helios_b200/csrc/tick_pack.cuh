@@ -70,6 +70,17 @@ constexpr int kTickThreads = 1024;
 
 __device__ __forceinline__ int row_splits(int end, int split_keys) { return (end + split_keys - 1) / split_keys; }
 
+// A decode row's own keys: the nearest whole number of split_keys (at least one), cut into
+// near-equal parts on 64-key boundaries, so no row ends in a sliver of a split (a unit of a
+// few keys costs a whole CTA's start and merge). split_keys >= 256, so every part holds at
+// least 170 keys.
+__device__ __forceinline__ int tail_split_count(int keys, int split_keys) {
+  return max(1, (keys + split_keys / 2) / split_keys);
+}
+__device__ __forceinline__ int tail_split_start(int keys, int n, int k) {
+  return k >= n ? keys : static_cast<int>((static_cast<int64_t>(keys) * k / n) & ~int64_t(63));
+}
+
 // Decode items, prefix items and partial records of row r (see the header).
 struct RowWork {
   int items, records, prefix_splits, tail_splits, prefix_items;
@@ -82,12 +93,12 @@ __device__ __forceinline__ RowWork row_work(const TickPackParams& p, int r) {
   if (shared > 0) {
     const int pair_rows = 2 * p.prefill_tile_tokens;
     w.prefix_splits = row_splits(shared, p.prefix_split_keys);
-    w.tail_splits = row_splits(end - shared, p.split_keys);
+    w.tail_splits = tail_split_count(end - shared, p.split_keys);
     w.items = w.tail_splits;
     w.records = (w.prefix_splits + w.tail_splits) * cnt;
     w.prefix_items = group > 0 ? ((group + pair_rows - 1) / pair_rows) * w.prefix_splits : 0;
   } else {
-    w.tail_splits = row_splits(end, p.split_keys);
+    w.tail_splits = tail_split_count(end, p.split_keys);
     w.items = w.tail_splits;
     w.records = w.tail_splits * cnt;
   }
@@ -233,10 +244,10 @@ __global__ void __launch_bounds__(kTickThreads) tick_pack_kernel(TickPackParams 
       for (int k = 0; k < w.tail_splits; ++k, ++at) {  // this row's own keys [shared, end)
         if (at >= p.decode_capacity) { raise_status(kStatusBadRow); break; }
         int32_t* it = p.decode_items + kDecodeItemInts * at;
-        const int kb = shared + k * p.split_keys;
+        const int own = end - shared;
         it[0] = r;
-        it[1] = kb;
-        it[2] = min(end, kb + p.split_keys);
+        it[1] = shared + tail_split_start(own, w.tail_splits, k);
+        it[2] = shared + tail_split_start(own, w.tail_splits, k + 1);
         it[3] = r_off[r] + (w.prefix_splits + k) * cnt;
         it[4] = nsplit;
         it[5] = 0;

@@ -418,7 +418,9 @@ class PagedBatchCache:
         prefix_split = choose_prefix_split_keys(int(pairs[heads].sum()) * config.n_kv_heads,
                                                 int(shared[heads].max(initial=0)), page_size)
         prefix_splits = (shared + prefix_split - 1) // prefix_split
-        tail_splits = (ends - shared + split - 1) // split
+        # Each row's own keys in the nearest whole number of splits, at least one (tick_pack.cuh,
+        # tail_split_count): no row ends in a sliver of a split.
+        tail_splits = np.maximum(1, (ends - shared + split // 2) // split)
         records = (prefix_splits + tail_splits) * cnts
         return {
             "rows": rows, "updates": np.asarray(updates, dtype=np.int32), "decode_max": decode_max,

@@ -31,3 +31,11 @@ def queue_pages(pool: KVPagePool, pages: Sequence[int]) -> None:
     for index in pages:
         pool._free.remove(index)
     pool._free.extend(reversed(list(pages)))
+
+
+def decode_units(keys: int, split: int) -> list[tuple[int, int]]:
+    """A decode row's own keys [0, keys) as tick packing cuts them: the nearest whole number of
+    ``split`` (at least one) near-equal parts on 64-key boundaries."""
+    n = max(1, (keys + split // 2) // split)
+    starts = [(keys * k // n) & ~63 for k in range(n)] + [keys]
+    return [(starts[k], starts[k + 1]) for k in range(n)]

@@ -15,7 +15,7 @@ import torch
 from helios_b200 import _native
 from helios_b200.paged_cache import KVPagePool, PackedBatchCache, PagedBatchCache, PagedKVCache
 from oracle.metadata import pack_tick
-from tests.helpers import attn_config, cache_with_pages, queue_pages
+from tests.helpers import attn_config, cache_with_pages, decode_units, queue_pages
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda")
@@ -83,9 +83,9 @@ def test_work_items_cover_every_row_once():
         assert rec[row] == record
         if count <= 64 // group:
             items = seen[row]
-            n = math.ceil(end / batch.split_keys)
-            sk = batch.split_keys
-            assert [(kb, ke) for kb, ke, _, _ in items] == [(s * sk, min(end, (s + 1) * sk)) for s in range(n)]
+            units = decode_units(end, batch.split_keys)
+            n = len(units)
+            assert [(kb, ke) for kb, ke, _, _ in items] == units
             assert all(k == n for _, _, _, k in items)
             assert [b for _, _, b, _ in items] == [record + s * count for s in range(n)]
             record += n * count
@@ -155,13 +155,13 @@ def test_rows_sharing_restored_pages_form_one_prefix_pass():
     for row, tail in enumerate(tails):
         end = shared + tail + 1
         own = [it for it in dec if it[0] == row]
-        n_own = math.ceil((end - shared) / sk)
-        assert [(kb, ke) for _, kb, ke, _, _, _ in own] == [(shared + k * sk, min(end, shared + (k + 1) * sk))
-                                                           for k in range(n_own)]
+        units = decode_units(end - shared, sk)
+        n_own = len(units)
+        assert [(kb, ke) for _, kb, ke, _, _, _ in own] == [(shared + a, shared + b) for a, b in units]
         assert [b for _, _, _, b, _, _ in own] == [rec[row] + n_prefix + k for k in range(n_own)]
         assert all(n == n_prefix + n_own for _, _, _, _, n, _ in own)
         assert rec[row + 1] - rec[row] == n_prefix + n_own
     own = [it for it in dec if it[0] == 5]
-    assert all(it[1] % sk == 0 for it in own)  # the unshared row: plain splits from key 0
+    assert [(it[1], it[2]) for it in own] == decode_units(2001, sk)  # the unshared row: from key 0
     assert rec[6] == batch.partial_records
     assert _native.device_status() == 0

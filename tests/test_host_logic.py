@@ -24,6 +24,8 @@ from helios_b200.paged_cache import (
     DECODE_SPLIT_CTAS_PER_SM_MIXED,
 )
 
+from tests.helpers import decode_units
+
 CPU = torch.device("cpu")
 
 
@@ -147,8 +149,9 @@ def test_descriptor_partitions_attention_work():
     assert d["decode_max"] == 16 and d["tile_tokens"] == 32
     split = d["split_keys"]
     assert split % 256 == 0 and split >= 256
-    assert d["num_decode_items"] == math.ceil(1001 / split) + math.ceil(3016 / split)
-    assert d["partial_records"] == math.ceil(1001 / split) * 1 + math.ceil(3016 / split) * 16
+    n1, n2 = len(decode_units(1001, split)), len(decode_units(3016, split))
+    assert d["num_decode_items"] == n1 + n2
+    assert d["partial_records"] == n1 * 1 + n2 * 16
     assert d["num_prefill_items"] == 2048 // 32 // 2  # tiles of 32 tokens, paired
     assert d["total_tokens"] == 2065 and d["num_logits"] == 3 and d["width"] == 16
 
@@ -188,7 +191,7 @@ def test_rows_restoring_one_prefix_are_grouped():
     # tiles); each row's own keys: decode items.
     prefix_splits = math.ceil(shared / prefix_split)
     assert prefix_split % 256 == 0 and prefix_split >= 512
-    own = [math.ceil((e - shared) / split) for e in ends[:3]] + [math.ceil(e / split) for e in ends[3:]]
+    own = [len(decode_units(e - shared, split)) for e in ends[:3]] + [len(decode_units(e, split)) for e in ends[3:]]
     assert d["num_decode_items"] == sum(own)
     assert d["num_prefix_items"] == prefix_splits
     assert d["partial_records"] == 3 * prefix_splits + sum(o * n for o, n in zip(own, counts))
