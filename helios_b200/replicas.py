@@ -28,8 +28,11 @@ def init(backend: str, timeout_s: float = 120.0) -> bool:
         return False
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     if backend == "nccl":
-        # NCCL's own log (its version banner at the VERSION and WARN levels) goes to stderr, so
-        # rank 0's stdout carries only what the caller prints.
+        # NCCL's own log goes to stderr, so rank 0's stdout carries only what the caller prints.
+        # At NCCL_DEBUG=VERSION (this image's default) NCCL prints its version banner to stdout
+        # whatever NCCL_DEBUG_FILE says; from WARN up the banner and warnings go to that file.
+        if os.environ.get("NCCL_DEBUG", "").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     dist.init_process_group(backend=backend, rank=rank, world_size=size, timeout=timedelta(seconds=timeout_s))
     return True
